@@ -1,0 +1,180 @@
+/*
+ * optiz_qwen_b200 -- C ABI of the B200 decode hot path for the Qwen3.5 hybrid LM.
+ *
+ * Every entry point takes plain device pointers, sizes, element strides and a
+ * cudaStream_t (passed as void*), enqueues its kernels on that stream and
+ * returns an oq_status code.  Nothing here allocates device memory, frees it or
+ * synchronises the stream; scratch comes from caller-provided workspaces.  No
+ * entry point aborts the process.  All pointers are device pointers unless a
+ * comment says otherwise.
+ *
+ * Storage of the paged INT4 KV cache (one pool per attention layer):
+ *   kv_codes  uint8   [num_pages, num_kv_heads, 2, page_size, head_dim/2]
+ *             index 2: 0 = keys, 1 = values; byte j of a token row holds
+ *             dimension 2j in its low nibble and 2j+1 in its high nibble.
+ *   kv_meta   fp16    [num_pages, num_kv_heads, 4, page_size]
+ *             index 4: 0 = key scale, 1 = key min, 2 = value scale, 3 = value min.
+ *   block_table int32 [batch, block_table_stride]  physical page of each logical page.
+ *   seq_lens  int32   [batch]  tokens held by each sequence.
+ * Dequantised value = min + code * scale (the reference's asymmetric "zero" is
+ * an additive minimum).
+ */
+#ifndef OPTIZ_QWEN_B200_H
+#define OPTIZ_QWEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum oq_status {
+  OQ_OK = 0,
+  OQ_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, bad stride */
+  OQ_ERR_UNSUPPORTED = 2,       /* shape / dtype / bit width this build does not implement */
+  OQ_ERR_MISALIGNED = 3,        /* pointer or stride breaks a 16-byte vector / TMA rule */
+  OQ_ERR_WORKSPACE = 4,         /* workspace missing or too small */
+  OQ_ERR_CUDA = 5               /* a CUDA runtime / driver call failed (see oq_last_error) */
+};
+
+/* Element types for the dtype arguments. */
+enum oq_dtype { OQ_F32 = 0, OQ_F16 = 1, OQ_BF16 = 2 };
+
+/* Bits a kernel ORs into the optional device status word when it meets bad data. */
+enum oq_device_status {
+  OQ_DEV_BAD_PAGE = 1,     /* block_table entry outside [0, num_pages): page skipped */
+  OQ_DEV_OVERFLOW = 2,     /* position beyond max_pages_per_seq * page_size: token skipped */
+  OQ_DEV_TIMEOUT = 4       /* a bounded wait on a copy ran out: the CTA gave up */
+};
+
+/* Static description of an oq_status value. */
+const char* oq_status_string(int status);
+/* Detail of the last failing call on this host thread ("" when none). */
+const char* oq_last_error(void);
+/* ABI version: bumped when a signature changes. */
+int oq_abi_version(void);
+
+/* ------------------------------------------------------------------ append-quantize
+ * Replaces QServeAttentionLayer._append_keys/_append_values/_quantize_and_append_*
+ * + _quantize_groupwise + _pack_uint4
+ * (optiz_qwen/compression/qserve_kv_cache.py:210-232, 278-292, 313-335, 356-362)
+ * with group_size = head_dim, fp16 scale/min, paged storage and no dense window.
+ *
+ * key/value: [batch, num_kv_heads, num_new, head_dim] in `dtype` (F32/F16/BF16),
+ * last dimension contiguous, other strides in elements.  Token t of sequence b
+ * is written at position seq_lens[b] + t.  Codes use the fp32 scale/min
+ * (round-half-even of (x - min) / scale, clamped to [0, 15]); the stored
+ * scale/min are the fp32 values rounded to fp16.  When advance_seq_lens != 0
+ * seq_lens[b] += num_new on exit (stream-ordered).  device_status may be NULL.
+ */
+int oq_append_quant_int4(
+    const void* key, const void* value, int dtype,
+    int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
+    int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
+    int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    int32_t* seq_lens, int advance_seq_lens,
+    int32_t* device_status, void* stream);
+
+/* seq_lens[b] += delta for b < batch (cache bookkeeping between steps). */
+int oq_advance_seq_lens(int32_t* seq_lens, int64_t batch, int32_t delta, void* stream);
+
+/* ------------------------------------------------------------------ decode attention
+ * Replaces qserve_int4_decode_attention / qserve_int4_split_decode_attention
+ * (optiz_qwen/kernels/qserve_int4_attention.py:520-545, 576-620) and their
+ * Triton kernels (:112-205, :209-261, :328-395).
+ *
+ * One query token per sequence: query [batch, num_heads, head_dim] (BF16 or
+ * F16, element strides for batch and head, last dim contiguous) attends over
+ * seq_lens[b] cached tokens of KV head h / (num_heads / num_kv_heads); scores
+ * are scaling * q.k.  head_dim must be 256 and num_heads / num_kv_heads <= 8
+ * in this build.  The KV range of each (sequence, KV head) is cut into
+ * num_splits page ranges (num_splits <= 0: chosen from the grid size); the
+ * partial (max, sum, acc) of each range are merged by log-sum-exp inside the
+ * same launch.
+ *
+ * Outputs (each may be NULL, at least one must be given):
+ *   out      [batch, num_heads, head_dim] in the query dtype, strides in elements;
+ *   out_f32  [batch, num_heads, head_dim] fp32, contiguous;
+ *   out_lse  [batch, num_heads] fp32 natural-log log-sum-exp of the scores
+ *            (-inf for an empty sequence, whose output row is 0).
+ * workspace: oq_decode_attn_workspace_bytes(...) bytes, zero-filled once before
+ * its first use; every launch leaves its counters at zero again.  Launches that
+ * share a workspace must be ordered on one stream.
+ */
+size_t oq_decode_attn_workspace_bytes(int64_t batch, int64_t num_heads, int64_t num_kv_heads,
+                                      int64_t head_dim, int64_t max_splits);
+
+int oq_decode_attn_int4_paged(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream);
+
+/* ------------------------------------------------------------------ log-sum-exp merge
+ * Combines attention partials computed over disjoint KV ranges (another GPU's
+ * slice of a long context, gathered over NVLink):
+ *   out = sum_i exp(lse_i - L) * part_out_i,  L = log sum_i exp(lse_i).
+ * part_out [num_parts, rows, head_dim] fp32, part_lse [num_parts, rows] fp32;
+ * out [rows, head_dim] in `dtype`; out_lse [rows] fp32 or NULL.
+ * No reference counterpart (the reference runs on one GPU).
+ */
+int oq_lse_merge(const float* part_out, const float* part_lse,
+                 int64_t num_parts, int64_t rows, int64_t head_dim,
+                 void* out, int dtype, float* out_lse, void* stream);
+
+/* ------------------------------------------------------------------ paged gather
+ * Replaces QServeAttentionLayer.materialize / _dequantize_groupwise / _unpack_uint4
+ * (qserve_kv_cache.py:126-135, 294-353, 365-372): writes the dequantised cache
+ * of every sequence, positions [0, length) with length = min(seq_lens[b], max_len),
+ * into keys/values [batch, num_kv_heads, max_len, head_dim] (`dtype`, contiguous).
+ * Rows at or beyond a sequence's length are left untouched.
+ */
+int oq_gather_dequant_int4(
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,
+    int64_t max_len, void* keys, void* values, int dtype,
+    int32_t* device_status, void* stream);
+
+/* ------------------------------------------------------------------ gated delta rule: recurrent
+ * Replaces the GDN hook `recurrent_gated_delta_rule` = fla 0.5.1
+ * fused_recurrent_gated_delta_rule (fla/ops/gated_delta_rule/fused_recurrent.py:291)
+ * or transformers torch_recurrent_gated_delta_rule
+ * (models/qwen3_5/modeling_qwen3_5.py:314-353), called from the decode branch
+ * of Qwen3_5GatedDeltaNet.forward (:511-520).
+ *
+ * q, k [batch, seq_len, num_heads, k_dim]; v [batch, seq_len, num_heads, v_dim]
+ * in qkv_dtype, element strides (b, t, h), last dim contiguous.
+ * g, beta [batch, seq_len, num_heads] contiguous, in g_dtype / beta_dtype.
+ * initial_state [batch, num_heads, k_dim, v_dim] fp32 or NULL (zeros);
+ * final_state same shape or NULL; it may alias initial_state (in place).
+ * out [batch, seq_len, num_heads, v_dim] contiguous in qkv_dtype.
+ * Per token: S *= exp(g); kv = S^T k; delta = beta (v - kv); S += k delta^T;
+ * o = S^T (scale q).  With use_qk_l2norm, q and k are first scaled by
+ * 1/sqrt(sum(x^2) + 1e-6).  k_dim = v_dim = 128 in this build.
+ */
+int oq_gdn_recurrent(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* OPTIZ_QWEN_B200_H */

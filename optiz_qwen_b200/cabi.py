@@ -1,0 +1,222 @@
+"""Tensor-level wrappers over the C ABI.
+
+Each function validates shapes/dtypes on the host, takes raw pointers from
+torch tensors and enqueues the kernel on the current CUDA stream of the
+tensors' device.  No function here synchronises or allocates except where it
+creates the output tensor the caller asked for (through torch's caching
+allocator, so calls are CUDA-graph capturable).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import call, dtype_code, ptr, require_cuda, stream_ptr
+
+HEAD_DIM_ATTN = 256
+PAGE_SIZE = 64
+
+
+class PagedKvPool:
+    """Device storage of one layer's paged INT4 KV cache.
+
+    ``kv_codes`` uint8 ``[num_pages, Hkv, 2, page_size, D/2]`` (0 = K, 1 = V) and
+    ``kv_meta`` fp16 ``[num_pages, Hkv, 4, page_size]`` (k_scale, k_min, v_scale, v_min).
+    Pages are zero-filled on creation.
+    """
+
+    def __init__(self, num_pages: int, num_kv_heads: int, head_dim: int, page_size: int = PAGE_SIZE,
+                 device: torch.device | str = "cuda"):
+        if head_dim % 2:
+            raise ValueError("head_dim must be even")
+        self.num_pages = int(num_pages)
+        self.num_kv_heads = int(num_kv_heads)
+        self.head_dim = int(head_dim)
+        self.page_size = int(page_size)
+        self.device = torch.device(device)
+        self.kv_codes = torch.zeros((num_pages, num_kv_heads, 2, page_size, head_dim // 2), dtype=torch.uint8,
+                                    device=self.device)
+        self.kv_meta = torch.zeros((num_pages, num_kv_heads, 4, page_size), dtype=torch.float16, device=self.device)
+
+    @property
+    def nbytes(self) -> int:
+        return self.kv_codes.numel() + 2 * self.kv_meta.numel()
+
+    def grow(self, num_pages: int) -> None:
+        """Enlarge the pool to ``num_pages`` pages, keeping page contents and ids."""
+        if num_pages <= self.num_pages:
+            return
+        codes = torch.zeros((num_pages, *self.kv_codes.shape[1:]), dtype=torch.uint8, device=self.device)
+        meta = torch.zeros((num_pages, *self.kv_meta.shape[1:]), dtype=torch.float16, device=self.device)
+        codes[: self.num_pages].copy_(self.kv_codes)
+        meta[: self.num_pages].copy_(self.kv_meta)
+        self.kv_codes, self.kv_meta, self.num_pages = codes, meta, int(num_pages)
+
+
+def _check_table(block_table: torch.Tensor, seq_lens: torch.Tensor, batch: int) -> None:
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise ValueError("block_table must be an int32 [batch, max_pages] tensor with contiguous rows")
+    if seq_lens.dtype != torch.int32 or seq_lens.dim() != 1 or not seq_lens.is_contiguous():
+        raise ValueError("seq_lens must be a contiguous int32 [batch] tensor")
+    if block_table.shape[0] < batch or seq_lens.shape[0] < batch:
+        raise ValueError("block_table / seq_lens have fewer rows than the batch")
+
+
+def append_quant_int4(key: torch.Tensor, value: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
+                      seq_lens: torch.Tensor, *, advance: bool = True,
+                      device_status: torch.Tensor | None = None) -> None:
+    """Quantise ``key``/``value`` ``[B, Hkv, n, D]`` into ``pool`` at positions ``seq_lens[b] + t``."""
+    require_cuda(key, value, block_table, seq_lens)
+    if key.shape != value.shape or key.dim() != 4:
+        raise ValueError("key and value must both be [batch, num_kv_heads, num_new, head_dim]")
+    if key.dtype != value.dtype:
+        raise ValueError("key and value must share a dtype")
+    b, h, n, d = key.shape
+    if h != pool.num_kv_heads or d != pool.head_dim:
+        raise ValueError(f"key shape {tuple(key.shape)} does not match the pool ({pool.num_kv_heads} heads, "
+                         f"head_dim {pool.head_dim})")
+    if key.stride(3) != 1 or value.stride(3) != 1:
+        key, value = key.contiguous(), value.contiguous()
+    _check_table(block_table, seq_lens, b)
+    call("oq_append_quant_int4", ptr(key), ptr(value), dtype_code(key.dtype), b, h, n, d,
+         key.stride(0), key.stride(1), key.stride(2), value.stride(0), value.stride(1), value.stride(2),
+         ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+         ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens), int(advance),
+         ptr(device_status), stream_ptr(key.device))
+
+
+def advance_seq_lens(seq_lens: torch.Tensor, delta: int = 1) -> None:
+    require_cuda(seq_lens)
+    call("oq_advance_seq_lens", ptr(seq_lens), seq_lens.shape[0], int(delta), stream_ptr(seq_lens.device))
+
+
+def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int = 148) -> int:
+    """Split count used when ``num_splits <= 0`` (kept in sync with the C side)."""
+    units = batch * num_kv_heads
+    target = sm_count * 6
+    splits = min(max(1, -(-target // units)), max_pages)
+    pps = -(-max_pages // splits)
+    return -(-max_pages // pps)
+
+
+def decode_workspace_bytes(batch: int, num_heads: int, num_kv_heads: int, max_splits: int,
+                           head_dim: int = HEAD_DIM_ATTN) -> int:
+    return int(_lib.load().oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, max_splits))
+
+
+def new_decode_workspace(batch: int, num_heads: int, num_kv_heads: int, max_pages: int,
+                         device: torch.device) -> torch.Tensor:
+    """Zero-filled workspace large enough for any split count of this batch shape."""
+    nbytes = decode_workspace_bytes(batch, num_heads, num_kv_heads, max(1, max_pages))
+    return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
+                          seq_lens: torch.Tensor, scaling: float, *, out: torch.Tensor | None = None,
+                          out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
+                          workspace: torch.Tensor | None = None, num_splits: int = 0,
+                          device_status: torch.Tensor | None = None, want_out: bool = True):
+    """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache.
+
+    Returns ``out`` (query dtype, ``[B, Hq, D]``) unless ``want_out`` is False.
+    """
+    require_cuda(query, block_table, seq_lens)
+    if query.dim() != 3:
+        raise ValueError("query must be [batch, num_heads, head_dim]")
+    if query.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("query must be bf16 or fp16")
+    b, hq, d = query.shape
+    if query.stride(2) != 1:
+        query = query.contiguous()
+    if pool.num_kv_heads <= 0 or hq % pool.num_kv_heads:
+        raise ValueError("Qwen GQA decode requires an integer query-to-KV head ratio.")
+    _check_table(block_table, seq_lens, b)
+    if want_out and out is None:
+        out = torch.empty((b, hq, d), dtype=query.dtype, device=query.device)
+    if workspace is None:
+        workspace = new_decode_workspace(b, hq, pool.num_kv_heads, block_table.shape[1], query.device)
+    for t, shape in ((out_f32, (b, hq, d)), (out_lse, (b, hq))):
+        if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous()):
+            raise ValueError("out_f32 / out_lse must be contiguous fp32 of shape [B, Hq, D] / [B, Hq]")
+    call("oq_decode_attn_int4_paged", ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
+         ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+         ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
+         b, hq, pool.num_kv_heads, d, float(scaling),
+         ptr(out), out.stride(0) if out is not None else 0, out.stride(1) if out is not None else 0,
+         ptr(out_f32), ptr(out_lse), ptr(workspace), workspace.numel(), int(num_splits),
+         ptr(device_status), stream_ptr(query.device))
+    return out
+
+
+def lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, dtype: torch.dtype = torch.bfloat16,
+              out: torch.Tensor | None = None, out_lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge ``part_out`` ``[N, R, D]`` / ``part_lse`` ``[N, R]`` (fp32) into ``[R, D]``."""
+    require_cuda(part_out, part_lse)
+    if part_out.dtype != torch.float32 or part_lse.dtype != torch.float32:
+        raise ValueError("partials must be fp32")
+    part_out, part_lse = part_out.contiguous(), part_lse.contiguous()
+    n, rows, d = part_out.shape
+    if tuple(part_lse.shape) != (n, rows):
+        raise ValueError("part_lse must be [num_parts, rows]")
+    if out is None:
+        out = torch.empty((rows, d), dtype=dtype, device=part_out.device)
+    call("oq_lse_merge", ptr(part_out), ptr(part_lse), n, rows, d, ptr(out), dtype_code(out.dtype), ptr(out_lse),
+         stream_ptr(part_out.device))
+    return out
+
+
+def gather_dequant_int4(pool: PagedKvPool, block_table: torch.Tensor, seq_lens: torch.Tensor, max_len: int,
+                        dtype: torch.dtype, *, device_status: torch.Tensor | None = None):
+    """Dequantised ``(keys, values)`` ``[B, Hkv, max_len, D]`` (rows past a sequence's length are 0)."""
+    require_cuda(block_table, seq_lens)
+    b = block_table.shape[0]
+    _check_table(block_table, seq_lens, b)
+    shape = (b, pool.num_kv_heads, int(max_len), pool.head_dim)
+    keys = torch.zeros(shape, dtype=dtype, device=pool.device)
+    values = torch.zeros(shape, dtype=dtype, device=pool.device)
+    call("oq_gather_dequant_int4", ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+         ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens), b, pool.num_kv_heads,
+         pool.head_dim, int(max_len), ptr(keys), ptr(values), dtype_code(dtype), ptr(device_status),
+         stream_ptr(pool.device))
+    return keys, values
+
+
+def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,
+                  scale: float | None = None, initial_state: torch.Tensor | None = None,
+                  final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  use_qk_l2norm: bool = False) -> torch.Tensor:
+    """Gated delta rule over ``T`` tokens: q, k ``[B, T, H, Dk]``, v ``[B, T, H, Dv]``, g/beta ``[B, T, H]``.
+
+    Writes ``final_state`` (may alias ``initial_state``) and returns ``out`` ``[B, T, H, Dv]``.
+    """
+    require_cuda(q, k, v, g, beta, initial_state, final_state)
+    if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError("q, k must be [B, T, H, Dk] and v [B, T, H, Dv]")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    bsz, t, h, dk = q.shape
+    dv = v.shape[-1]
+    q, k, v = (x if x.stride(3) == 1 else x.contiguous() for x in (q, k, v))
+    g, beta = g.contiguous(), beta.contiguous()
+    if tuple(g.shape) != (bsz, t, h) or tuple(beta.shape) != (bsz, t, h):
+        raise ValueError("g and beta must be [B, T, H]")
+    for s in (initial_state, final_state):
+        if s is not None and (s.dtype != torch.float32 or tuple(s.shape) != (bsz, h, dk, dv) or not s.is_contiguous()):
+            raise ValueError("states must be contiguous fp32 [B, H, Dk, Dv]")
+    if out is None:
+        out = torch.empty((bsz, t, h, dv), dtype=q.dtype, device=q.device)
+    scale = dk ** -0.5 if scale is None else float(scale)
+    call("oq_gdn_recurrent", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
+         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+         v.stride(0), v.stride(1), v.stride(2),
+         ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
+         ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
+         stream_ptr(q.device))
+    return out
+
+
+def pages_for(length: int, page_size: int = PAGE_SIZE) -> int:
+    return max(0, math.ceil(length / page_size))

@@ -1,0 +1,247 @@
+// Fused append-quantize into the paged INT4 KV cache.
+//
+// Replaces the reference's per-token torch.cat into a dense residual window and
+// its periodic groupwise quantise + torch.cat of the whole code tensor
+// (optiz_qwen/compression/qserve_kv_cache.py:210-232, 278-292, 313-335, 356-362).
+// Here every appended token is quantised at once into its page slot: one warp
+// per (token, KV head, K-or-V) row of head_dim values, min/max by warp shuffles,
+// codes from the fp32 scale/min with IEEE division and round-half-even exactly
+// as the reference computes them, then one 4-byte store per lane.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace oq {
+namespace {
+
+constexpr int kWarps = 4;
+
+struct AppendParams {
+  const void* key;
+  const void* value;
+  int64_t stride[2][3];  // [K/V][b, h, t] in elements
+  int64_t num_kv_heads, num_new;
+  uint8_t* kv_codes;
+  uint16_t* kv_meta;
+  int64_t num_pages, page_size;
+  const int32_t* block_table;
+  int64_t block_table_stride, max_pages_per_seq;
+  int32_t* seq_lens;
+  int advance;
+  int32_t* status;
+};
+
+template <typename T, int EPL, bool VEC>
+__device__ __forceinline__ void load_row(const T* row, int lane, float (&x)[EPL]) {
+  const T* p = row + lane * EPL;
+  if constexpr (VEC && (EPL * sizeof(T)) % 16 == 0) {
+    constexpr int kVecs = EPL * sizeof(T) / 16;
+    constexpr int kPer = 16 / sizeof(T);
+#pragma unroll
+    for (int v = 0; v < kVecs; ++v) {
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + v);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) x[v * kPer + i] = to_float<T>(e[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) x[i] = to_float<T>(p[i]);
+  }
+}
+
+// One (token, head, K|V) row per warp; head_dim = 32 * EPL.
+template <typename T, int EPL, bool VEC>
+__global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams p) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.y;
+  const int32_t start = p.seq_lens[b];
+  const int64_t jobs = p.num_kv_heads * p.num_new * 2;
+  constexpr int kHeadDim = EPL * 32;
+  constexpr int kRowBytes = kHeadDim / 2;
+
+  for (int64_t job = int64_t(blockIdx.x) * kWarps + warp; job < jobs; job += int64_t(gridDim.x) * kWarps) {
+    const int kv = int(job & 1);
+    const int64_t th = job >> 1;
+    const int64_t t = th % p.num_new;
+    const int64_t h = th / p.num_new;
+    const int64_t pos = int64_t(start) + t;
+    const int64_t logical_page = pos / p.page_size;
+    const int64_t slot = pos - logical_page * p.page_size;
+    if (logical_page >= p.max_pages_per_seq) {
+      if (lane == 0) report(p.status, OQ_DEV_OVERFLOW);
+      continue;
+    }
+    const int64_t page = p.block_table[b * p.block_table_stride + logical_page];
+    if (page < 0 || page >= p.num_pages) {
+      if (lane == 0) report(p.status, OQ_DEV_BAD_PAGE);
+      continue;
+    }
+
+    const T* src = static_cast<const T*>(kv ? p.value : p.key) + b * p.stride[kv][0] + h * p.stride[kv][1] +
+                   t * p.stride[kv][2];
+    float x[EPL];
+    load_row<T, EPL, VEC>(src, lane, x);
+
+    float mn = x[0], mx = x[0];
+#pragma unroll
+    for (int i = 1; i < EPL; ++i) {
+      mn = fminf(mn, x[i]);
+      mx = fmaxf(mx, x[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    // scale = (max - min) / 15 in fp32; 1 where it is not positive (qserve_kv_cache.py:326-328)
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    if (!(scale > 0.0f)) scale = 1.0f;
+
+    uint32_t packed[EPL / 8 > 0 ? EPL / 8 : 1] = {};
+    uint32_t small = 0;  // EPL < 8: fewer than 4 bytes per lane
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      float c = rintf(__fdiv_rn(__fsub_rn(x[i], mn), scale));
+      c = fminf(fmaxf(c, 0.0f), 15.0f);
+      const uint32_t code = static_cast<uint32_t>(c);
+      if constexpr (EPL >= 8) {
+        packed[i / 8] |= code << (4 * (i % 8));
+      } else {
+        small |= code << (4 * i);
+      }
+    }
+
+    const int64_t block = (page * p.num_kv_heads + h) * 2 + kv;
+    uint8_t* row = p.kv_codes + (block * p.page_size + slot) * kRowBytes + lane * (EPL / 2);
+    if constexpr (EPL >= 8) {
+#pragma unroll
+      for (int w = 0; w < EPL / 8; ++w) reinterpret_cast<uint32_t*>(row)[w] = packed[w];
+    } else if constexpr (EPL == 4) {
+      *reinterpret_cast<uint16_t*>(row) = static_cast<uint16_t>(small);
+    } else {
+      *row = static_cast<uint8_t>(small);
+    }
+    if (lane == 0) {
+      uint16_t* meta = p.kv_meta + ((page * p.num_kv_heads + h) * 4 + kv * 2) * p.page_size + slot;
+      meta[0] = __half_as_ushort(__float2half_rn(scale));
+      meta[p.page_size] = __half_as_ushort(__float2half_rn(mn));
+    }
+  }
+  if (p.advance) {
+    __syncthreads();  // every warp has read seq_lens[b]
+    if (threadIdx.x == 0) p.seq_lens[b] = start + int32_t(p.num_new);
+  }
+}
+
+__global__ void advance_kernel(int32_t* seq_lens, int64_t batch, int32_t delta) {
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < batch) seq_lens[i] += delta;
+}
+
+template <typename T, int EPL>
+void launch_append(const AppendParams& p, bool vec, dim3 grid, cudaStream_t s) {
+  if (vec) {
+    append_quant_kernel<T, EPL, true><<<grid, kWarps * 32, 0, s>>>(p);
+  } else {
+    append_quant_kernel<T, EPL, false><<<grid, kWarps * 32, 0, s>>>(p);
+  }
+}
+
+template <typename T>
+void launch_dim(const AppendParams& p, int64_t head_dim, bool vec, dim3 grid, cudaStream_t s) {
+  switch (head_dim) {
+    case 64: launch_append<T, 2>(p, vec, grid, s); break;
+    case 128: launch_append<T, 4>(p, vec, grid, s); break;
+    case 256: launch_append<T, 8>(p, vec, grid, s); break;
+    default: launch_append<T, 16>(p, vec, grid, s); break;  // 512
+  }
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_advance_seq_lens(int32_t* seq_lens, int64_t batch, int32_t delta, void* stream) {
+  using namespace oq;
+  if (seq_lens == nullptr || batch < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "advance_seq_lens: bad arguments");
+  if (batch == 0) return ok();
+  const int threads = 256;
+  advance_kernel<<<unsigned((batch + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      seq_lens, batch, delta);
+  return check_launch("advance_seq_lens");
+}
+
+extern "C" int oq_append_quant_int4(
+    const void* key, const void* value, int dtype,
+    int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
+    int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
+    int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    int32_t* seq_lens, int advance_seq_lens,
+    int32_t* device_status, void* stream) {
+  using namespace oq;
+  if (!valid_dtype(dtype)) return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: unknown dtype %d", dtype);
+  if (batch < 0 || num_kv_heads <= 0 || num_new < 0 || num_pages <= 0 || page_size <= 0 ||
+      max_pages_per_seq <= 0 || block_table_stride < max_pages_per_seq) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: bad sizes");
+  }
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512) {
+    return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: head_dim %lld not in {64,128,256,512}",
+                (long long)head_dim);
+  }
+  if (batch == 0 || num_new == 0) return ok();
+  if (!key || !value || !kv_codes || !kv_meta || !block_table || !seq_lens) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: null pointer");
+  }
+  const int64_t esize = dtype == OQ_F32 ? 4 : 2;
+  const int64_t strides[6] = {key_stride_b, key_stride_h, key_stride_t, value_stride_b, value_stride_h, value_stride_t};
+  bool vec = (reinterpret_cast<uintptr_t>(key) % 16 == 0) && (reinterpret_cast<uintptr_t>(value) % 16 == 0) &&
+             ((head_dim / 32) * esize % 16 == 0);
+  for (int64_t s : strides) {
+    if (s < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: negative stride");
+    vec = vec && ((s * esize) % 16 == 0);
+  }
+
+  AppendParams p;
+  p.key = key;
+  p.value = value;
+  for (int i = 0; i < 3; ++i) {
+    p.stride[0][i] = strides[i];
+    p.stride[1][i] = strides[3 + i];
+  }
+  p.num_kv_heads = num_kv_heads;
+  p.num_new = num_new;
+  p.kv_codes = kv_codes;
+  p.kv_meta = kv_meta;
+  p.num_pages = num_pages;
+  p.page_size = page_size;
+  p.block_table = block_table;
+  p.block_table_stride = block_table_stride;
+  p.max_pages_per_seq = max_pages_per_seq;
+  p.seq_lens = seq_lens;
+  p.status = device_status;
+
+  // Decode appends (a few rows per sequence) run one CTA per sequence and bump
+  // seq_lens in the same launch; bulk appends (prefill adoption) spread over
+  // more CTAs and bump seq_lens with a follow-up launch on the same stream.
+  const int64_t jobs = num_kv_heads * num_new * 2;
+  const int64_t blocks_x = std::min<int64_t>((jobs + kWarps - 1) / kWarps, 1024);
+  const bool fused_advance = blocks_x == 1;
+  p.advance = (advance_seq_lens && fused_advance) ? 1 : 0;
+  if (batch > 65535) return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: batch > 65535");
+  dim3 grid((unsigned)blocks_x, (unsigned)batch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case OQ_F32: launch_dim<float>(p, head_dim, vec, grid, s); break;
+    case OQ_F16: launch_dim<__half>(p, head_dim, vec, grid, s); break;
+    default: launch_dim<__nv_bfloat16>(p, head_dim, vec, grid, s); break;
+  }
+  int st = check_launch("append_quant_int4");
+  if (st != OQ_OK) return st;
+  if (advance_seq_lens && !fused_advance) {
+    return oq_advance_seq_lens(seq_lens, batch, int32_t(num_new), stream);
+  }
+  return ok();
+}

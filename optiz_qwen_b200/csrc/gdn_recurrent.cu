@@ -1,0 +1,223 @@
+// Gated delta rule, recurrent form (the GDN decode step).
+//
+// Replaces the hook `recurrent_gated_delta_rule` of Qwen3_5GatedDeltaNet
+// (transformers models/qwen3_5/modeling_qwen3_5.py:511-520; fla 0.5.1
+// fused_recurrent_gated_delta_rule, fla/ops/gated_delta_rule/fused_recurrent.py:291;
+// torch fallback modeling_qwen3_5.py:314-353).  The fp32 state of one head is
+// 128 x 128 = 64 KiB; a CTA owns a 128 x 32 column slice of it in registers
+// (32 floats per thread), so every state byte crosses HBM exactly once per
+// launch in each direction, however many tokens the launch steps through:
+//   S *= exp(g);  kv = S^T k;  delta = beta (v - kv);  S += k delta^T;  o = S^T q.
+// Column sums over the 128 state rows are reduced with warp shuffles and a
+// 4-warp shared-memory step.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace oq {
+namespace {
+
+constexpr int kDk = 128;
+constexpr int kDv = 128;
+constexpr int kCols = 32;               // state columns per CTA
+constexpr int kThreads = 128;           // = kDk: one q/k element per thread when loading
+constexpr int kRowsPerThread = kDk / 16;  // 16 row groups x 8 rows
+
+struct GdnParams {
+  const void *q, *k, *v;
+  int64_t qs[3], ks[3], vs[3];  // strides (b, t, h) in elements
+  const void *g, *beta;
+  int g_dtype, beta_dtype;
+  const float* s_in;
+  float* s_out;
+  void* out;
+  int64_t seq_len, num_heads;
+  float scale;
+  int l2norm;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
+  __shared__ float q_s[kDk], k_s[kDk], v_s[kCols];
+  __shared__ float red_kv[4][kCols], red_o[4][kCols];
+  __shared__ float norm_q[4], norm_k[4];
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int cg = lane & 7;                 // column group: columns 4cg .. 4cg+3 of the slice
+  const int rg = (lane >> 3) + 4 * warp;   // row group: rows rg + 16 i
+  const int v0 = blockIdx.x * kCols;
+  const int64_t h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t H = p.num_heads;
+
+  float S[kRowsPerThread][4];
+  const int64_t state_off = ((b * H + h) * kDk) * kDv + v0 + 4 * cg;
+  if (p.s_in != nullptr) {
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      const float4 x = *reinterpret_cast<const float4*>(p.s_in + state_off + int64_t(rg + 16 * i) * kDv);
+      S[i][0] = x.x;
+      S[i][1] = x.y;
+      S[i][2] = x.z;
+      S[i][3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) S[i][0] = S[i][1] = S[i][2] = S[i][3] = 0.0f;
+  }
+
+  for (int64_t t = 0; t < p.seq_len; ++t) {
+    const T* qrow = static_cast<const T*>(p.q) + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+    const T* krow = static_cast<const T*>(p.k) + b * p.ks[0] + t * p.ks[1] + h * p.ks[2];
+    const T* vrow = static_cast<const T*>(p.v) + b * p.vs[0] + t * p.vs[1] + h * p.vs[2];
+    const float qv = to_float<T>(qrow[tid]);
+    const float kvv = to_float<T>(krow[tid]);
+    q_s[tid] = qv;
+    k_s[tid] = kvv;
+    if (tid < kCols) v_s[tid] = to_float<T>(vrow[v0 + tid]);
+    if (p.l2norm) {
+      float sq = qv * qv, sk = kvv * kvv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      }
+      if (lane == 0) {
+        norm_q[warp] = sq;
+        norm_k[warp] = sk;
+      }
+    }
+    const int64_t gi = (b * p.seq_len + t) * H + h;
+    const float gt = load_as_float(p.g, p.g_dtype, gi);
+    const float bt = load_as_float(p.beta, p.beta_dtype, gi);
+    __syncthreads();
+
+    float inv_q = 1.0f, inv_k = 1.0f;
+    if (p.l2norm) {
+      // l2norm: x * rsqrt(sum(x*x) + 1e-6)  (modeling_qwen3_5.py:228-231)
+      inv_q = 1.0f / sqrtf((norm_q[0] + norm_q[1]) + (norm_q[2] + norm_q[3]) + 1e-6f);
+      inv_k = 1.0f / sqrtf((norm_k[0] + norm_k[1]) + (norm_k[2] + norm_k[3]) + 1e-6f);
+    }
+    const float decay = expf(gt);
+
+    // S *= exp(g); partial kv = sum_rows S * k
+    float kv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float kr[kRowsPerThread];
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      kr[i] = __fmul_rn(k_s[rg + 16 * i], inv_k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        S[i][j] = __fmul_rn(S[i][j], decay);
+        kv[j] = fmaf(S[i][j], kr[i], kv[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], 8);
+      kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], 16);
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red_kv[warp][4 * cg + j] = kv[j];
+    }
+    __syncthreads();
+
+    // delta = beta (v - kv); S += k delta^T; partial o = sum_rows S * q
+    float delta[4], o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = 4 * cg + j;
+      const float kvs = (red_kv[0][col] + red_kv[1][col]) + (red_kv[2][col] + red_kv[3][col]);
+      delta[j] = __fmul_rn(__fsub_rn(v_s[col], kvs), bt);
+    }
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      const float qr = __fmul_rn(__fmul_rn(q_s[rg + 16 * i], inv_q), p.scale);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        S[i][j] = fmaf(kr[i], delta[j], S[i][j]);
+        o[j] = fmaf(S[i][j], qr, o[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o[j] += __shfl_xor_sync(0xffffffffu, o[j], 8);
+      o[j] += __shfl_xor_sync(0xffffffffu, o[j], 16);
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red_o[warp][4 * cg + j] = o[j];
+    }
+    __syncthreads();
+    if (tid < kCols) {
+      const float ov = (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]);
+      static_cast<T*>(p.out)[((b * p.seq_len + t) * H + h) * kDv + v0 + tid] = from_float<T>(ov);
+    }
+  }
+
+  if (p.s_out != nullptr) {
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      *reinterpret_cast<float4*>(p.s_out + state_off + int64_t(rg + 16 * i) * kDv) =
+          make_float4(S[i][0], S[i][1], S[i][2], S[i][3]);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_gdn_recurrent(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, void* stream) {
+  using namespace oq;
+  if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
+    return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
+  }
+  if (k_dim != kDk || v_dim != kDv) return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: k_dim = v_dim = 128 required");
+  if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_recurrent: bad sizes");
+  if (batch == 0) return ok();
+  if (batch > 65535 || num_heads > 65535) return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: grid too large");
+  if (!g || !beta || (seq_len > 0 && (!q || !k || !v || !out))) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_recurrent: null pointer");
+  }
+  if ((initial_state && reinterpret_cast<uintptr_t>(initial_state) % 16) ||
+      (final_state && reinterpret_cast<uintptr_t>(final_state) % 16)) {
+    return fail(OQ_ERR_MISALIGNED, "gdn_recurrent: state must be 16-byte aligned");
+  }
+  GdnParams p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.qs[0] = q_stride_b; p.qs[1] = q_stride_t; p.qs[2] = q_stride_h;
+  p.ks[0] = k_stride_b; p.ks[1] = k_stride_t; p.ks[2] = k_stride_h;
+  p.vs[0] = v_stride_b; p.vs[1] = v_stride_t; p.vs[2] = v_stride_h;
+  p.g = g;
+  p.beta = beta;
+  p.g_dtype = g_dtype;
+  p.beta_dtype = beta_dtype;
+  p.s_in = initial_state;
+  p.s_out = final_state;
+  p.out = out;
+  p.seq_len = seq_len;
+  p.num_heads = num_heads;
+  p.scale = scale;
+  p.l2norm = use_qk_l2norm;
+  dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (qkv_dtype) {
+    case OQ_F32: gdn_recurrent_kernel<float><<<grid, kThreads, 0, s>>>(p); break;
+    case OQ_F16: gdn_recurrent_kernel<__half><<<grid, kThreads, 0, s>>>(p); break;
+    default: gdn_recurrent_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(p); break;
+  }
+  return check_launch("gdn_recurrent");
+}

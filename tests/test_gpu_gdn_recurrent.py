@@ -1,0 +1,111 @@
+"""Parity of the GDN recurrent kernel: state and outputs rel 1e-4 in fp32."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn
+from oracle import kv_quant as kq
+from tests._util import assert_gdn_close
+
+pytestmark = pytest.mark.gpu
+
+GOLD = __file__.replace("test_gpu_gdn_recurrent.py", "golden/gdn_golden.npz")
+
+
+def _t(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda().to(dtype)
+
+
+def _config0_inputs(rng, b=2, t=1, h=16, d=128):
+    """Config-0 distributions: q,k,v bf16 N(0,1); beta = sigmoid(N); g = -softplus(N); S = 0.02 N."""
+    q = kq.round_bf16(rng.standard_normal((b, t, h, d), dtype=np.float32))
+    k = kq.round_bf16(rng.standard_normal((b, t, h, d), dtype=np.float32))
+    v = kq.round_bf16(rng.standard_normal((b, t, h, d), dtype=np.float32))
+    beta = 1.0 / (1.0 + np.exp(-rng.standard_normal((b, t, h), dtype=np.float32)))
+    g = -np.logaddexp(0.0, rng.standard_normal((b, t, h), dtype=np.float32)).astype(np.float32)
+    s0 = (0.02 * rng.standard_normal((b, h, d, d), dtype=np.float32)).astype(np.float32)
+    return q, k, v, g, beta.astype(np.float32), s0
+
+
+@pytest.mark.parametrize("name", ["step", "multi"])
+def test_reference_golden(name):
+    from optiz_qwen_b200.cabi import gdn_recurrent
+
+    gold = np.load(GOLD)
+    s = _t(gold[f"{name}_s0"]).clone()
+    out = gdn_recurrent(_t(gold[f"{name}_q"]), _t(gold[f"{name}_k"]), _t(gold[f"{name}_v"]), _t(gold[f"{name}_g"]),
+                        _t(gold[f"{name}_beta"]), initial_state=s, final_state=s, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), gold[f"{name}_o"])
+    assert_gdn_close(s.cpu().numpy(), gold[f"{name}_s"])
+
+
+def test_config0_step_fp32():
+    from optiz_qwen_b200.cabi import gdn_recurrent
+
+    rng = np.random.default_rng(0)
+    q, k, v, g, beta, s0 = _config0_inputs(rng)
+    ref_o, ref_s = gdn.recurrent_gated_delta_rule(q, k, v, g, beta, s0, True, True)
+    s_out = torch.empty_like(_t(s0))
+    out = gdn_recurrent(_t(q), _t(k), _t(v), _t(g), _t(beta), initial_state=_t(s0), final_state=s_out,
+                        use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), ref_o)
+    assert_gdn_close(s_out.cpu().numpy(), ref_s)
+
+
+def test_bf16_inputs_bf16_beta():
+    """Model dtypes: q/k/v/beta bf16, g fp32.  State stays fp32 (rel 1e-4); the bf16 output
+    is within bf16 rounding of the fp32 oracle."""
+    from optiz_qwen_b200.cabi import gdn_recurrent
+
+    rng = np.random.default_rng(1)
+    q, k, v, g, beta, s0 = _config0_inputs(rng, b=3, t=1)
+    beta = kq.round_bf16(beta)
+    ref_o, ref_s = gdn.recurrent_gated_delta_rule(q, k, v, g, beta, s0, True, True)
+    s = _t(s0)
+    out = gdn_recurrent(_t(q, torch.bfloat16), _t(k, torch.bfloat16), _t(v, torch.bfloat16), _t(g),
+                        _t(beta, torch.bfloat16), initial_state=s, final_state=s, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.bfloat16
+    assert_gdn_close(s.cpu().numpy(), ref_s)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref_o, rtol=8e-3, atol=8e-3 * np.abs(ref_o).max())
+
+
+def test_multi_token_no_initial_state_no_l2norm():
+    from optiz_qwen_b200.cabi import gdn_recurrent
+
+    rng = np.random.default_rng(2)
+    q, k, v, g, beta, _ = _config0_inputs(rng, b=2, t=37, h=3)
+    k = gdn.l2norm(k)
+    q = gdn.l2norm(q)
+    ref_o, ref_s = gdn.recurrent_gated_delta_rule(q, k, v, g, beta, None, True, False, scale=0.3)
+    s_out = torch.empty((2, 3, 128, 128), device="cuda")
+    out = gdn_recurrent(_t(q), _t(k), _t(v), _t(g), _t(beta), scale=0.3, final_state=s_out)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), ref_o)
+    assert_gdn_close(s_out.cpu().numpy(), ref_s)
+
+
+def test_strided_qkv_views():
+    """q/k/v as views of one fused projection (the module's torch.split layout)."""
+    from optiz_qwen_b200.cabi import gdn_recurrent
+
+    rng = np.random.default_rng(3)
+    b, t, h, d = 2, 3, 4, 128
+    mixed = kq.round_bf16(rng.standard_normal((b, t, 3 * h * d), dtype=np.float32))
+    mt = _t(mixed)
+    q, k, v = (x.reshape(b, t, h, d) for x in torch.split(mt, [h * d] * 3, dim=-1))
+    g = -np.logaddexp(0.0, rng.standard_normal((b, t, h))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((b, t, h))))).astype(np.float32)
+    s0 = (0.02 * rng.standard_normal((b, h, d, d))).astype(np.float32)
+    ref_o, ref_s = gdn.recurrent_gated_delta_rule(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), g, beta, s0,
+                                                  True, True)
+    s = _t(s0)
+    out = gdn_recurrent(q, k, v, _t(g), _t(beta), initial_state=s, final_state=s, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), ref_o)
+    assert_gdn_close(s.cpu().numpy(), ref_s)
