@@ -97,7 +97,7 @@ def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int =
     """Split count used when ``num_splits <= 0`` (kept in sync with the C side)."""
     units = batch * num_kv_heads
     target = sm_count * 6
-    splits = min(max(1, -(-target // units)), max_pages)
+    splits = min(max(1, -(-target // units)), max_pages, 512)
     pps = -(-max_pages // splits)
     return -(-max_pages // pps)
 

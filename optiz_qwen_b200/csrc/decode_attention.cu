@@ -38,6 +38,7 @@ constexpr int kStages = 4;
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 8;
+constexpr int kMaxSplits = 512;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz: a copy that has not landed by then never will
 
 struct AttnParams {
@@ -72,23 +73,24 @@ struct __align__(16) SmemTail {
 constexpr size_t kSmemBytes =
     1024 /*alignment slack*/ + kStages * (kStageCodeBytes + kStageMetaBytes) + sizeof(SmemTail);
 
+// Nibble -> 16-bit float conversion.  lop3 puts codes c0 (bits 0-3) and c4
+// (bits 16-19) of a word into the mantissa of an exponent-biased constant, giving
+// (bias + c) exactly; callers either fold the bias into the epilogue or subtract it.
 template <typename T> struct QkTraits;
 template <> struct QkTraits<__nv_bfloat16> {
-  static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128.0 in both halves
-  static __device__ __forceinline__ uint32_t to_codes(uint32_t x) {
-    uint32_t v = lop3_and_or(x, 0x000F000Fu, kMagic);
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
-    __nv_bfloat162 r = __hsub2(h, __floats2bfloat162_rn(128.0f, 128.0f));
-    return *reinterpret_cast<uint32_t*>(&r);
-  }
+  // q.k runs on bf16 operands: codes become 128 + c; the 128 * sum(q) term is
+  // removed in the score epilogue.
+  static constexpr float kBias = 128.0f;
+  static __device__ __forceinline__ uint32_t codes(uint32_t x) { return lop3_and_or(x, 0x000F000Fu, 0x43004300u); }
   static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     mma_bf16_16816(d, a, b0, b1);
   }
 };
 template <> struct QkTraits<__half> {
-  static constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
-  static __device__ __forceinline__ uint32_t to_codes(uint32_t x) {
-    uint32_t v = lop3_and_or(x, 0x000F000Fu, kMagic);
+  // fp16 queries: exact codes (1024 + c) - 1024.
+  static constexpr float kBias = 0.0f;
+  static __device__ __forceinline__ uint32_t codes(uint32_t x) {
+    uint32_t v = lop3_and_or(x, 0x000F000Fu, 0x64006400u);
     __half2 h = *reinterpret_cast<__half2*>(&v);
     __half2 r = __hsub2(h, __floats2half2_rn(1024.0f, 1024.0f));
     return *reinterpret_cast<uint32_t*>(&r);
@@ -98,8 +100,16 @@ template <> struct QkTraits<__half> {
   }
 };
 
-// fp16 codes for the p.v product (both operands fp16).
-__device__ __forceinline__ uint32_t codes_f16(uint32_t x) { return QkTraits<__half>::to_codes(x); }
+// p.v runs on fp16 operands: codes become 1024 + c, removed with 1024 * sum(P').
+constexpr float kVBias = 1024.0f;
+__device__ __forceinline__ uint32_t v_codes(uint32_t x) { return lop3_and_or(x, 0x000F000Fu, 0x64006400u); }
+
+// Lazy softmax rescale: the running max only moves when a tile's max exceeds it
+// by more than kTau (log2 units), so p <= 2^kTau; P' = p * v_scale * 2^-kTau
+// therefore stays inside the fp16 range whatever the stored fp16 scale.
+constexpr float kTau = 4.0f;
+constexpr float kPScale = 0.0625f;  // 2^-kTau
+constexpr float kPUnscale = 16.0f;
 
 // Shared-memory address of 16-byte chunk `chunk` of row `row` in a 128B-swizzled stage.
 __device__ __forceinline__ const uint4* swz(const uint8_t* base, int row, int chunk) {
@@ -113,6 +123,19 @@ __device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
     if (clock64() - t0 > kWaitCycles) return false;
   }
   return true;
+}
+
+__device__ __forceinline__ float lse_nat(float m_log2, float l) {
+  return l > 0.0f ? (m_log2 + log2f(l)) * 0.69314718055994531f : -INFINITY;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
+                                          float l) {
+  const int64_t hq_total = p.num_kv_heads * p.group;
+  if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(o);
+  if (p.out_f32) p.out_f32[(b * hq_total + hq) * kHeadDim + d] = o;
+  if (p.out_lse && d == 0) p.out_lse[b * hq_total + hq] = lse_nat(m, l);
 }
 
 template <typename T>
@@ -197,9 +220,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   float acc[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-  float m_a = -INFINITY, m_b = -INFINITY;  // running max (log2 units) of heads 2c, 2c+1
-  float l_a = 0.0f, l_b = 0.0f;            // this lane's share of the softmax sums
-  float mp_a = 0.0f, mp_b = 0.0f;          // this lane's share of sum(p * v_min)
+  float m_a = -INFINITY, m_b = -INFINITY;  // reference max (log2 units) of heads 2c, 2c+1
+  float l_a = 0.0f, l_b = 0.0f;            // this lane's share of sum(p)
+  float mp_a = 0.0f, mp_b = 0.0f;          // ... of sum(p * v_min)
+  float sp_a = 0.0f, sp_b = 0.0f;          // ... of sum(P') with P' as rounded to fp16
 
   const int tok0 = warp * 16 + r;  // token rows of this lane in the page (A rows r and r+8)
   const int tok1 = tok0 + 8;
@@ -214,26 +238,31 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     if (ready && tail->stage_ok[s] && warp * 16 < page_tokens) {
       const uint8_t* st = codes + s * kStageCodeBytes;
       const __half* meta = reinterpret_cast<const __half*>(metas + s * kStageMetaBytes);
+      const int tb = warp * 16 + kPage;  // V rows follow the 64 K rows
+      const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
+      const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
+      const uint4 va = *swz(st, tb + 2 * c, r), vb = *swz(st, tb + 2 * c + 1, r);
+      const uint4 vc = *swz(st, tb + 2 * c + 8, r), vd = *swz(st, tb + 2 * c + 9, r);
 
-      // ---------------- scores: A = K codes (16 tokens x 16 dims), B = q (16 dims x 8 heads)
-      float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // ---------------- scores: A = K codes (16 tokens x 16 dims), B = q (16 dims x 8 heads);
+      // two independent accumulator chains
+      float sc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       {
-        const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
-        const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
         const uint32_t w0[8] = {k00.x, k00.y, k00.z, k00.w, k01.x, k01.y, k01.z, k01.w};
         const uint32_t w1[8] = {k10.x, k10.y, k10.z, k10.w, k11.x, k11.y, k11.z, k11.w};
 #pragma unroll
         for (int wi = 0; wi < 8; ++wi) {
+          float(&sc)[4] = (wi & 1) ? sc1 : sc0;
           uint32_t a[4];
-          a[0] = Q::to_codes(w0[wi]);
-          a[1] = Q::to_codes(w1[wi]);
-          a[2] = Q::to_codes(w0[wi] >> 4);
-          a[3] = Q::to_codes(w1[wi] >> 4);
+          a[0] = Q::codes(w0[wi]);
+          a[1] = Q::codes(w1[wi]);
+          a[2] = Q::codes(w0[wi] >> 4);
+          a[3] = Q::codes(w1[wi] >> 4);
           Q::mma(sc, a, qb[2 * wi][0], qb[2 * wi][1]);
-          a[0] = Q::to_codes(w0[wi] >> 8);
-          a[1] = Q::to_codes(w1[wi] >> 8);
-          a[2] = Q::to_codes(w0[wi] >> 12);
-          a[3] = Q::to_codes(w1[wi] >> 12);
+          a[0] = Q::codes(w0[wi] >> 8);
+          a[1] = Q::codes(w1[wi] >> 8);
+          a[2] = Q::codes(w0[wi] >> 12);
+          a[3] = Q::codes(w1[wi] >> 12);
           Q::mma(sc, a, qb[2 * wi + 1][0], qb[2 * wi + 1][1]);
         }
       }
@@ -242,47 +271,62 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       const float ks1 = __half2float(meta[tok1]), km1 = __half2float(meta[kPage + tok1]);
       const float vs0 = __half2float(meta[2 * kPage + tok0]), vm0 = __half2float(meta[3 * kPage + tok0]);
       const float vs1 = __half2float(meta[2 * kPage + tok1]), vm1 = __half2float(meta[3 * kPage + tok1]);
-      const float s0a = v0 ? (ks0 * sc[0] + km0 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s0b = v0 ? (ks0 * sc[1] + km0 * qs_b) * p.scale_log2 : -INFINITY;
-      const float s1a = v1 ? (ks1 * sc[2] + km1 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s1b = v1 ? (ks1 * sc[3] + km1 * qs_b) * p.scale_log2 : -INFINITY;
+      // q.k = scale * sum(q * (bias + c)) + (min - bias * scale) * sum(q)
+      const float kb0 = fmaf(-Q::kBias, ks0, km0), kb1 = fmaf(-Q::kBias, ks1, km1);
+      const float s0a = v0 ? fmaf(ks0, sc0[0] + sc1[0], kb0 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s0b = v0 ? fmaf(ks0, sc0[1] + sc1[1], kb0 * qs_b) * p.scale_log2 : -INFINITY;
+      const float s1a = v1 ? fmaf(ks1, sc0[2] + sc1[2], kb1 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s1b = v1 ? fmaf(ks1, sc0[3] + sc1[3], kb1 * qs_b) * p.scale_log2 : -INFINITY;
 
-      // ---------------- online softmax over this 16-token tile
+      // ---------------- online softmax with a lazily moved reference max
       float tm_a = fmaxf(s0a, s1a), tm_b = fmaxf(s0b, s1b);
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
         tm_a = fmaxf(tm_a, __shfl_xor_sync(0xffffffffu, tm_a, o));
         tm_b = fmaxf(tm_b, __shfl_xor_sync(0xffffffffu, tm_b, o));
       }
-      const float nm_a = fmaxf(m_a, tm_a), nm_b = fmaxf(m_b, tm_b);
-      const float corr_a = nm_a == -INFINITY ? 1.0f : exp2f(m_a - nm_a);
-      const float corr_b = nm_b == -INFINITY ? 1.0f : exp2f(m_b - nm_b);
-      const float p0a = v0 ? exp2f(s0a - nm_a) : 0.0f, p0b = v0 ? exp2f(s0b - nm_b) : 0.0f;
-      const float p1a = v1 ? exp2f(s1a - nm_a) : 0.0f, p1b = v1 ? exp2f(s1b - nm_b) : 0.0f;
-      m_a = nm_a;
-      m_b = nm_b;
-      l_a = l_a * corr_a + p0a + p1a;
-      l_b = l_b * corr_b + p0b + p1b;
-      mp_a = mp_a * corr_a + (v0 ? p0a * vm0 : 0.0f) + (v1 ? p1a * vm1 : 0.0f);
-      mp_b = mp_b * corr_b + (v0 ? p0b * vm0 : 0.0f) + (v1 ? p1b * vm1 : 0.0f);
+      if (__any_sync(0xffffffffu, tm_a > m_a + kTau || tm_b > m_b + kTau)) {
+        const float nm_a = fmaxf(m_a, tm_a), nm_b = fmaxf(m_b, tm_b);
+        const float corr_a = nm_a == -INFINITY ? 1.0f : exp2f(m_a - nm_a);
+        const float corr_b = nm_b == -INFINITY ? 1.0f : exp2f(m_b - nm_b);
+        m_a = nm_a;
+        m_b = nm_b;
+        l_a *= corr_a;
+        l_b *= corr_b;
+        mp_a *= corr_a;
+        mp_b *= corr_b;
+        sp_a *= corr_a;
+        sp_b *= corr_b;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        acc[j][0] *= corr_a;
-        acc[j][2] *= corr_a;
-        acc[j][1] *= corr_b;
-        acc[j][3] *= corr_b;
+        for (int j = 0; j < 16; ++j) {
+          acc[j][0] *= corr_a;
+          acc[j][2] *= corr_a;
+          acc[j][1] *= corr_b;
+          acc[j][3] *= corr_b;
+        }
       }
-      // P' = p * v_scale in fp16, rows = tokens, cols = heads; transpose into the B operand of p.v
-      const uint32_t blk0 = pack_half2(v0 ? p0a * vs0 : 0.0f, v0 ? p0b * vs0 : 0.0f);
-      const uint32_t blk1 = pack_half2(v1 ? p1a * vs1 : 0.0f, v1 ? p1b * vs1 : 0.0f);
+      const float p0a = v0 ? exp2f(s0a - m_a) : 0.0f, p0b = v0 ? exp2f(s0b - m_b) : 0.0f;
+      const float p1a = v1 ? exp2f(s1a - m_a) : 0.0f, p1b = v1 ? exp2f(s1b - m_b) : 0.0f;
+      l_a += p0a + p1a;
+      l_b += p0b + p1b;
+      mp_a += (v0 ? p0a * vm0 : 0.0f) + (v1 ? p1a * vm1 : 0.0f);
+      mp_b += (v0 ? p0b * vm0 : 0.0f) + (v1 ? p1b * vm1 : 0.0f);
+      // P' = p * v_scale * 2^-kTau in fp16, rows = tokens, cols = heads
+      const float ps0 = v0 ? vs0 * kPScale : 0.0f, ps1 = v1 ? vs1 * kPScale : 0.0f;
+      const uint32_t blk0 = pack_half2(p0a * ps0, p0b * ps0);
+      const uint32_t blk1 = pack_half2(p1a * ps1, p1b * ps1);
+      {
+        const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&blk0));
+        const float2 r1 = __half22float2(*reinterpret_cast<const __half2*>(&blk1));
+        sp_a += r0.x + r1.x;
+        sp_b += r0.y + r1.y;
+      }
+      // transpose into the B operand of p.v
       const uint32_t pb0 = movmatrix_trans(blk0);
       const uint32_t pb1 = movmatrix_trans(blk1);
 
       // ---------------- values: A = V^T codes (16 dims x 16 tokens), B = P' (16 tokens x 8 heads)
       {
-        const int tb = warp * 16 + kPage;  // V rows follow the 64 K rows
-        const uint4 va = *swz(st, tb + 2 * c, r), vb = *swz(st, tb + 2 * c + 1, r);
-        const uint4 vc = *swz(st, tb + 2 * c + 8, r), vd = *swz(st, tb + 2 * c + 9, r);
         const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
         const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w}, wd[4] = {vd.x, vd.y, vd.z, vd.w};
 #pragma unroll
@@ -295,10 +339,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             const uint32_t y = u < 2 ? y_lo : y_hi;
             const int sh = (u & 1) * 8;
             uint32_t a[4];
-            a[0] = codes_f16(x >> sh);
-            a[1] = codes_f16(x >> (sh + 4));
-            a[2] = codes_f16(y >> sh);
-            a[3] = codes_f16(y >> (sh + 4));
+            a[0] = v_codes(x >> sh);
+            a[1] = v_codes(x >> (sh + 4));
+            a[2] = v_codes(y >> sh);
+            a[3] = v_codes(y >> (sh + 4));
             mma_f16_16816(acc[4 * wi + u], a, pb0, pb1);
           }
         }
@@ -326,13 +370,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     return;
   }
 
-  // ---- reduce this warp's softmax sums over the 8 token rows
+  // ---- reduce this warp's per-lane sums over the 8 token rows
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
     l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
     mp_a += __shfl_xor_sync(0xffffffffu, mp_a, o);
     mp_b += __shfl_xor_sync(0xffffffffu, mp_b, o);
+    sp_a += __shfl_xor_sync(0xffffffffu, sp_a, o);
+    sp_b += __shfl_xor_sync(0xffffffffu, sp_b, o);
   }
   if (r == 0) {
     tail->warp_m[warp][2 * c] = m_a;
@@ -342,7 +388,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();  // also: every stage has been consumed, codes[] is free for reuse
 
-  // ---- merge the 4 warps: red[w][h][d] = (acc + sum(p*min)) * 2^(m_w - M)
+  // ---- merge the 4 warps: red[w][h][d] = numerator_w * 2^(m_w - M),
+  //      numerator = 2^kTau * (acc - 1024 * sum(P')) + sum(p * v_min)
   float* red = reinterpret_cast<float*>(codes);  // kWarps * kMaxGroup * 256 floats = 32 KB
   {
     const int ha = 2 * c, hb = 2 * c + 1;
@@ -357,16 +404,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][hb]);
       fb = M == -INFINITY ? 0.0f : exp2f(m_b - M);
     }
+    const float off_a = -kVBias * sp_a, off_b = -kVBias * sp_b;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int d0 = 32 * r + 2 * j;
       if (ha < G) {
-        red[(warp * kMaxGroup + ha) * kHeadDim + d0] = (acc[j][0] + mp_a) * fa;
-        red[(warp * kMaxGroup + ha) * kHeadDim + d0 + 1] = (acc[j][2] + mp_a) * fa;
+        red[(warp * kMaxGroup + ha) * kHeadDim + d0] = fmaf(acc[j][0] + off_a, kPUnscale, mp_a) * fa;
+        red[(warp * kMaxGroup + ha) * kHeadDim + d0 + 1] = fmaf(acc[j][2] + off_a, kPUnscale, mp_a) * fa;
       }
       if (hb < G) {
-        red[(warp * kMaxGroup + hb) * kHeadDim + d0] = (acc[j][1] + mp_b) * fb;
-        red[(warp * kMaxGroup + hb) * kHeadDim + d0 + 1] = (acc[j][3] + mp_b) * fb;
+        red[(warp * kMaxGroup + hb) * kHeadDim + d0] = fmaf(acc[j][1] + off_b, kPUnscale, mp_b) * fb;
+        red[(warp * kMaxGroup + hb) * kHeadDim + d0 + 1] = fmaf(acc[j][3] + off_b, kPUnscale, mp_b) * fb;
       }
     }
   }
@@ -390,13 +438,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       num += red[(w * kMaxGroup + h) * kHeadDim + d];
     }
     if (single) {
-      const float o = L > 0.0f ? num / L : 0.0f;
-      const int64_t hq = int64_t(kvh) * G + h;
-      if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(o);
-      if (p.out_f32) p.out_f32[(b * (p.num_kv_heads * G) + hq) * kHeadDim + d] = o;
-      if (p.out_lse && d == 0) {
-        p.out_lse[b * (p.num_kv_heads * G) + hq] = L > 0.0f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
-      }
+      store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
     } else {
       my_rec[e] = num;
       if (d == 0) {
@@ -418,24 +460,56 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   if (!tail->is_last) return;
   __threadfence();
   const float* recs = p.partials + unit * p.max_splits * rec_floats;
-  for (int e = tid; e < outputs; e += kThreads) {
-    const int h = e / kHeadDim;
-    const int d = e - h * kHeadDim;
+  // stage every split's (M, L) in shared memory, then turn M into merge weights
+  float* wm = reinterpret_cast<float*>(codes);  // [nsplit_b][G]
+  float* wl = wm + nsplit_b * G;                // [nsplit_b][G]
+  float* head_m = wl + nsplit_b * G;            // [G]
+  float* head_l = head_m + kMaxGroup;           // [G]
+  for (int idx = tid; idx < nsplit_b * G; idx += kThreads) {
+    const int s = idx / G, h = idx - (idx / G) * G;
+    wm[idx] = __ldcg(recs + s * rec_floats + outputs + h);
+    wl[idx] = __ldcg(recs + s * rec_floats + outputs + G + h);
+  }
+  __syncthreads();
+  if (tid < G) {
     float M = -INFINITY;
-    for (int s = 0; s < nsplit_b; ++s) M = fmaxf(M, __ldcg(recs + s * rec_floats + outputs + h));
-    float L = 0.0f, num = 0.0f;
-    for (int s = 0; s < nsplit_b; ++s) {
-      const float ms = __ldcg(recs + s * rec_floats + outputs + h);
-      const float f = M == -INFINITY ? 0.0f : exp2f(ms - M);
-      L += __ldcg(recs + s * rec_floats + outputs + G + h) * f;
-      num += __ldcg(recs + s * rec_floats + e) * f;
+    for (int s = 0; s < nsplit_b; ++s) M = fmaxf(M, wm[s * G + tid]);
+    float L = 0.0f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < nsplit_b; ++s) L += wl[s * G + tid] * exp2f(wm[s * G + tid] - M);
     }
-    const float o = L > 0.0f ? num / L : 0.0f;
-    const int64_t hq = int64_t(kvh) * G + h;
-    if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(o);
-    if (p.out_f32) p.out_f32[(b * (p.num_kv_heads * G) + hq) * kHeadDim + d] = o;
-    if (p.out_lse && d == 0) {
-      p.out_lse[b * (p.num_kv_heads * G) + hq] = L > 0.0f ? (M + log2f(L)) * 0.69314718055994531f : -INFINITY;
+    head_m[tid] = M;
+    head_l[tid] = L;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < nsplit_b * G; idx += kThreads) {
+    const int h = idx - (idx / G) * G;
+    const float M = head_m[h];
+    wm[idx] = M == -INFINITY ? 0.0f : exp2f(wm[idx] - M);
+  }
+  __syncthreads();
+  constexpr int kMaxPer = kMaxGroup * kHeadDim / kThreads;  // 16 outputs per thread at most
+  const int per = outputs / kThreads;
+  float num[kMaxPer];
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) num[j] = 0.0f;
+  for (int s = 0; s < nsplit_b; ++s) {
+    const float* rec = recs + s * rec_floats;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      if (j < per) {
+        const int e = tid + j * kThreads;
+        num[j] = fmaf(wm[s * G + e / kHeadDim], __ldcg(rec + e), num[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    if (j < per) {
+      const int e = tid + j * kThreads;
+      const int h = e / kHeadDim;
+      const float L = head_l[h];
+      store_out<T>(p, b, int64_t(kvh) * G + h, e - h * kHeadDim, L > 0.0f ? num[j] / L : 0.0f, head_m[h], L);
     }
   }
   if (tid == 0) p.counters[unit] = 0;  // ready for the next launch
@@ -528,7 +602,8 @@ extern "C" int oq_decode_attn_int4_paged(
     const int64_t target = 148 * 6;
     splits = int(std::min<int64_t>(std::max<int64_t>(1, (target + units - 1) / units), max_pages_per_seq));
   }
-  splits = int(std::min<int64_t>(splits, max_pages_per_seq));
+  // the merging CTA stages (max, sum) of every split in 64 KB of shared memory
+  splits = int(std::min<int64_t>(std::min<int64_t>(splits, max_pages_per_seq), kMaxSplits));
   const int pps = int((max_pages_per_seq + splits - 1) / splits);
   splits = int((max_pages_per_seq + pps - 1) / pps);
 
