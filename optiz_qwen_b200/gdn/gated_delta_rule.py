@@ -1,0 +1,105 @@
+"""Gated DeltaNet hooks backed by the sm_100a kernels.
+
+Qwen3_5GatedDeltaNet calls its instance attributes ``recurrent_gated_delta_rule``
+(decode) and ``chunk_gated_delta_rule`` (prefill) as
+``f(q, k, v, g=g, beta=beta, initial_state=S | None, output_final_state=bool,
+use_qk_l2norm_in_kernel=True)`` (transformers models/qwen3_5/modeling_qwen3_5.py:499-520)
+and expects ``(o [B, T, H, Dv] in q's dtype, S_final [B, H, Dk, Dv] fp32 | None)``.
+The reference binds fla 0.5.1's Triton kernels there (or transformers' torch
+loops, :234-353); these functions take their place with fla's keyword
+signature.  The state stays fp32; q/k L2 normalisation is done in fp32 inside
+the kernel (as fla does).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import cabi
+
+
+def _check_unsupported(cu_seqlens, use_gate_in_kernel, kwargs):
+    if cu_seqlens is not None:
+        raise NotImplementedError("variable-length (cu_seqlens) inputs are not supported; pass [B, T, H, D] batches")
+    if use_gate_in_kernel:
+        raise NotImplementedError("use_gate_in_kernel is not supported; pass the log-space decay g")
+    if kwargs.get("transpose_state_layout"):
+        raise NotImplementedError("transpose_state_layout is not supported; the state layout is [B, H, Dk, Dv]")
+
+
+def _expand_value_heads(q, k, v):
+    """GVA (more value heads than q/k heads): repeat q/k heads on the device."""
+    h, hv = q.shape[2], v.shape[2]
+    if hv == h:
+        return q, k
+    if hv % h:
+        raise ValueError(f"value heads ({hv}) must be a multiple of q/k heads ({h})")
+    return q.repeat_interleave(hv // h, dim=2), k.repeat_interleave(hv // h, dim=2)
+
+
+def fused_recurrent_gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                     g: torch.Tensor | None = None, gk=None, gv=None,
+                                     beta: torch.Tensor | None = None, scale: float | None = None,
+                                     initial_state: torch.Tensor | None = None, output_final_state: bool = False,
+                                     use_qk_l2norm_in_kernel: bool = False, use_gate_in_kernel: bool = False,
+                                     A_log=None, dt_bias=None, cu_seqlens=None, **kwargs):
+    """Token-by-token gated delta rule (fla/ops/gated_delta_rule/fused_recurrent.py:291 signature)."""
+    _check_unsupported(cu_seqlens, use_gate_in_kernel, kwargs)
+    if gk is not None or gv is not None:
+        raise NotImplementedError("per-channel decays (gk / gv) are not supported")
+    q, k = _expand_value_heads(q, k, v)
+    if g is None:
+        g = torch.zeros(q.shape[:3], dtype=torch.float32, device=q.device)
+    if beta is None:
+        beta = torch.ones(q.shape[:3], dtype=q.dtype, device=q.device)
+    batch, _, heads, dk = q.shape
+    dv = v.shape[-1]
+    if initial_state is not None:
+        initial_state = initial_state.to(torch.float32).contiguous()
+    final = (torch.empty((batch, heads, dk, dv), dtype=torch.float32, device=q.device)
+             if output_final_state else None)
+    out = cabi.gdn_recurrent(q, k, v, g, beta, scale=scale, initial_state=initial_state, final_state=final,
+                             use_qk_l2norm=use_qk_l2norm_in_kernel)
+    return out, final
+
+
+def recurrent_gated_delta_rule(query, key, value, g, beta, initial_state=None, output_final_state=False,
+                               use_qk_l2norm_in_kernel=False, scale=None):
+    """Same operation with transformers' torch-fallback argument order
+    (``torch_recurrent_gated_delta_rule``, modeling_qwen3_5.py:314)."""
+    return fused_recurrent_gated_delta_rule(query, key, value, g=g, beta=beta, scale=scale,
+                                            initial_state=initial_state, output_final_state=output_final_state,
+                                            use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+
+
+def chunk_gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                           beta: torch.Tensor, scale: float | None = None,
+                           initial_state: torch.Tensor | None = None, output_final_state: bool = False,
+                           use_qk_l2norm_in_kernel: bool = False, cu_seqlens=None, chunk_size: int = 64,
+                           **kwargs):
+    """Prefill form (fla/ops/gated_delta_rule/chunk.py:365 signature).
+
+    The result equals the chunked WY formulation of
+    ``torch_chunk_gated_delta_rule`` (modeling_qwen3_5.py:234-311) to fp32
+    rounding: the recurrence is the same, run by the kernel with the state
+    held on-chip across all T tokens.
+    """
+    _check_unsupported(cu_seqlens, kwargs.pop("use_gate_in_kernel", False), kwargs)
+    return fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, scale=scale, initial_state=initial_state,
+                                            output_final_state=output_final_state,
+                                            use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+
+
+def install_gdn_fastpath(model) -> int:
+    """Bind the hooks on every Gated-DeltaNet module of ``model``; returns how many were patched.
+
+    This replaces the reference's PYTHONPATH overlay that makes fla importable
+    before transformers binds its fast path (scripts/run_v11_cuda_matrix.py:285-289).
+    """
+    patched = 0
+    for module in model.modules():
+        if "GatedDeltaNet" in type(module).__name__ and hasattr(module, "recurrent_gated_delta_rule"):
+            module.recurrent_gated_delta_rule = fused_recurrent_gated_delta_rule
+            module.chunk_gated_delta_rule = chunk_gated_delta_rule
+            patched += 1
+    return patched

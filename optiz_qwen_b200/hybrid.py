@@ -1,0 +1,271 @@
+"""One decode token through the Qwen3.5 hybrid stack's hot path, on one GPU.
+
+Per full-attention layer: fused append-quantize of the new token's K/V into the
+layer's paged INT4 pool, then split-KV INT4 decode attention of the query over
+it.  Per Gated-DeltaNet layer: the recurrent gated-delta-rule step on the
+layer's fp32 state, in place.  Layer order follows Qwen3.5's ``layer_types``
+(every ``full_attention_interval``-th layer is full attention,
+transformers models/qwen3_5/configuration_qwen3_5.py).  The projections and MLPs
+around these kernels are not part of this path.
+
+``HybridDecodeStack.step`` is the host-facing call: it copies the step's
+inputs from pinned host memory, runs the step (a captured CUDA graph of every
+kernel launch) and copies the outputs back.  ``step_device`` launches the same
+kernels on device-resident inputs.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import cabi
+from .compression.paged_kv import PageAllocator, PagedKvState
+
+
+@dataclass
+class HybridShape:
+    batch: int = 64
+    context: int | list[int] = 4096
+    num_layers: int = 24
+    full_attention_interval: int = 4
+    num_heads: int = 8
+    num_kv_heads: int = 2
+    head_dim: int = 256
+    gdn_heads: int = 16
+    gdn_dim: int = 128
+    page_size: int = 64
+
+    @property
+    def layer_types(self) -> list[str]:
+        k = self.full_attention_interval
+        return ["full_attention" if (i + 1) % k == 0 else "linear_attention" for i in range(self.num_layers)]
+
+    @property
+    def lengths(self) -> list[int]:
+        if isinstance(self.context, int):
+            return [self.context] * self.batch
+        return [int(x) for x in self.context]
+
+
+@dataclass
+class _AttnLayer:
+    paged: PagedKvState
+    write_pos: torch.Tensor      # int32 [B]: slot the new token is written to
+    attend_lens: torch.Tensor    # int32 [B]: tokens attended (includes the new one)
+    workspace: torch.Tensor
+    q: torch.Tensor = None
+    k: torch.Tensor = None
+    v: torch.Tensor = None
+    out: torch.Tensor = None
+
+
+@dataclass
+class _GdnLayer:
+    state: torch.Tensor
+    q: torch.Tensor = None
+    k: torch.Tensor = None
+    v: torch.Tensor = None
+    g: torch.Tensor = None
+    beta: torch.Tensor = None
+    out: torch.Tensor = None
+
+
+@dataclass
+class StepCounts:
+    launches: int
+    attn_bytes: int          # algorithmic KV bytes read per step (all attention layers)
+    gdn_bytes: int           # state bytes read + written per step (all GDN layers)
+    append_bytes: int
+    h2d_bytes: int
+    d2h_bytes: int
+    per_kernel: dict = field(default_factory=dict)
+
+
+class HybridDecodeStack:
+    """Device state of the hybrid stack for ``shape.batch`` sequences.
+
+    ``hold_context=True`` keeps every sequence at its configured context: each
+    step quantises the new token into slot ``context`` of its page and attends
+    over ``context + 1`` tokens, so repeated steps measure the same workload.
+    With ``hold_context=False`` the caches grow by one token per step.
+    """
+
+    KV_BYTES_PER_TOKEN_HEAD = 264  # 2 x 128 B codes + 4 x 2 B fp16 scale/min
+
+    def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
+                 hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.hold_context = hold_context
+        self.gen = torch.Generator(device=self.device)
+        self.gen.manual_seed(seed)
+        lengths = shape.lengths
+        b = shape.batch
+        self.attn: list[_AttnLayer] = []
+        self.gdn: list[_GdnLayer] = []
+        self.order: list[tuple[str, int]] = []
+        for kind in shape.layer_types:
+            if kind == "full_attention":
+                self.order.append(("attn", len(self.attn)))
+                self.attn.append(self._make_attn_layer(lengths, extra_tokens, page_seed))
+            else:
+                self.order.append(("gdn", len(self.gdn)))
+                state = torch.randn((b, shape.gdn_heads, shape.gdn_dim, shape.gdn_dim), generator=self.gen,
+                                    device=self.device, dtype=torch.float32).mul_(0.02)
+                self.gdn.append(_GdnLayer(state=state))
+        self._alloc_io()
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.stream = torch.cuda.Stream(self.device)
+
+    # ------------------------------------------------------------------ setup
+    def _make_attn_layer(self, lengths, extra_tokens, page_seed) -> _AttnLayer:
+        s = self.shape
+        need = [cabi.pages_for(n + 1 + extra_tokens, s.page_size) for n in lengths]
+        pool = cabi.PagedKvPool(sum(need), s.num_kv_heads, s.head_dim, s.page_size, self.device)
+        paged = PagedKvState(pool, s.batch, max_pages=max(need), allocator=PageAllocator(sum(need), page_seed))
+        paged.reserve([n + 1 + extra_tokens for n in lengths])
+        # populate each sequence's history with bf16 N(0,1) K/V, quantised by the append kernel itself;
+        # rows of equal length are appended together, in token chunks of bounded size
+        by_len: dict[int, list[int]] = {}
+        for r, n in enumerate(lengths):
+            by_len.setdefault(int(n), []).append(r)
+        for n, rows in sorted(by_len.items()):
+            idx = torch.tensor(rows, dtype=torch.long, device=self.device)
+            table = paged.block_table.index_select(0, idx).contiguous()
+            lens = torch.zeros(len(rows), dtype=torch.int32, device=self.device)
+            chunk = max(1, (1 << 26) // (len(rows) * s.num_kv_heads * s.head_dim))
+            for lo in range(0, n, chunk):
+                m = min(chunk, n - lo)
+                shp = (len(rows), s.num_kv_heads, m, s.head_dim)
+                k = torch.randn(shp, generator=self.gen, device=self.device, dtype=torch.float32).to(self.dtype)
+                v = torch.randn(shp, generator=self.gen, device=self.device, dtype=torch.float32).to(self.dtype)
+                cabi.append_quant_int4(k, v, pool, table, lens, advance=True)
+                del k, v
+            paged.seq_lens.index_copy_(0, idx, lens)
+        torch.cuda.synchronize(self.device)
+        paged.host_lens = list(lengths)
+        write_pos = torch.tensor(lengths, dtype=torch.int32, device=self.device)
+        attend = write_pos + 1
+        if not self.hold_context:
+            write_pos = paged.seq_lens
+            attend = paged.seq_lens
+        ws = cabi.new_decode_workspace(s.batch, s.num_heads, s.num_kv_heads, paged.max_pages, self.device)
+        return _AttnLayer(paged=paged, write_pos=write_pos, attend_lens=attend, workspace=ws)
+
+    def _alloc_io(self) -> None:
+        """One flat input buffer and one flat output buffer, viewed per layer."""
+        s = self.shape
+        b = s.batch
+        in_specs, out_specs = [], []
+        for kind, i in self.order:
+            if kind == "attn":
+                in_specs += [(("attn", i, "q"), (b, s.num_heads, s.head_dim)),
+                             (("attn", i, "k"), (b, s.num_kv_heads, 1, s.head_dim)),
+                             (("attn", i, "v"), (b, s.num_kv_heads, 1, s.head_dim))]
+                out_specs += [(("attn", i, "out"), (b, s.num_heads, s.head_dim))]
+            else:
+                shp = (b, 1, s.gdn_heads, s.gdn_dim)
+                in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp),
+                             (("gdn", i, "beta"), (b, 1, s.gdn_heads))]
+                out_specs += [(("gdn", i, "out"), shp)]
+        n_in = sum(math.prod(shp) for _, shp in in_specs)
+        n_out = sum(math.prod(shp) for _, shp in out_specs)
+        # g stays fp32 (the module computes it in fp32): a separate flat buffer
+        n_g = len(self.gdn) * b * s.gdn_heads
+        self.in_dev = torch.empty(n_in, dtype=self.dtype, device=self.device)
+        self.g_dev = torch.empty(n_g, dtype=torch.float32, device=self.device)
+        self.out_dev = torch.empty(n_out, dtype=self.dtype, device=self.device)
+        self.in_host = torch.empty(n_in, dtype=self.dtype, pin_memory=True)
+        self.g_host = torch.empty(n_g, dtype=torch.float32, pin_memory=True)
+        self.out_host = torch.empty(n_out, dtype=self.dtype, pin_memory=True)
+        off = 0
+        for (kind, i, name), shp in in_specs:
+            view = self.in_dev[off:off + math.prod(shp)].view(shp)
+            setattr((self.attn if kind == "attn" else self.gdn)[i], name, view)
+            off += math.prod(shp)
+        off = 0
+        for (kind, i, name), shp in out_specs:
+            view = self.out_dev[off:off + math.prod(shp)].view(shp)
+            setattr((self.attn if kind == "attn" else self.gdn)[i], name, view)
+            off += math.prod(shp)
+        for i, layer in enumerate(self.gdn):
+            layer.g = self.g_dev[i * b * s.gdn_heads:(i + 1) * b * s.gdn_heads].view(b, 1, s.gdn_heads)
+
+    def fill_inputs(self) -> None:
+        """Synthetic step inputs with the config-0 distributions (q/k/v bf16 N(0,1), beta = sigmoid(N),
+        g = -softplus(N)), written to the pinned host buffers and the device buffers."""
+        gen = torch.Generator().manual_seed(12345)
+        self.in_host.copy_(torch.randn(self.in_host.shape, generator=gen).to(self.dtype))
+        self.g_host.copy_(-torch.nn.functional.softplus(torch.randn(self.g_host.shape, generator=gen)))
+        self.in_dev.copy_(self.in_host)
+        self.g_dev.copy_(self.g_host)
+        for layer in self.gdn:
+            layer.beta.copy_(torch.sigmoid(layer.beta.float()).to(self.dtype))
+        self.in_host.copy_(self.in_dev)
+
+    # ------------------------------------------------------------------ the step
+    def step_device(self, kinds=("attn", "gdn", "append")) -> None:
+        s = self.shape
+        scaling = s.head_dim ** -0.5
+        for kind, i in self.order:
+            if kind == "attn":
+                layer = self.attn[i]
+                p = layer.paged
+                if "append" in kinds:
+                    cabi.append_quant_int4(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
+                                           advance=not self.hold_context)
+                if "attn" in kinds:
+                    cabi.decode_attention_int4(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
+                                               out=layer.out, workspace=layer.workspace)
+            elif "gdn" in kinds:
+                layer = self.gdn[i]
+                cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
+                                   final_state=layer.state, out=layer.out, use_qk_l2norm=True)
+
+    def capture(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
+        """Capture one step's launches in a CUDA graph (after one eager warm-up step)."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            self.step_device(kinds)
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            self.step_device(kinds)
+        return graph
+
+    def step(self) -> torch.Tensor:
+        """Host-facing step: pinned inputs -> device, graph replay, outputs -> pinned host buffer."""
+        if self.graph is None:
+            self.graph = self.capture()
+        cur = torch.cuda.current_stream(self.device)
+        self.in_dev.copy_(self.in_host, non_blocking=True)
+        self.g_dev.copy_(self.g_host, non_blocking=True)
+        self.graph.replay()
+        self.out_host.copy_(self.out_dev, non_blocking=True)
+        return self.out_host
+
+    # ------------------------------------------------------------------ accounting
+    def counts(self) -> StepCounts:
+        s = self.shape
+        lengths = np.array(s.lengths)
+        attend = lengths + 1 if self.hold_context else lengths
+        attn_bytes_layer = int(attend.sum()) * s.num_kv_heads * self.KV_BYTES_PER_TOKEN_HEAD
+        gdn_bytes_layer = 2 * s.batch * s.gdn_heads * s.gdn_dim * s.gdn_dim * 4
+        append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.KV_BYTES_PER_TOKEN_HEAD)
+        n_attn, n_gdn = len(self.attn), len(self.gdn)
+        esize = self.in_dev.element_size()
+        return StepCounts(
+            launches=2 * n_attn + n_gdn,
+            attn_bytes=attn_bytes_layer * n_attn,
+            gdn_bytes=gdn_bytes_layer * n_gdn,
+            append_bytes=append_bytes_layer * n_attn,
+            h2d_bytes=self.in_dev.numel() * esize + self.g_dev.numel() * 4,
+            d2h_bytes=self.out_dev.numel() * esize,
+            per_kernel={"decode_attn_int4_paged": attn_bytes_layer, "gdn_recurrent": gdn_bytes_layer,
+                        "append_quant_int4": append_bytes_layer},
+        )

@@ -1,0 +1,58 @@
+"""INT4 paged-KV decode attention launchers (drop-in for optiz_qwen/kernels/qserve_int4_attention.py).
+
+Signatures, return shapes and error behaviour follow the reference launchers
+(:516-660): ``fn(query [B, Hq, 1, D] CUDA, layer, *, scaling) -> [B, 1, Hq, D]``
+in the query dtype; ``RuntimeError`` when the query is not a one-token CUDA
+tensor or the layer holds no packed KV; ``ValueError`` on a non-integer GQA
+ratio.  Both launchers run the same sm_100a kernel (C ABI
+``oq_decode_attn_int4_paged``): the one-pass backend gives each (sequence, KV
+head) a single CTA, the split backend cuts the KV range over CTAs and merges
+the partials by log-sum-exp in the same launch.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+
+from .. import _lib, cabi
+
+
+def triton_int4_decode_available(query: torch.Tensor) -> bool:
+    """Reference name kept for the fused-forward dispatch: a one-token CUDA query and a built library."""
+    return bool(query.is_cuda and query.shape[-2] == 1 and _lib.available())
+
+
+int4_decode_available = triton_int4_decode_available
+
+
+def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: int, what: str) -> torch.Tensor:
+    if not (query.is_cuda and query.shape[-2] == 1):
+        raise RuntimeError(f"{what} requires a CUDA query with sequence length 1.")
+    paged = getattr(layer, "paged", None)
+    if paged is None or getattr(layer, "_key_code", None) is None:
+        raise RuntimeError("Fused qserve attention requires packed KV tensors.")
+    batch, num_heads, _, head_dim = query.shape
+    num_kv_heads = paged.pool.num_kv_heads
+    if num_heads % num_kv_heads:
+        raise ValueError("Qwen GQA decode requires an integer query-to-KV head ratio.")
+    q = query[:, :, 0, :]
+    out = cabi.decode_attention_int4(q, paged.pool, paged.block_table, paged.seq_lens, scaling,
+                                     workspace=layer.decode_workspace(num_heads), num_splits=num_splits)
+    return out.unsqueeze(1)
+
+
+def qserve_int4_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
+    """Attend to the packed cache with one KV range per (sequence, KV head)."""
+    return _paged_decode(query, layer, scaling, 1, "INT4 decode attention")
+
+
+def qserve_int4_split_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
+    """Split-KV decode: KV ranges spread over the SMs, partials merged by log-sum-exp in-launch."""
+    return _paged_decode(query, layer, scaling, 0, "INT4 split decode")
+
+
+def qserve_int8_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
+    """The 8-bit KV backend is not built on this path yet (the layer rejects k_bits=8)."""
+    raise NotImplementedError("INT8 paged decode attention is not implemented on this build.")
