@@ -120,6 +120,30 @@ int oq_decode_attn_int4_paged(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream);
 
+/* Same attention, for callers that cannot allocate device memory (no counterpart
+ * in the reference, which only runs inside PyTorch's allocator).  A decode loop
+ * embedded in a host runtime whose arena owns all device memory, or a
+ * foreign-language caller holding only buffers allocated by someone else, has
+ * no way to provide the workspace above.  This variant takes its split-KV
+ * scratch from a fixed 8 MiB array compiled into the library (held on every
+ * GPU that loads it until exit) and calls no allocator.  The caller still
+ * passes inputs and outputs.  An explicit num_splits whose scratch exceeds
+ * 8 MiB is rejected with OQ_ERR_WORKSPACE; num_splits <= 0 picks the usual
+ * split count capped to fit.  All calls share the array: its merge counters are
+ * cleared on `stream` at the start of each call, and calls that overlap on the
+ * GPU race.  The first call on a device looks up the array's address with that
+ * device current; make it before any stream capture. */
+int oq_decode_attn_int4_paged_noalloc(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    int num_splits, int32_t* device_status, void* stream);
+
 /* ------------------------------------------------------------------ log-sum-exp merge
  * Combines attention partials computed over disjoint KV ranges (another GPU's
  * slice of a long context, gathered over NVLink):
