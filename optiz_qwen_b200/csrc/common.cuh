@@ -80,6 +80,15 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D = A(16x32 u8, row) * B(32x8 s8, col) + D, exact int32 accumulate.
+__device__ __forceinline__ void imma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // Transpose of an 8x8 b16 matrix held in the mma fragment layout
 // (lane = 4*row + col/2 holds elements (row, col), (row, col+1)).
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {

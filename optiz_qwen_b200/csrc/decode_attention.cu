@@ -11,9 +11,10 @@
 //     shared memory by one TMA tensor copy (128-byte swizzle) and one bulk copy,
 //     four pages in flight per CTA, completion tracked by mbarriers with
 //     bounded waits;
-//   * nibbles are turned into bf16/fp16 in registers (lop3 with an exponent
-//     bias, then an exact subtract) and both q.k and p.v run on the tensor
-//     cores (mma.sync m16n8k16, the GQA heads as the N=8 dimension);
+//   * q.k runs on the integer tensor cores: q is per-head 15-bit fixed point split
+//     into two s8 digits, the codes are u8 (nibbles masked in place, no shifts),
+//     mma.sync m16n8k32 gives exact int32 dot products; p.v runs on fp16 tensor
+//     cores with the nibbles dropped into the mantissa of 1024.0 (lop3);
 //     scale/min are applied after the dot products:
 //       q.k = scale * sum(q*code) + min * sum(q),  p.v = sum((p*scale)*code) + sum(p*min);
 //   * the KV range is split across CTAs and the partial (max, sum, acc) are
@@ -73,36 +74,30 @@ struct __align__(16) SmemTail {
 constexpr size_t kSmemBytes =
     1024 /*alignment slack*/ + kStages * (kStageCodeBytes + kStageMetaBytes) + sizeof(SmemTail);
 
-// Nibble -> 16-bit float conversion.  lop3 puts codes c0 (bits 0-3) and c4
-// (bits 16-19) of a word into the mantissa of an exponent-biased constant, giving
-// (bias + c) exactly; callers either fold the bias into the epilogue or subtract it.
-template <typename T> struct QkTraits;
-template <> struct QkTraits<__nv_bfloat16> {
-  // q.k runs on bf16 operands: codes become 128 + c; the 128 * sum(q) term is
-  // removed in the score epilogue.
-  static constexpr float kBias = 128.0f;
-  static __device__ __forceinline__ uint32_t codes(uint32_t x) { return lop3_and_or(x, 0x000F000Fu, 0x43004300u); }
-  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    mma_bf16_16816(d, a, b0, b1);
-  }
-};
-template <> struct QkTraits<__half> {
-  // fp16 queries: exact codes (1024 + c) - 1024.
-  static constexpr float kBias = 0.0f;
-  static __device__ __forceinline__ uint32_t codes(uint32_t x) {
-    uint32_t v = lop3_and_or(x, 0x000F000Fu, 0x64006400u);
-    __half2 h = *reinterpret_cast<__half2*>(&v);
-    __half2 r = __hsub2(h, __floats2half2_rn(1024.0f, 1024.0f));
-    return *reinterpret_cast<uint32_t*>(&r);
-  }
-  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    mma_f16_16816(d, a, b0, b1);
-  }
-};
+// ---- q.k on integer tensor cores.
+// Each query head is turned into 15-bit fixed point, q ~ q_int * 2^-e_h with
+// |q_int| <= 16383, split into two signed 8-bit digits q_int = 128 * hi + lo
+// (lo in [0, 127]).  mma.sync m16n8k32 u8 x s8 -> s32 then gives exact integer
+// dot products of the codes with each digit.  With at most 4 query heads per
+// KV head the 8 MMA columns hold (hi digits of heads 0-3, lo digits of heads
+// 0-3), so one MMA per 32 dims covers every head ("packed"); with 5-8 heads hi
+// and lo digits take one MMA each ("dual").
+//
+// Code unpacking needs no shifts: w & 0x0F0F0F0F gives the even dims' codes as
+// bytes, w & 0xF0F0F0F0 the odd dims' codes times 16; the two are accumulated
+// in separate MMA chains and the second is divided by 16 (exactly) at the end.
+constexpr uint32_t kLowNibbles = 0x0F0F0F0Fu;
+constexpr uint32_t kHighNibbles = 0xF0F0F0F0u;
+constexpr int kQMax = 16383;
 
-// p.v runs on fp16 operands: codes become 1024 + c, removed with 1024 * sum(P').
+// ---- p.v on fp16 tensor cores.  prmt pairs byte b of two tokens' words into
+// the two 16-bit lanes; lop3 then drops a nibble into the mantissa of fp16
+// 1024.0: mask 0x000F000F gives 1024 + c (even dim), mask 0x00F000F0 gives
+// 1024 + 16 c (odd dim).  The 1024 * sum(P') bias and the factor 16 of the odd
+// dims are removed in the epilogue.
 constexpr float kVBias = 1024.0f;
-__device__ __forceinline__ uint32_t v_codes(uint32_t x) { return lop3_and_or(x, 0x000F000Fu, 0x64006400u); }
+constexpr uint32_t kFp16Bias = 0x64006400u;
+__device__ __forceinline__ uint32_t byte_pair_sel(int b) { return uint32_t(b) | (uint32_t(4 + b) << 8); }
 
 // Lazy softmax rescale: the running max only moves when a tile's max exceeds it
 // by more than kTau (log2 units), so p <= 2^kTau; P' = p * v_scale * 2^-kTau
@@ -110,6 +105,11 @@ __device__ __forceinline__ uint32_t v_codes(uint32_t x) { return lop3_and_or(x, 
 constexpr float kTau = 4.0f;
 constexpr float kPScale = 0.0625f;  // 2^-kTau
 constexpr float kPUnscale = 16.0f;
+
+// Cross-warp reduction buffer: row (warp, head) of 256 dims, padded so that the
+// 32 lanes' stores of one MMA tile fall in 32 different banks.
+constexpr int kRedStride = 268;
+__device__ __forceinline__ int red_index(int w, int h, int d) { return (w * kMaxGroup + h) * kRedStride + d + (d >> 5); }
 
 // Shared-memory address of 16-byte chunk `chunk` of row `row` in a 128B-swizzled stage.
 __device__ __forceinline__ const uint4* swz(const uint8_t* base, int row, int chunk) {
@@ -129,6 +129,11 @@ __device__ __forceinline__ float lse_nat(float m_log2, float l) {
   return l > 0.0f ? (m_log2 + log2f(l)) * 0.69314718055994531f : -INFINITY;
 }
 
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
+         ((uint32_t(d) & 0xFFu) << 24);
+}
+
 template <typename T>
 __device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
                                           float l) {
@@ -138,7 +143,7 @@ __device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_
   if (p.out_lse && d == 0) p.out_lse[b * hq_total + hq] = lse_nat(m, l);
 }
 
-template <typename T>
+template <typename T, bool kDual>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -192,30 +197,81 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     for (; issued < min(n, kStages); ++issued) issue(issued, issued);
   }
 
-  // ---- query fragments (B operand of q.k): head r, dims 64c + 8i + {0..7}
-  using Q = QkTraits<T>;
-  uint32_t qb[16][2];
-  float qsum = 0.0f;
+  // ---- query digits (B operand of q.k).  This lane feeds MMA column r: head
+  // (packed) r & 3, digit hi for r < 4 and lo for r >= 4; (dual) head r, both
+  // digits.  Lane c supplies dims 64c .. 64c+63; step s covers dims
+  // 64c + 16s + {0..15}: the even dims in the "low nibble" MMA, the odd dims in
+  // the "high nibble" MMA.
+  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
+  uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
+  float qsum, qscale;
   {
-    const bool has = r < G;
-    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? r : 0)) * p.q_sh + 64 * c;
+    const int head = kDual ? r : (r & 3);
+    const bool has = head < G;
+    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? head : 0)) * p.q_sh + 64 * c;
+    float qf[64];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      uint4 w = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
-      qb[2 * i][0] = prmt(w.x, w.z, 0x5410);
-      qb[2 * i][1] = prmt(w.x, w.z, 0x7632);
-      qb[2 * i + 1][0] = prmt(w.y, w.w, 0x5410);
-      qb[2 * i + 1][1] = prmt(w.y, w.w, 0x7632);
+      const uint4 w = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
       const T* e = reinterpret_cast<const T*>(&w);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) qsum += to_float<T>(e[j]);
+      for (int j = 0; j < 8; ++j) qf[8 * i + j] = to_float<T>(e[j]);
     }
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+    float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      amax = fmaxf(amax, fabsf(qf[j]));
+      sum += qf[j];
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    int ex = 0;
+    if (amax > 0.0f) {
+      frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
+      ex -= 1;                                            // 2^ex <= kQMax / amax
+    }
+    const float up = ldexpf(1.0f, ex);
+    qscale = ldexpf(1.0f, -ex);
+    qsum = sum;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {      // word 2s (b0) and word 2s+1 (b1) of the step
+        int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int de = 16 * s + 8 * half + 2 * j;  // even dim (low nibble), odd dim = de + 1
+          const int qe = max(-kQMax, min(kQMax, __float2int_rn(qf[de] * up)));
+          const int qo = max(-kQMax, min(kQMax, __float2int_rn(qf[de + 1] * up)));
+          hi_e[j] = qe >> 7;
+          lo_e[j] = qe - 128 * hi_e[j];
+          hi_o[j] = qo >> 7;
+          lo_o[j] = qo - 128 * hi_o[j];
+        }
+        if (kDual) {
+          bq_lo[0][s][half] = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
+          bq_hi[0][s][half] = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
+          bq_lo[kSets - 1][s][half] = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
+          bq_hi[kSets - 1][s][half] = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+        } else {
+          const bool hi_digit = r < 4;
+          bq_lo[0][s][half] = hi_digit ? pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3])
+                                       : pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
+          bq_hi[0][s][half] = hi_digit ? pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3])
+                                       : pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+        }
+      }
+    }
   }
-  // sum(q) of the two heads (2c, 2c+1) whose scores this lane holds
+  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds (lane 4h carries head h)
   const float qs_a = __shfl_sync(0xffffffffu, qsum, (2 * c) * 4);
   const float qs_b = __shfl_sync(0xffffffffu, qsum, (2 * c + 1) * 4);
+  const float qx_a = __shfl_sync(0xffffffffu, qscale, (2 * c) * 4);
+  const float qx_b = __shfl_sync(0xffffffffu, qscale, (2 * c + 1) * 4);
+  const bool ha_ok = (kDual || c < 2) && 2 * c < G;
+  const bool hb_ok = (kDual || c < 2) && 2 * c + 1 < G;
 
   float acc[16][4];
 #pragma unroll
@@ -244,39 +300,60 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       const uint4 va = *swz(st, tb + 2 * c, r), vb = *swz(st, tb + 2 * c + 1, r);
       const uint4 vc = *swz(st, tb + 2 * c + 8, r), vd = *swz(st, tb + 2 * c + 9, r);
 
-      // ---------------- scores: A = K codes (16 tokens x 16 dims), B = q (16 dims x 8 heads);
-      // two independent accumulator chains
-      float sc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // ---------------- integer q.k: A = K codes (16 tokens x 32 dims, u8), B = q digits (s8)
+      int dot_a0, dot_b0, dot_a1, dot_b1;  // (token r, head 2c), (r, 2c+1), (r+8, 2c), (r+8, 2c+1)
       {
         const uint32_t w0[8] = {k00.x, k00.y, k00.z, k00.w, k01.x, k01.y, k01.z, k01.w};
         const uint32_t w1[8] = {k10.x, k10.y, k10.z, k10.w, k11.x, k11.y, k11.z, k11.w};
+        int lo[kSets][4], hi[kSets][4];
 #pragma unroll
-        for (int wi = 0; wi < 8; ++wi) {
-          float(&sc)[4] = (wi & 1) ? sc1 : sc0;
-          uint32_t a[4];
-          a[0] = Q::codes(w0[wi]);
-          a[1] = Q::codes(w1[wi]);
-          a[2] = Q::codes(w0[wi] >> 4);
-          a[3] = Q::codes(w1[wi] >> 4);
-          Q::mma(sc, a, qb[2 * wi][0], qb[2 * wi][1]);
-          a[0] = Q::codes(w0[wi] >> 8);
-          a[1] = Q::codes(w1[wi] >> 8);
-          a[2] = Q::codes(w0[wi] >> 12);
-          a[3] = Q::codes(w1[wi] >> 12);
-          Q::mma(sc, a, qb[2 * wi + 1][0], qb[2 * wi + 1][1]);
+        for (int k = 0; k < kSets; ++k) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) lo[k][j] = hi[k][j] = 0;
         }
+#pragma unroll
+        for (int st4 = 0; st4 < 4; ++st4) {
+          const uint32_t al[4] = {w0[2 * st4] & kLowNibbles, w1[2 * st4] & kLowNibbles,
+                                  w0[2 * st4 + 1] & kLowNibbles, w1[2 * st4 + 1] & kLowNibbles};
+          const uint32_t ah[4] = {w0[2 * st4] & kHighNibbles, w1[2 * st4] & kHighNibbles,
+                                  w0[2 * st4 + 1] & kHighNibbles, w1[2 * st4 + 1] & kHighNibbles};
+#pragma unroll
+          for (int k = 0; k < kSets; ++k) {
+            imma_u8s8_16832(lo[k], al, bq_lo[k][st4][0], bq_lo[k][st4][1]);
+            imma_u8s8_16832(hi[k], ah, bq_hi[k][st4][0], bq_hi[k][st4][1]);
+          }
+        }
+        int tot[kSets][4];
+#pragma unroll
+        for (int k = 0; k < kSets; ++k) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tot[k][j] = lo[k][j] + (hi[k][j] >> 4);
+        }
+        int dot[4];
+        if (kDual) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + tot[kSets - 1][j];
+        } else {
+          // columns 2c, 2c+1 of lanes c < 2 hold hi digits; lane c + 2 holds the same heads' lo digits
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
+        }
+        dot_a0 = dot[0];
+        dot_b0 = dot[1];
+        dot_a1 = dot[2];
+        dot_b1 = dot[3];
       }
       const bool v0 = tok0 < page_tokens, v1 = tok1 < page_tokens;
       const float ks0 = __half2float(meta[tok0]), km0 = __half2float(meta[kPage + tok0]);
       const float ks1 = __half2float(meta[tok1]), km1 = __half2float(meta[kPage + tok1]);
       const float vs0 = __half2float(meta[2 * kPage + tok0]), vm0 = __half2float(meta[3 * kPage + tok0]);
       const float vs1 = __half2float(meta[2 * kPage + tok1]), vm1 = __half2float(meta[3 * kPage + tok1]);
-      // q.k = scale * sum(q * (bias + c)) + (min - bias * scale) * sum(q)
-      const float kb0 = fmaf(-Q::kBias, ks0, km0), kb1 = fmaf(-Q::kBias, ks1, km1);
-      const float s0a = v0 ? fmaf(ks0, sc0[0] + sc1[0], kb0 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s0b = v0 ? fmaf(ks0, sc0[1] + sc1[1], kb0 * qs_b) * p.scale_log2 : -INFINITY;
-      const float s1a = v1 ? fmaf(ks1, sc0[2] + sc1[2], kb1 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s1b = v1 ? fmaf(ks1, sc0[3] + sc1[3], kb1 * qs_b) * p.scale_log2 : -INFINITY;
+      // q.k = scale * 2^-e * sum(code * q_int) + min * sum(q), in log2 units
+      const bool ok0a = v0 && ha_ok, ok0b = v0 && hb_ok, ok1a = v1 && ha_ok, ok1b = v1 && hb_ok;
+      const float s0a = ok0a ? fmaf(ks0 * qx_a, float(dot_a0), km0 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s0b = ok0b ? fmaf(ks0 * qx_b, float(dot_b0), km0 * qs_b) * p.scale_log2 : -INFINITY;
+      const float s1a = ok1a ? fmaf(ks1 * qx_a, float(dot_a1), km1 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s1b = ok1b ? fmaf(ks1 * qx_b, float(dot_b1), km1 * qs_b) * p.scale_log2 : -INFINITY;
 
       // ---------------- online softmax with a lazily moved reference max
       float tm_a = fmaxf(s0a, s1a), tm_b = fmaxf(s0b, s1b);
@@ -305,8 +382,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
           acc[j][3] *= corr_b;
         }
       }
-      const float p0a = v0 ? exp2f(s0a - m_a) : 0.0f, p0b = v0 ? exp2f(s0b - m_b) : 0.0f;
-      const float p1a = v1 ? exp2f(s1a - m_a) : 0.0f, p1b = v1 ? exp2f(s1b - m_b) : 0.0f;
+      const float p0a = ok0a ? exp2f(s0a - m_a) : 0.0f, p0b = ok0b ? exp2f(s0b - m_b) : 0.0f;
+      const float p1a = ok1a ? exp2f(s1a - m_a) : 0.0f, p1b = ok1b ? exp2f(s1b - m_b) : 0.0f;
       l_a += p0a + p1a;
       l_b += p0b + p1b;
       mp_a += (v0 ? p0a * vm0 : 0.0f) + (v1 ? p1a * vm1 : 0.0f);
@@ -331,19 +408,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w}, wd[4] = {vd.x, vd.y, vd.z, vd.w};
 #pragma unroll
         for (int wi = 0; wi < 4; ++wi) {
-          const uint32_t x_lo = prmt(wa[wi], wb[wi], 0x5410), x_hi = prmt(wa[wi], wb[wi], 0x7632);
-          const uint32_t y_lo = prmt(wc[wi], wd[wi], 0x5410), y_hi = prmt(wc[wi], wd[wi], 0x7632);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t x = u < 2 ? x_lo : x_hi;
-            const uint32_t y = u < 2 ? y_lo : y_hi;
-            const int sh = (u & 1) * 8;
+          for (int bs = 0; bs < 4; ++bs) {
+            const uint32_t x = prmt(wa[wi], wb[wi], byte_pair_sel(bs));  // tokens 2c, 2c+1: dims 2bs, 2bs+1
+            const uint32_t y = prmt(wc[wi], wd[wi], byte_pair_sel(bs));  // tokens 2c+8, 2c+9
             uint32_t a[4];
-            a[0] = v_codes(x >> sh);
-            a[1] = v_codes(x >> (sh + 4));
-            a[2] = v_codes(y >> sh);
-            a[3] = v_codes(y >> (sh + 4));
-            mma_f16_16816(acc[4 * wi + u], a, pb0, pb1);
+            a[0] = lop3_and_or(x, 0x000F000Fu, kFp16Bias);  // row r: even dim, 1024 + c
+            a[1] = lop3_and_or(x, 0x00F000F0u, kFp16Bias);  // row r+8: odd dim, 1024 + 16 c
+            a[2] = lop3_and_or(y, 0x000F000Fu, kFp16Bias);
+            a[3] = lop3_and_or(y, 0x00F000F0u, kFp16Bias);
+            mma_f16_16816(acc[4 * wi + bs], a, pb0, pb1);
           }
         }
       }
@@ -388,9 +462,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();  // also: every stage has been consumed, codes[] is free for reuse
 
-  // ---- merge the 4 warps: red[w][h][d] = numerator_w * 2^(m_w - M),
-  //      numerator = 2^kTau * (acc - 1024 * sum(P')) + sum(p * v_min)
-  float* red = reinterpret_cast<float*>(codes);  // kWarps * kMaxGroup * 256 floats = 32 KB
+  // ---- merge the 4 warps: red[w][h][d] = numerator_w * 2^(m_w - M), with
+  //      numerator = 2^kTau * (acc - 1024 sum(P')) / (1 or 16) + sum(p * v_min)
+  float* red = reinterpret_cast<float*>(codes);  // kWarps * kMaxGroup rows of kRedStride floats
   {
     const int ha = 2 * c, hb = 2 * c + 1;
     float fa = 0.0f, fb = 0.0f;
@@ -407,14 +481,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     const float off_a = -kVBias * sp_a, off_b = -kVBias * sp_b;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const int d0 = 32 * r + 2 * j;
+      const int d0 = 32 * r + 2 * j;  // row r: even dim d0 (weight 1); row r+8: odd dim d0+1 (weight 16)
       if (ha < G) {
-        red[(warp * kMaxGroup + ha) * kHeadDim + d0] = fmaf(acc[j][0] + off_a, kPUnscale, mp_a) * fa;
-        red[(warp * kMaxGroup + ha) * kHeadDim + d0 + 1] = fmaf(acc[j][2] + off_a, kPUnscale, mp_a) * fa;
+        red[red_index(warp, ha, d0)] = fmaf(acc[j][0] + off_a, kPUnscale, mp_a) * fa;
+        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2] + off_a, kPUnscale / 16.0f, mp_a) * fa;
       }
       if (hb < G) {
-        red[(warp * kMaxGroup + hb) * kHeadDim + d0] = fmaf(acc[j][1] + off_b, kPUnscale, mp_b) * fb;
-        red[(warp * kMaxGroup + hb) * kHeadDim + d0 + 1] = fmaf(acc[j][3] + off_b, kPUnscale, mp_b) * fb;
+        red[red_index(warp, hb, d0)] = fmaf(acc[j][1] + off_b, kPUnscale, mp_b) * fb;
+        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3] + off_b, kPUnscale / 16.0f, mp_b) * fb;
       }
     }
   }
@@ -435,7 +509,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     for (int w = 0; w < kWarps; ++w) {
       const float f = M == -INFINITY ? 0.0f : exp2f(tail->warp_m[w][h] - M);
       L += tail->warp_l[w][h] * f;
-      num += red[(w * kMaxGroup + h) * kHeadDim + d];
+      num += red[red_index(w, h, d)];
     }
     if (single) {
       store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
@@ -649,13 +723,16 @@ extern "C" int oq_decode_attn_int4_paged(
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+    kernel<<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
+  };
   if (dtype == OQ_BF16) {
-    cudaFuncSetAttribute(decode_attn_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int(kSmemBytes));
-    decode_attn_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
+    if (group > 4) launch(decode_attn_kernel<__nv_bfloat16, true>);
+    else launch(decode_attn_kernel<__nv_bfloat16, false>);
   } else {
-    cudaFuncSetAttribute(decode_attn_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    decode_attn_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
+    if (group > 4) launch(decode_attn_kernel<__half, true>);
+    else launch(decode_attn_kernel<__half, false>);
   }
   return check_launch("decode_attn_int4_paged");
 }
