@@ -93,11 +93,11 @@ def advance_seq_lens(seq_lens: torch.Tensor, delta: int = 1) -> None:
     call("oq_advance_seq_lens", ptr(seq_lens), seq_lens.shape[0], int(delta), stream_ptr(seq_lens.device))
 
 
-def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int = 148) -> int:
-    """Split count used when ``num_splits <= 0`` (kept in sync with the C side)."""
+def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int = 148, ctas_per_sm: int = 3) -> int:
+    """Split count used when ``num_splits <= 0``: enough KV ranges per (sequence, KV head) to
+    fill one wave of resident CTAs (the C side reads SM count and occupancy from the device)."""
     units = batch * num_kv_heads
-    target = sm_count * 6
-    splits = min(max(1, -(-target // units)), max_pages, 512)
+    splits = min(max(1, (sm_count * ctas_per_sm) // units), max_pages, 512)
     pps = -(-max_pages // splits)
     return -(-max_pages // pps)
 

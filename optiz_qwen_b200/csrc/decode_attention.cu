@@ -40,7 +40,6 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 8;
 constexpr int kMaxSplits = 512;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz: a copy that has not landed by then never will
 
 struct AttnParams {
   const void* query;
@@ -64,10 +63,17 @@ struct AttnParams {
 };
 
 struct __align__(16) SmemTail {
+  uint32_t qfrag[4][32][8];  // per k-step, per lane: B-operand digit fragments (built once per CTA)
   uint64_t full[kStages];
   int stage_ok[kStages];
+  int q_exp[kMaxGroup];      // per head: q ~ q_int * 2^-q_exp
+  float q_scale[kMaxGroup];  // 2^-q_exp
+  float q_sum[kMaxGroup];    // sum(q) (exact fp32)
   float warp_m[kWarps][kMaxGroup];
   float warp_l[kWarps][kMaxGroup];
+  float warp_f[kWarps][kMaxGroup];  // 2^(m_w - M) merge factor of each warp
+  float head_m[kMaxGroup];
+  float head_l[kMaxGroup];
   int is_last;
 };
 
@@ -116,13 +122,15 @@ __device__ __forceinline__ const uint4* swz(const uint8_t* base, int row, int ch
   return reinterpret_cast<const uint4*>(base + row * kRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
+// Bounded wait for a stage: the thread sleeps in try_wait (up to 20 us per poll) and
+// gives up after kWaitPolls polls (~2 s): a copy that has not landed by then never will.
+constexpr uint32_t kWaitHintNs = 20000;
+constexpr int kWaitPolls = 100000;
 __device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
+  for (int i = 0; i < kWaitPolls; ++i) {
+    if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
   }
-  return true;
+  return false;
 }
 
 __device__ __forceinline__ float lse_nat(float m_log2, float l) {
@@ -199,77 +207,103 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 
   // ---- query digits (B operand of q.k).  This lane feeds MMA column r: head
   // (packed) r & 3, digit hi for r < 4 and lo for r >= 4; (dual) head r, both
-  // digits.  Lane c supplies dims 64c .. 64c+63; step s covers dims
+  // digits.  Lane c supplies dims 64c .. 64c+63; k-step s covers dims
   // 64c + 16s + {0..15}: the even dims in the "low nibble" MMA, the odd dims in
-  // the "high nibble" MMA.
+  // the "high nibble" MMA.  Built once per CTA: warp 0 finds each head's
+  // fixed-point exponent, then warp w builds k-step w for all 32 lanes.
   constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
-  uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
-  float qsum, qscale;
-  {
-    const int head = kDual ? r : (r & 3);
-    const bool has = head < G;
-    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? head : 0)) * p.q_sh + 64 * c;
-    float qf[64];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 w = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
-      const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) qf[8 * i + j] = to_float<T>(e[j]);
-    }
+  if (warp == 0) {
+    const int head = lane >> 2, part = lane & 3;
     float amax = 0.0f, sum = 0.0f;
+    if (head < G) {
+      const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + head) * p.q_sh + 64 * part;
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      amax = fmaxf(amax, fabsf(qf[j]));
-      sum += qf[j];
+      for (int i = 0; i < 8; ++i) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i));
+        const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float v = to_float<T>(e[j]);
+          amax = fmaxf(amax, fabsf(v));
+          sum += v;
+        }
+      }
     }
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    int ex = 0;
-    if (amax > 0.0f) {
-      frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
-      ex -= 1;                                            // 2^ex <= kQMax / amax
-    }
-    const float up = ldexpf(1.0f, ex);
-    qscale = ldexpf(1.0f, -ex);
-    qsum = sum;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {      // word 2s (b0) and word 2s+1 (b1) of the step
-        int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int de = 16 * s + 8 * half + 2 * j;  // even dim (low nibble), odd dim = de + 1
-          const int qe = max(-kQMax, min(kQMax, __float2int_rn(qf[de] * up)));
-          const int qo = max(-kQMax, min(kQMax, __float2int_rn(qf[de + 1] * up)));
-          hi_e[j] = qe >> 7;
-          lo_e[j] = qe - 128 * hi_e[j];
-          hi_o[j] = qo >> 7;
-          lo_o[j] = qo - 128 * hi_o[j];
-        }
-        if (kDual) {
-          bq_lo[0][s][half] = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
-          bq_hi[0][s][half] = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
-          bq_lo[kSets - 1][s][half] = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
-          bq_hi[kSets - 1][s][half] = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
-        } else {
-          const bool hi_digit = r < 4;
-          bq_lo[0][s][half] = hi_digit ? pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3])
-                                       : pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
-          bq_hi[0][s][half] = hi_digit ? pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3])
-                                       : pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
-        }
+    if (part == 0) {
+      int ex = 0;
+      if (amax > 0.0f) {
+        frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
+        ex -= 1;                                            // 2^ex <= kQMax / amax
       }
+      tail->q_exp[head] = ex;
+      tail->q_scale[head] = ldexpf(1.0f, -ex);
+      tail->q_sum[head] = sum;
     }
   }
-  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds (lane 4h carries head h)
-  const float qs_a = __shfl_sync(0xffffffffu, qsum, (2 * c) * 4);
-  const float qs_b = __shfl_sync(0xffffffffu, qsum, (2 * c + 1) * 4);
-  const float qx_a = __shfl_sync(0xffffffffu, qscale, (2 * c) * 4);
-  const float qx_b = __shfl_sync(0xffffffffu, qscale, (2 * c + 1) * 4);
+  __syncthreads();
+  {
+    const int s = warp;  // kWarps == 4 k-steps
+    const int head = kDual ? r : (r & 3);
+    const bool has = head < G;
+    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? head : 0)) * p.q_sh +
+                    64 * c + 16 * s;
+    const float up = has ? ldexpf(1.0f, tail->q_exp[head]) : 0.0f;
+    uint32_t frag[8];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // word 2s (b0) and word 2s+1 (b1) of the step
+      const uint4 w = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * half)) : make_uint4(0, 0, 0, 0);
+      const T* e = reinterpret_cast<const T*>(&w);
+      int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int qe = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j]) * up)));
+        const int qo = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j + 1]) * up)));
+        hi_e[j] = qe >> 7;
+        lo_e[j] = qe - 128 * hi_e[j];
+        hi_o[j] = qo >> 7;
+        lo_o[j] = qo - 128 * hi_o[j];
+      }
+      const uint32_t he = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
+      const uint32_t le = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
+      const uint32_t ho = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
+      const uint32_t lo = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+      if (kDual) {
+        frag[half] = he;          // set 0 (hi digits): low-nibble MMA
+        frag[2 + half] = ho;      //                     high-nibble MMA
+        frag[4 + half] = le;      // set 1 (lo digits)
+        frag[6 + half] = lo;
+      } else {
+        frag[half] = r < 4 ? he : le;
+        frag[2 + half] = r < 4 ? ho : lo;
+        frag[4 + half] = 0;
+        frag[6 + half] = 0;
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(tail->qfrag[s][lane]);
+    dst[0] = make_uint4(frag[0], frag[1], frag[2], frag[3]);
+    dst[1] = make_uint4(frag[4], frag[5], frag[6], frag[7]);
+  }
+  __syncthreads();
+  uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint4* src = reinterpret_cast<const uint4*>(tail->qfrag[s][lane]);
+#pragma unroll
+    for (int k = 0; k < kSets; ++k) {
+      const uint4 f = src[k];
+      bq_lo[k][s][0] = f.x;
+      bq_lo[k][s][1] = f.y;
+      bq_hi[k][s][0] = f.z;
+      bq_hi[k][s][1] = f.w;
+    }
+  }
+  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds
+  const float qs_a = tail->q_sum[2 * c], qs_b = tail->q_sum[2 * c + 1];
+  const float qx_a = tail->q_scale[2 * c], qx_b = tail->q_scale[2 * c + 1];
   const bool ha_ok = (kDual || c < 2) && 2 * c < G;
   const bool hb_ok = (kDual || c < 2) && 2 * c + 1 < G;
 
@@ -462,22 +496,27 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();  // also: every stage has been consumed, codes[] is free for reuse
 
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][tid]);
+    float L = 0.0f;
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = M == -INFINITY ? 0.0f : exp2f(tail->warp_m[w][tid] - M);
+      tail->warp_f[w][tid] = f;
+      L += tail->warp_l[w][tid] * f;
+    }
+    tail->head_m[tid] = M;
+    tail->head_l[tid] = L;
+  }
+  __syncthreads();
+
   // ---- merge the 4 warps: red[w][h][d] = numerator_w * 2^(m_w - M), with
   //      numerator = 2^kTau * (acc - 1024 sum(P')) / (1 or 16) + sum(p * v_min)
   float* red = reinterpret_cast<float*>(codes);  // kWarps * kMaxGroup rows of kRedStride floats
   {
     const int ha = 2 * c, hb = 2 * c + 1;
-    float fa = 0.0f, fb = 0.0f;
-    if (ha < G) {
-      float M = -INFINITY;
-      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][ha]);
-      fa = M == -INFINITY ? 0.0f : exp2f(m_a - M);
-    }
-    if (hb < G) {
-      float M = -INFINITY;
-      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][hb]);
-      fb = M == -INFINITY ? 0.0f : exp2f(m_b - M);
-    }
+    const float fa = ha < G ? tail->warp_f[warp][ha] : 0.0f;
+    const float fb = hb < G ? tail->warp_f[warp][hb] : 0.0f;
     const float off_a = -kVBias * sp_a, off_b = -kVBias * sp_b;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -503,14 +542,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   for (int e = tid; e < outputs; e += kThreads) {
     const int h = e / kHeadDim;
     const int d = e - h * kHeadDim;
-    float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][h]);
-    float L = 0.0f, num = 0.0f;
-    for (int w = 0; w < kWarps; ++w) {
-      const float f = M == -INFINITY ? 0.0f : exp2f(tail->warp_m[w][h] - M);
-      L += tail->warp_l[w][h] * f;
-      num += red[red_index(w, h, d)];
-    }
+    const float M = tail->head_m[h], L = tail->head_l[h];
+    float num = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) num += red[red_index(w, h, d)];
     if (single) {
       store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
     } else {
@@ -606,6 +641,28 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 size_t counters_bytes(int64_t units) { return size_t((units * sizeof(int) + 255) / 256 * 256); }
 
+// SMs x resident CTAs per SM of `kernel` on the current device (cached per device and kernel).
+int64_t resident_slots(const void* kernel) {
+  static std::mutex mu;
+  static int64_t cache[64][4] = {};
+  static const void* kernels[4] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 3;
+  std::lock_guard<std::mutex> lock(mu);
+  int k = 0;
+  for (; k < 4 && kernels[k] != nullptr && kernels[k] != kernel; ++k) {
+  }
+  if (k == 4) return 148 * 3;
+  kernels[k] = kernel;
+  if (cache[dev][k] == 0) {
+    int sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes);
+    cache[dev][k] = int64_t(std::max(1, sms)) * std::max(1, per_sm);
+  }
+  return cache[dev][k];
+}
+
 }  // namespace
 
 int encode_codes_map(CUtensorMap* map, const uint8_t* kv_codes, int64_t num_pages, int64_t num_kv_heads) {
@@ -669,12 +726,19 @@ extern "C" int oq_decode_attn_int4_paged(
     return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: page pool too large for 32-bit TMA rows");
   }
 
-  // Split heuristic: enough CTAs for ~6 per SM of 148, at least one page each.
+  using Kernel = void (*)(const CUtensorMap, AttnParams);
+  Kernel kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true>
+                                                : decode_attn_kernel<__nv_bfloat16, false>)
+                                   : (group > 4 ? decode_attn_kernel<__half, true> : decode_attn_kernel<__half, false>);
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+
+  // Split heuristic: as many KV ranges per (sequence, KV head) as fill one wave of
+  // resident CTAs (SMs x CTAs per SM), so no SM idles behind a short last wave.
   const int64_t units = batch * num_kv_heads;
   int splits = num_splits;
   if (splits <= 0) {
-    const int64_t target = 148 * 6;
-    splits = int(std::min<int64_t>(std::max<int64_t>(1, (target + units - 1) / units), max_pages_per_seq));
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel));
+    splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units), max_pages_per_seq));
   }
   // the merging CTA stages (max, sum) of every split in 64 KB of shared memory
   splits = int(std::min<int64_t>(std::min<int64_t>(splits, max_pages_per_seq), kMaxSplits));
@@ -723,16 +787,6 @@ extern "C" int oq_decode_attn_int4_paged(
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto launch = [&](auto kernel) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    kernel<<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
-  };
-  if (dtype == OQ_BF16) {
-    if (group > 4) launch(decode_attn_kernel<__nv_bfloat16, true>);
-    else launch(decode_attn_kernel<__nv_bfloat16, false>);
-  } else {
-    if (group > 4) launch(decode_attn_kernel<__half, true>);
-    else launch(decode_attn_kernel<__half, false>);
-  }
+  kernel<<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
   return check_launch("decode_attn_int4_paged");
 }

@@ -215,6 +215,6 @@ def test_install_gdn_fastpath_binds_hooks():
 def test_workspace_split_heuristic_matches_the_c_side():
     from optiz_qwen_b200 import cabi
 
-    assert cabi.choose_splits(64, 2, 66) == 7
+    assert cabi.choose_splits(64, 2, 66) == 3
     assert cabi.choose_splits(1, 2, 2048) <= 512
     assert cabi.choose_splits(1024, 2, 128) == 1
