@@ -62,8 +62,13 @@ struct AttnParams {
   int32_t* status;
 };
 
+constexpr int kPageIdSlots = 1024;  // page ids of a CTA's range kept in shared memory
+
 struct __align__(16) SmemTail {
-  uint32_t qfrag[4][32][8];  // per k-step, per lane: B-operand digit fragments (built once per CTA)
+  union {
+    uint32_t qfrag[4][32][8];        // prologue: per k-step, per lane B-operand digit fragments
+    int32_t page_ids[kPageIdSlots];  // main loop: block-table entries of this CTA's page range
+  } u;
   uint64_t full[kStages];
   int stage_ok[kStages];
   int q_exp[kMaxGroup];      // per head: q ~ q_int * 2^-q_exp
@@ -186,8 +191,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   __syncthreads();
 
   const int32_t* bt_row = p.block_table + b * p.bt_stride;
+  // page id of range page i: the first kStages come straight from the block table,
+  // later ones from the shared-memory copy made after the prologue
   auto issue = [&](int i, int s) {
-    const int64_t page = bt_row[page_begin + i];
+    const int64_t page = (i >= kStages && i < kPageIdSlots) ? tail->u.page_ids[i] : bt_row[page_begin + i];
     if (page < 0 || page >= p.num_pages) {
       tail->stage_ok[s] = 0;
       report(p.status, OQ_DEV_BAD_PAGE);
@@ -283,7 +290,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         frag[6 + half] = 0;
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(tail->qfrag[s][lane]);
+    uint4* dst = reinterpret_cast<uint4*>(tail->u.qfrag[s][lane]);
     dst[0] = make_uint4(frag[0], frag[1], frag[2], frag[3]);
     dst[1] = make_uint4(frag[4], frag[5], frag[6], frag[7]);
   }
@@ -291,7 +298,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
-    const uint4* src = reinterpret_cast<const uint4*>(tail->qfrag[s][lane]);
+    const uint4* src = reinterpret_cast<const uint4*>(tail->u.qfrag[s][lane]);
 #pragma unroll
     for (int k = 0; k < kSets; ++k) {
       const uint4 f = src[k];
@@ -301,6 +308,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       bq_hi[k][s][1] = f.w;
     }
   }
+  __syncthreads();  // every warp holds its fragments: the union now takes the page ids
+  for (int idx = kStages + tid; idx < min(n, kPageIdSlots); idx += kThreads) tail->u.page_ids[idx] = bt_row[page_begin + idx];
+  __syncthreads();
   // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds
   const float qs_a = tail->q_sum[2 * c], qs_b = tail->q_sum[2 * c + 1];
   const float qx_a = tail->q_scale[2 * c], qx_b = tail->q_scale[2 * c + 1];
