@@ -184,17 +184,79 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int page_begin = split * p.pages_per_split;
   const int n = max(0, min(npages_b, page_begin + p.pages_per_split) - page_begin);
 
+  // ---- every independent global load of the prologue is issued first, so their
+  // latencies overlap: the first kStages page ids (one lane each), this thread's
+  // share of the remaining page ids, and the query elements this thread needs.
+  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
+  constexpr int kPidRegs = kPageIdSlots / kThreads;
+  const int32_t* bt_row = p.block_table + b * p.bt_stride;
+  const int n_smem = min(n, kPageIdSlots);
+  const int first_page = (warp == 0 && lane < min(n, kStages)) ? bt_row[page_begin + lane] : -1;
+  int pid_reg[kPidRegs];
+#pragma unroll
+  for (int j = 0; j < kPidRegs; ++j) {
+    const int idx = kStages + tid + j * kThreads;
+    pid_reg[j] = idx < n_smem ? bt_row[page_begin + idx] : 0;
+  }
+  // warp 0: a quarter of one head per lane (head lane/4, dims 64*(lane%4) ..) for the exponents
+  const int e_head = lane >> 2, e_part = lane & 3;
+  uint4 qe[8];
+  {
+    const bool has = warp == 0 && e_head < G;
+    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? e_head : 0)) * p.q_sh +
+                    64 * e_part;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qe[i] = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
+  }
+  // every warp: the 16 dims of k-step `warp` for this lane's MMA column (see below)
+  const int f_head = kDual ? r : (r & 3);
+  const bool f_has = f_head < G;
+  uint4 qf[2];
+  {
+    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (f_has ? f_head : 0)) * p.q_sh +
+                    64 * c + 16 * warp;
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+      qf[half] = f_has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * half)) : make_uint4(0, 0, 0, 0);
+  }
+
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&tail->full[s], 1);
     fence_mbar_init();
   }
-  __syncthreads();
+  // warp 0: per-head fixed-point exponent and sum(q)
+  if (warp == 0) {
+    float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const T* e = reinterpret_cast<const T*>(&qe[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = to_float<T>(e[j]);
+        amax = fmaxf(amax, fabsf(v));
+        sum += v;
+      }
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (e_part == 0) {
+      int ex = 0;
+      if (amax > 0.0f) {
+        frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
+        ex -= 1;                                            // 2^ex <= kQMax / amax
+      }
+      tail->q_exp[e_head] = ex;
+      tail->q_scale[e_head] = ldexpf(1.0f, -ex);
+      tail->q_sum[e_head] = sum;
+    }
+  }
+  __syncthreads();  // barriers initialised, exponents known
 
-  const int32_t* bt_row = p.block_table + b * p.bt_stride;
-  // page id of range page i: the first kStages come straight from the block table,
-  // later ones from the shared-memory copy made after the prologue
-  auto issue = [&](int i, int s) {
-    const int64_t page = (i >= kStages && i < kPageIdSlots) ? tail->u.page_ids[i] : bt_row[page_begin + i];
+  // page id of range page i: the first kStages were fetched by warp 0's lanes,
+  // later ones come from the shared-memory copy made after the prologue
+  auto issue = [&](int i, int s, int64_t page) {
     if (page < 0 || page >= p.num_pages) {
       tail->stage_ok[s] = 0;
       report(p.status, OQ_DEV_BAD_PAGE);
@@ -208,71 +270,35 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     bulk_load(metas + s * kStageMetaBytes, p.kv_meta + blk * 4 * kPage, kStageMetaBytes, &tail->full[s]);
   };
   int issued = 0;
-  if (tid == 0) {
-    for (; issued < min(n, kStages); ++issued) issue(issued, issued);
+  if (warp == 0) {
+#pragma unroll
+    for (int i = 0; i < kStages; ++i) {
+      const int page = __shfl_sync(0xffffffffu, first_page, i);
+      if (lane == 0 && i < n) issue(i, i, page);
+    }
+    issued = min(n, kStages);
   }
 
   // ---- query digits (B operand of q.k).  This lane feeds MMA column r: head
   // (packed) r & 3, digit hi for r < 4 and lo for r >= 4; (dual) head r, both
   // digits.  Lane c supplies dims 64c .. 64c+63; k-step s covers dims
   // 64c + 16s + {0..15}: the even dims in the "low nibble" MMA, the odd dims in
-  // the "high nibble" MMA.  Built once per CTA: warp 0 finds each head's
-  // fixed-point exponent, then warp w builds k-step w for all 32 lanes.
-  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
-  if (warp == 0) {
-    const int head = lane >> 2, part = lane & 3;
-    float amax = 0.0f, sum = 0.0f;
-    if (head < G) {
-      const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + head) * p.q_sh + 64 * part;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i));
-        const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float v = to_float<T>(e[j]);
-          amax = fmaxf(amax, fabsf(v));
-          sum += v;
-        }
-      }
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (part == 0) {
-      int ex = 0;
-      if (amax > 0.0f) {
-        frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
-        ex -= 1;                                            // 2^ex <= kQMax / amax
-      }
-      tail->q_exp[head] = ex;
-      tail->q_scale[head] = ldexpf(1.0f, -ex);
-      tail->q_sum[head] = sum;
-    }
-  }
-  __syncthreads();
+  // the "high nibble" MMA.  Warp w builds k-step w for all 32 lanes.
   {
-    const int s = warp;  // kWarps == 4 k-steps
-    const int head = kDual ? r : (r & 3);
-    const bool has = head < G;
-    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? head : 0)) * p.q_sh +
-                    64 * c + 16 * s;
-    const float up = has ? ldexpf(1.0f, tail->q_exp[head]) : 0.0f;
+    const float up = f_has ? ldexpf(1.0f, tail->q_exp[f_head]) : 0.0f;
     uint32_t frag[8];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {  // word 2s (b0) and word 2s+1 (b1) of the step
-      const uint4 w = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * half)) : make_uint4(0, 0, 0, 0);
-      const T* e = reinterpret_cast<const T*>(&w);
+      const T* e = reinterpret_cast<const T*>(&qf[half]);
       int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int qe = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j]) * up)));
-        const int qo = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j + 1]) * up)));
-        hi_e[j] = qe >> 7;
-        lo_e[j] = qe - 128 * hi_e[j];
-        hi_o[j] = qo >> 7;
-        lo_o[j] = qo - 128 * hi_o[j];
+        const int q_e = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j]) * up)));
+        const int q_o = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j + 1]) * up)));
+        hi_e[j] = q_e >> 7;
+        lo_e[j] = q_e - 128 * hi_e[j];
+        hi_o[j] = q_o >> 7;
+        lo_o[j] = q_o - 128 * hi_o[j];
       }
       const uint32_t he = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
       const uint32_t le = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
@@ -290,7 +316,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         frag[6 + half] = 0;
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(tail->u.qfrag[s][lane]);
+    uint4* dst = reinterpret_cast<uint4*>(tail->u.qfrag[warp][lane]);
     dst[0] = make_uint4(frag[0], frag[1], frag[2], frag[3]);
     dst[1] = make_uint4(frag[4], frag[5], frag[6], frag[7]);
   }
@@ -309,7 +335,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   }
   __syncthreads();  // every warp holds its fragments: the union now takes the page ids
-  for (int idx = kStages + tid; idx < min(n, kPageIdSlots); idx += kThreads) tail->u.page_ids[idx] = bt_row[page_begin + idx];
+#pragma unroll
+  for (int j = 0; j < kPidRegs; ++j) {
+    const int idx = kStages + tid + j * kThreads;
+    if (idx < n_smem) tail->u.page_ids[idx] = pid_reg[j];
+  }
   __syncthreads();
   // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds
   const float qs_a = tail->q_sum[2 * c], qs_b = tail->q_sum[2 * c + 1];
@@ -472,7 +502,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       break;
     }
     if (tid == 0 && i + kStages < n) {
-      issue(i + kStages, s);
+      const int nxt = i + kStages;
+      issue(nxt, s, nxt < kPageIdSlots ? tail->u.page_ids[nxt] : bt_row[page_begin + nxt]);
       ++issued;
     }
   }
