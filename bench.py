@@ -45,7 +45,7 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["hybrid", "serving"], default="hybrid")
+    ap.add_argument("--workload", choices=["hybrid", "serving", "longctx"], default="hybrid")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
     return ap.parse_args(argv)
@@ -404,8 +404,66 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_longctx(args):
+    """Config 2: one sequence at context 131072, 6 attention layers, KV range split across the ranks;
+    per layer: append on the tail rank, partial attention, NCCL all-gather of (out, lse), LSE merge."""
+    import torch
+
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_pg(world, local)
+    hbm_peak, peak_src = peaks()
+    length, layers = 131072, 6
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2 * 1000 + rank)
+    decs = []
+    for _ in range(layers):
+        d = ContextParallelDecoder(2, 256, rank=rank, world=world, device=device)
+        d.prefill_random(length, generator=gen, capacity_tokens=0, page_seed=2)
+        decs.append(d)
+    q = torch.randn((1, 8, 256), generator=gen, device=device).to(torch.bfloat16)
+
+    def step():
+        for d in decs:
+            d.decode(q)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier(dist, device)
+    steps = max(10, min(args.steps, 200))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    ms = max_over_ranks(start.elapsed_time(end) / steps, dist, device)
+    kv_bytes = length * 2 * 264 * layers
+    line = {"metric": METRIC, "value": round(1000.0 / ms, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int4 KV codes x int8/fp16 tensor-core dots, fp32 softmax/merge",
+            "data": "synthetic, seeded",
+            "config": {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
+                                   "KV range split evenly across GPUs, NCCL all-gather of fp32 (out, lse) partials "
+                                   "+ LSE merge per layer (eager launches)", "global_batch": 1},
+            "step_hbm": {"kv_bytes_per_step_total": kv_bytes,
+                         "GB_s_per_gpu": round(kv_bytes / world / ms / 1e6, 1),
+                         "frac_per_gpu": round(kv_bytes / world / ms / 1e6 / hbm_peak, 4), "peak_source": peak_src}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main(argv=None):
     args = parse_args(argv)
+    if args.workload == "longctx" and args.impl != "reference":
+        run_longctx(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -1,0 +1,161 @@
+"""Long-context decode attention split across the GPUs of one box.
+
+One sequence's KV cache is cut into contiguous, page-aligned token ranges, one
+per rank (``kv_ranges``).  Each rank stores only its range in its own paged
+INT4 pool and runs the split-KV decode kernel over it, producing the
+normalised fp32 partial output and the natural-log log-sum-exp of its scores
+(``oq_decode_attn_int4_paged`` with ``out_f32`` / ``out_lse``).  One all-gather
+over NCCL (NVLink / NVSwitch) exchanges the partials -- B x Hq x (D + 1) fp32
+per rank, 8,224 B for one sequence with 8 heads of 256 -- and every rank
+combines them with ``oq_lse_merge``:
+
+    out = sum_r exp(lse_r - L) * out_r,   L = log sum_r exp(lse_r).
+
+New decode tokens are appended to the last rank's range (the tail of the
+sequence).  The reference decodes on one GPU; this module has no counterpart
+there.  The exchange goes through torch.distributed (NCCL); no kernel here
+reads another GPU's memory.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+
+
+def kv_ranges(length: int, world: int, page_size: int = 64) -> list[tuple[int, int]]:
+    """Even split of ``[0, length)`` into ``world`` page-aligned contiguous ranges (may be empty)."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    pages = -(-int(length) // page_size)
+    per = -(-pages // world) if pages else 0
+    out = []
+    for r in range(world):
+        lo = min(length, r * per * page_size)
+        hi = min(length, (r + 1) * per * page_size)
+        out.append((lo, hi))
+    return out
+
+
+def pack_partial(out_f32: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
+    """[B, Hq, D] fp32 + [B, Hq] fp32 -> one contiguous [B * Hq, D + 1] message."""
+    b, h, d = out_f32.shape
+    msg = torch.empty((b * h, d + 1), dtype=torch.float32, device=out_f32.device)
+    msg[:, :d].copy_(out_f32.reshape(b * h, d))
+    msg[:, d].copy_(lse.reshape(b * h))
+    return msg
+
+
+def unpack_partials(gathered: torch.Tensor, head_dim: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """[world, R, D + 1] -> (part_out [world, R, D], part_lse [world, R]), both contiguous."""
+    return gathered[..., :head_dim].contiguous(), gathered[..., head_dim].contiguous()
+
+
+@dataclass
+class PartialFns:
+    """The compute a rank plugs in: partial attention over its range, and the merge."""
+
+    partial: Callable[[torch.Tensor], tuple[torch.Tensor, torch.Tensor]]  # q [B,Hq,D] -> (out_f32, lse)
+    merge: Callable[[torch.Tensor, torch.Tensor], torch.Tensor]          # (part_out, part_lse) -> out [R, D]
+
+
+def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> torch.Tensor:
+    """Attention of ``q`` ``[B, Hq, D]`` over the KV ranges of every rank of ``group``; returns ``[B, Hq, D]``.
+
+    Every rank takes the same collective step (one all-gather) per call.
+    """
+    import torch.distributed as dist
+
+    out_f32, lse = fns.partial(q)
+    msg = pack_partial(out_f32, lse)
+    world = dist.get_world_size(group)
+    gathered = torch.empty((world * msg.shape[0], msg.shape[1]), dtype=msg.dtype, device=msg.device)
+    dist.all_gather_into_tensor(gathered, msg, group=group)
+    part_out, part_lse = unpack_partials(gathered.view(world, *msg.shape), q.shape[-1])
+    return fns.merge(part_out, part_lse).reshape(q.shape)
+
+
+class ContextParallelDecoder:
+    """One attention layer's share of a long sequence on this rank, backed by the sm_100a kernels.
+
+    ``keys`` / ``values`` passed to ``prefill`` are the whole sequence's K/V
+    ``[B, Hkv, T, D]``; each rank keeps only its own range.  ``decode(q)`` runs
+    the partial attention, the all-gather and the merge; ``append`` adds one new
+    token on the last rank.
+    """
+
+    def __init__(self, num_kv_heads: int, head_dim: int, *, rank: int, world: int, device, group=None,
+                 page_size: int = 64, out_dtype=torch.bfloat16):
+        from . import cabi
+
+        self.cabi = cabi
+        self.rank, self.world, self.group = rank, world, group
+        self.num_kv_heads, self.head_dim, self.page_size = num_kv_heads, head_dim, page_size
+        self.device = torch.device(device)
+        self.out_dtype = out_dtype
+        self.paged = None
+        self.range = (0, 0)
+        self._ws = None
+
+    def prefill(self, keys: torch.Tensor, values: torch.Tensor, *, capacity_tokens: int | None = None,
+                page_seed: int | None = None) -> None:
+        from .compression.paged_kv import PageAllocator, PagedKvState
+
+        b, h, t, d = keys.shape
+        lo, hi = kv_ranges(t, self.world, self.page_size)[self.rank]
+        self.range = (lo, hi)
+        extra = (capacity_tokens or 0) if self.rank == self.world - 1 else 0
+        cap = (hi - lo) + extra
+        pages = max(1, self.cabi.pages_for(max(cap, 1), self.page_size))
+        pool = self.cabi.PagedKvPool(b * pages, h, d, self.page_size, self.device)
+        self.paged = PagedKvState(pool, b, max_pages=pages, allocator=PageAllocator(b * pages, page_seed))
+        self.paged.reserve([max(cap, 1)] * b)
+        if hi > lo:
+            self.paged.append(keys[:, :, lo:hi].to(self.device), values[:, :, lo:hi].to(self.device))
+
+    def prefill_random(self, length: int, *, generator: torch.Generator, capacity_tokens: int = 0,
+                       page_seed: int | None = None, batch: int = 1, dtype=torch.bfloat16) -> None:
+        """Fill this rank's range of a ``length``-token sequence with N(0,1) K/V (synthetic workloads);
+        only the rank's own slice is generated and stored."""
+        from .compression.paged_kv import PageAllocator, PagedKvState
+
+        lo, hi = kv_ranges(length, self.world, self.page_size)[self.rank]
+        self.range = (lo, hi)
+        extra = capacity_tokens if self.rank == self.world - 1 else 0
+        cap = max(1, (hi - lo) + extra)
+        pages = self.cabi.pages_for(cap, self.page_size)
+        pool = self.cabi.PagedKvPool(batch * pages, self.num_kv_heads, self.head_dim, self.page_size, self.device)
+        self.paged = PagedKvState(pool, batch, max_pages=pages, allocator=PageAllocator(batch * pages, page_seed))
+        self.paged.reserve([cap] * batch)
+        chunk = 8192
+        for start in range(lo, hi, chunk):
+            m = min(chunk, hi - start)
+            shp = (batch, self.num_kv_heads, m, self.head_dim)
+            k = torch.randn(shp, generator=generator, device=self.device, dtype=torch.float32).to(dtype)
+            v = torch.randn(shp, generator=generator, device=self.device, dtype=torch.float32).to(dtype)
+            self.paged.append(k, v)
+
+    def append(self, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Append new tokens ``[B, Hkv, n, D]`` to the sequence tail (held by the last rank)."""
+        if self.rank == self.world - 1:
+            self.paged.append(key, value)
+            self.range = (self.range[0], self.range[1] + int(key.shape[-2]))
+
+    def _partial(self, q: torch.Tensor):
+        b, hq, d = q.shape
+        out_f32 = torch.empty((b, hq, d), dtype=torch.float32, device=self.device)
+        lse = torch.empty((b, hq), dtype=torch.float32, device=self.device)
+        if self._ws is None:
+            self._ws = self.cabi.new_decode_workspace(b, hq, self.num_kv_heads, self.paged.max_pages, self.device)
+        self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
+                                        self.head_dim ** -0.5, out_f32=out_f32, out_lse=lse, workspace=self._ws,
+                                        want_out=False)
+        return out_f32, lse
+
+    def _merge(self, part_out: torch.Tensor, part_lse: torch.Tensor) -> torch.Tensor:
+        return self.cabi.lse_merge(part_out, part_lse, dtype=self.out_dtype)
+
+    def decode(self, q: torch.Tensor) -> torch.Tensor:
+        return context_parallel_attention(q, PartialFns(self._partial, self._merge), self.group)

@@ -1,0 +1,92 @@
+"""Long-context decode split across 2 GPUs (NCCL), against one GPU and the oracle.
+
+Runs as two spawned ranks, one per GPU; skipped when fewer than 2 GPUs are
+visible.  NVLS is disabled for the test's NCCL communicator.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LENGTH = 3000
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    from oracle import kv_quant as kq
+
+    rng = np.random.default_rng(22)
+    k = kq.round_bf16(rng.standard_normal((1, 2, LENGTH, 256), dtype=np.float32))
+    v = kq.round_bf16(rng.standard_normal((1, 2, LENGTH, 256), dtype=np.float32))
+    q = kq.round_bf16(rng.standard_normal((2, 1, 8, 256), dtype=np.float32))       # two decode steps
+    kn = kq.round_bf16(rng.standard_normal((1, 2, 1, 256), dtype=np.float32))      # token appended between them
+    return k, v, q, kn
+
+
+def _rank(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    k, v, q, kn = _inputs()
+    dec = ContextParallelDecoder(2, 256, rank=rank, world=world, device=dev)
+    dec.prefill(torch.from_numpy(k).to(torch.bfloat16), torch.from_numpy(v).to(torch.bfloat16), capacity_tokens=16)
+    outs = [dec.decode(torch.from_numpy(q[0]).to(dev, torch.bfloat16)).float().cpu().numpy()]
+    knt = torch.from_numpy(kn).to(dev, torch.bfloat16)
+    dec.append(knt, knt)
+    outs.append(dec.decode(torch.from_numpy(q[1]).to(dev, torch.bfloat16)).float().cpu().numpy())
+    np.save(os.path.join(outdir, f"out{rank}.npy"), np.stack(outs))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_long_context_split_over_two_gpus_matches_one_gpu_and_oracle():
+    import torch.multiprocessing as mp
+
+    from oracle import kv_quant as kq
+    from oracle.attention import decode_attention
+    from optiz_qwen_b200 import cabi
+    from optiz_qwen_b200.compression.paged_kv import PagedKvState
+    from tests._util import assert_attn_close
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_rank, args=(2, _free_port(), d), nprocs=2, join=True)
+        outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(2)]
+    k, v, q, kn = _inputs()
+    # one GPU, whole cache
+    pool = cabi.PagedKvPool(64, 2, 256, 64, "cuda")
+    paged = PagedKvState(pool, 1, max_pages=60)
+    paged.append(torch.from_numpy(k).cuda().to(torch.bfloat16), torch.from_numpy(v).cuda().to(torch.bfloat16))
+    single0 = cabi.decode_attention_int4(torch.from_numpy(q[0]).cuda().to(torch.bfloat16), pool, paged.block_table,
+                                         paged.seq_lens, 1 / 16).float().cpu().numpy()
+    # oracle: fp32 attention over the dequantised cache (+ the appended token for step 2)
+    kd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([k, kn], axis=2)))[0]
+    vd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([v, kn], axis=2)))[0]
+    ref0, _ = decode_attention(q[0], [kd[:, :LENGTH]], [vd[:, :LENGTH]], 1 / 16)
+    ref1, _ = decode_attention(q[1], [kd], [vd], 1 / 16)
+    for out in outs:
+        assert_attn_close(out[0], ref0)
+        assert_attn_close(out[1], ref1)
+        assert_attn_close(out[0], single0)
+    assert np.array_equal(outs[0], outs[1])        # every rank holds the same merged output
