@@ -97,7 +97,7 @@ def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int =
     """Split count used when ``num_splits <= 0``: enough KV ranges per (sequence, KV head) to
     fill one wave of resident CTAs (the C side reads SM count and occupancy from the device)."""
     units = batch * num_kv_heads
-    splits = min(max(1, (sm_count * ctas_per_sm) // units), max_pages, 512)
+    splits = min(max(1, (sm_count * ctas_per_sm) // units), max(1, max_pages // 8), 512)
     pps = -(-max_pages // splits)
     return -(-max_pages // pps)
 

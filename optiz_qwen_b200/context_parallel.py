@@ -70,7 +70,10 @@ def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> 
 
     out_f32, lse = fns.partial(q)
     msg = pack_partial(out_f32, lse)
-    world = dist.get_world_size(group)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        part_out, part_lse = unpack_partials(msg.view(1, *msg.shape), q.shape[-1])
+        return fns.merge(part_out, part_lse).reshape(q.shape)
     gathered = torch.empty((world * msg.shape[0], msg.shape[1]), dtype=msg.dtype, device=msg.device)
     dist.all_gather_into_tensor(gathered, msg, group=group)
     part_out, part_lse = unpack_partials(gathered.view(world, *msg.shape), q.shape[-1])

@@ -40,6 +40,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 8;
 constexpr int kMaxSplits = 512;
+constexpr int kMinPagesPerSplit = 8;
 
 struct AttnParams {
   const void* query;
@@ -779,7 +780,9 @@ extern "C" int oq_decode_attn_int4_paged(
   int splits = num_splits;
   if (splits <= 0) {
     const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel));
-    splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units), max_pages_per_seq));
+    // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
+    splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
+                                   std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
   }
   // the merging CTA stages (max, sum) of every split in 64 KB of shared memory
   splits = int(std::min<int64_t>(std::min<int64_t>(splits, max_pages_per_seq), kMaxSplits));
