@@ -41,6 +41,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 8;
 constexpr int kMaxSplits = 512;
 constexpr int kMinPagesPerSplit = 8;
+constexpr int kInLaunchMergeSplits = 8;
 
 struct AttnParams {
   const void* query;
@@ -60,6 +61,7 @@ struct AttnParams {
   int* counters;
   int max_splits;
   int pages_per_split;
+  int defer_merge;  // 1: write partials only, a separate merge kernel combines them
   int32_t* status;
 };
 
@@ -598,7 +600,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
   }
-  if (single) return;
+  if (single || p.defer_merge) return;
 
   // ---- split-KV merge by the last CTA of this (sequence, KV head)
   __threadfence();
@@ -664,6 +666,70 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   }
   if (tid == 0) p.counters[unit] = 0;  // ready for the next launch
+}
+
+// ---- split-KV merge for many splits: one CTA per (sequence x KV head, query head),
+// one thread per output dim; the (max, sum) of every split are staged in shared
+// memory and each thread reduces its dim over the splits with coalesced loads.
+constexpr int kMergeThreads = kHeadDim;
+
+template <typename T>
+__global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p) {
+  __shared__ float sm_w[kMaxSplits];
+  __shared__ float sm_l[kMaxSplits];
+  __shared__ float red_buf[kMergeThreads / 32];
+  const int h = blockIdx.y;
+  const int64_t unit = blockIdx.x;
+  const int G = p.group;
+  const int64_t b = unit / p.num_kv_heads;
+  const int kvh = int(unit - b * p.num_kv_heads);
+  const int len = max(p.seq_lens[b], 0);
+  const int npages_b = int(min(int64_t((len + kPage - 1) / kPage), p.max_pages));
+  const int nsplit = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
+  if (nsplit == 1) return;  // the attention kernel wrote this unit's output itself
+  const int tid = threadIdx.x;
+  const int rec_floats = G * (kHeadDim + 2);
+  const int outputs = G * kHeadDim;
+  const float* recs = p.partials + unit * p.max_splits * rec_floats;
+  float mloc = -INFINITY;
+  for (int s = tid; s < nsplit; s += kMergeThreads) {
+    const float m = recs[s * rec_floats + outputs + h];
+    sm_w[s] = m;
+    sm_l[s] = recs[s * rec_floats + outputs + G + h];
+    mloc = fmaxf(mloc, m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+  if ((tid & 31) == 0) red_buf[tid >> 5] = mloc;
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < kMergeThreads / 32; ++w) M = fmaxf(M, red_buf[w]);
+  __syncthreads();
+  float lloc = 0.0f;
+  for (int s = tid; s < nsplit; s += kMergeThreads) {
+    const float w = M == -INFINITY ? 0.0f : exp2f(sm_w[s] - M);
+    sm_w[s] = w;
+    lloc += sm_l[s] * w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
+  if ((tid & 31) == 0) red_buf[tid >> 5] = lloc;
+  __syncthreads();
+  float L = 0.0f;
+  for (int w = 0; w < kMergeThreads / 32; ++w) L += red_buf[w];
+  const int d = tid;
+  const float* col = recs + h * kHeadDim + d;
+  float n0 = 0.0f, n1 = 0.0f, n2 = 0.0f, n3 = 0.0f;
+  int s = 0;
+  for (; s + 4 <= nsplit; s += 4) {
+    n0 = fmaf(sm_w[s], col[(s + 0) * rec_floats], n0);
+    n1 = fmaf(sm_w[s + 1], col[(s + 1) * rec_floats], n1);
+    n2 = fmaf(sm_w[s + 2], col[(s + 2) * rec_floats], n2);
+    n3 = fmaf(sm_w[s + 3], col[(s + 3) * rec_floats], n3);
+  }
+  for (; s < nsplit; ++s) n0 = fmaf(sm_w[s], col[s * rec_floats], n0);
+  const float num = (n0 + n1) + (n2 + n3);
+  store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
 }
 
 // ---------------------------------------------------------------- host side
@@ -827,10 +893,20 @@ extern "C" int oq_decode_attn_int4_paged(
   p.partials = workspace ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters_bytes(units)) : nullptr;
   p.max_splits = int(std::min<int64_t>(max_splits_ws, 1 << 20));
   p.pages_per_split = pps;
+  // few splits: the last CTA of each (sequence, KV head) merges in-launch; many: a merge kernel
+  p.defer_merge = splits > kInLaunchMergeSplits ? 1 : 0;
   p.status = device_status;
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   kernel<<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
+  if (p.defer_merge) {
+    const dim3 mgrid((unsigned)units, (unsigned)group);
+    if (dtype == OQ_BF16) {
+      split_merge_kernel<__nv_bfloat16><<<mgrid, kMergeThreads, 0, s>>>(p);
+    } else {
+      split_merge_kernel<__half><<<mgrid, kMergeThreads, 0, s>>>(p);
+    }
+  }
   return check_launch("decode_attn_int4_paged");
 }
