@@ -197,6 +197,25 @@ int oq_gdn_recurrent(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, void* stream);
 
+/* Chunked gated delta rule (GDN prefill) on the tensor cores (tcgen05 / TMEM).
+ * Replaces the hook chunk_gated_delta_rule (transformers models/qwen3_5/modeling_qwen3_5.py:466-476;
+ * torch_chunk_gated_delta_rule :234-311; fla chunk_gated_delta_rule, fla/ops/gated_delta_rule/chunk.py:365).
+ * q, k, v: bf16 [B, T, H, 128], element strides per (b, t, h), unit stride along the head dim,
+ * every stride a multiple of 16 bytes and the pointers 16-byte aligned.  g, beta: [B, T, H]
+ * contiguous (f32 / f16 / bf16).  out: bf16 [B, T, H, 128] contiguous.  States fp32
+ * [B, H, 128, 128] contiguous; initial_state NULL = zeros, final_state may be NULL.
+ * chunk_size must be 64.  One CTA per (sequence, head).  device_status (nullable) gets
+ * OQ_DEV_TIMEOUT if an internal wait gives up. */
+int oq_gdn_chunk_fwd(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int64_t chunk_size, int32_t* device_status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -218,5 +218,46 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
     return out
 
 
+CHUNK_SIZE = 64
+
+
+def gdn_chunk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,
+                  scale: float | None = None, initial_state: torch.Tensor | None = None,
+                  final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  use_qk_l2norm: bool = False, device_status: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked gated delta rule (prefill) on the tensor cores; same contract as :func:`gdn_recurrent`.
+
+    q, k, v must be bf16 with unit stride along the head dim and 16-byte-multiple
+    strides (a slice of a fused projection qualifies); Dk = Dv = 128.
+    """
+    require_cuda(q, k, v, g, beta, initial_state, final_state)
+    if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError("q, k must be [B, T, H, Dk] and v [B, T, H, Dv]")
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
+        raise ValueError("q, k, v must be bf16")
+    bsz, t, h, dk = q.shape
+    dv = v.shape[-1]
+    q, k, v = (x if x.stride(3) == 1 and all((s * 2) % 16 == 0 and s > 0 for s in x.stride()[:3])
+               and x.data_ptr() % 16 == 0 else x.contiguous() for x in (q, k, v))
+    g, beta = g.contiguous(), beta.contiguous()
+    if tuple(g.shape) != (bsz, t, h) or tuple(beta.shape) != (bsz, t, h):
+        raise ValueError("g and beta must be [B, T, H]")
+    for s in (initial_state, final_state):
+        if s is not None and (s.dtype != torch.float32 or tuple(s.shape) != (bsz, h, dk, dv) or not s.is_contiguous()):
+            raise ValueError("states must be contiguous fp32 [B, H, Dk, Dv]")
+    if out is None:
+        out = torch.empty((bsz, t, h, dv), dtype=q.dtype, device=q.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (bsz, t, h, dv) or not out.is_contiguous():
+        raise ValueError("out must be contiguous bf16 [B, T, H, Dv]")
+    scale = dk ** -0.5 if scale is None else float(scale)
+    call("oq_gdn_chunk_fwd", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
+         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+         v.stride(0), v.stride(1), v.stride(2),
+         ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
+         ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
+         CHUNK_SIZE, ptr(device_status), stream_ptr(q.device))
+    return out
+
+
 def pages_for(length: int, page_size: int = PAGE_SIZE) -> int:
     return max(0, math.ceil(length / page_size))

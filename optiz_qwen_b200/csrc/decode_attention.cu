@@ -733,20 +733,6 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-  });
-  return fn;
-}
-
 size_t counters_bytes(int64_t units) { return size_t((units * sizeof(int) + 255) / 256 * 256); }
 
 // SMs x resident CTAs per SM of `kernel` on the current device (cached per device and kernel).
@@ -774,7 +760,7 @@ int64_t resident_slots(const void* kernel) {
 }  // namespace
 
 int encode_codes_map(CUtensorMap* map, const uint8_t* kv_codes, int64_t num_pages, int64_t num_kv_heads) {
-  auto fn = encode_fn();
+  auto fn = tensor_map_encoder();
   if (fn == nullptr) return fail(OQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {cuuint64_t(kRowBytes), cuuint64_t(num_pages * num_kv_heads * 2 * kPage)};
   const cuuint64_t strides[1] = {cuuint64_t(kRowBytes)};

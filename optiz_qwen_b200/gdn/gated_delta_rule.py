@@ -79,15 +79,29 @@ def chunk_gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g:
                            **kwargs):
     """Prefill form (fla/ops/gated_delta_rule/chunk.py:365 signature).
 
-    The result equals the chunked WY formulation of
-    ``torch_chunk_gated_delta_rule`` (modeling_qwen3_5.py:234-311) to fp32
-    rounding: the recurrence is the same, run by the kernel with the state
-    held on-chip across all T tokens.
+    bf16 inputs with 128-wide heads run the chunked WY form of
+    ``torch_chunk_gated_delta_rule`` (modeling_qwen3_5.py:234-311) on the tensor
+    cores (``oq_gdn_chunk_fwd``, 64-token chunks, fp32 state in tensor memory).
+    Other input dtypes run the same recurrence token by token through the
+    recurrent kernel, which reads fp16 / fp32 directly.
     """
     _check_unsupported(cu_seqlens, kwargs.pop("use_gate_in_kernel", False), kwargs)
-    return fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, scale=scale, initial_state=initial_state,
-                                            output_final_state=output_final_state,
-                                            use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+    if chunk_size != cabi.CHUNK_SIZE:
+        raise ValueError(f"chunk_size must be {cabi.CHUNK_SIZE}")
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16) or q.shape[-1] != 128 or v.shape[-1] != 128:
+        return fused_recurrent_gated_delta_rule(q, k, v, g=g, beta=beta, scale=scale, initial_state=initial_state,
+                                                output_final_state=output_final_state,
+                                                use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+    q, k = _expand_value_heads(q, k, v)
+    batch, _, heads, dk = q.shape
+    dv = v.shape[-1]
+    if initial_state is not None:
+        initial_state = initial_state.to(torch.float32).contiguous()
+    final = (torch.empty((batch, heads, dk, dv), dtype=torch.float32, device=q.device)
+             if output_final_state else None)
+    out = cabi.gdn_chunk_fwd(q, k, v, g, beta, scale=scale, initial_state=initial_state, final_state=final,
+                             use_qk_l2norm=use_qk_l2norm_in_kernel)
+    return out, final
 
 
 def install_gdn_fastpath(model) -> int:
