@@ -36,16 +36,16 @@ namespace {
 
 constexpr int kC = 64;          // chunk length
 constexpr int kD = 128;         // dk = dv
-constexpr int kThreads = 128;   // one thread per TMEM lane
+constexpr int kThreads = 256;   // two threads per TMEM lane (warps w and w + 4), splitting the columns
 constexpr uint32_t kTmemCols = 512;
 
 // TMEM columns (fp32 accumulators, lane = dv row unless noted)
-constexpr uint32_t kColG = 0;     // [K;Q]K^T (lane = token), then W^T (lane = dk), then Vn^T P^T
+constexpr uint32_t kColG = 0;     // [K;Q]K^T (lane = token), then W^T (lane = dk)
 constexpr uint32_t kColU = 64;    // U^T
 constexpr uint32_t kColWS = 128;  // (W S)^T
 constexpr uint32_t kColQS = 192;  // (Q S)^T
-constexpr uint32_t kColDS = 256;  // dS^T, 128 columns
-constexpr uint32_t kColS = 384;   // S^T, 128 columns: the state
+constexpr uint32_t kColPV = 256;  // Vn^T P^T
+constexpr uint32_t kColS = 384;   // S^T, 128 columns: the state (dS^T accumulates onto e^{gc_last} S^T)
 
 // Shared memory (byte offsets from a 1024-aligned base).  A "tile" is 64 rows x 128 B.
 constexpr uint32_t kTile = 8192;
@@ -53,13 +53,17 @@ constexpr uint32_t kKQBytes = 4 * kTile;           // one input stage: K d<64 | 
 constexpr uint32_t kOffV = 2 * kKQBytes;           // V d<64 | V d>=64
 constexpr uint32_t kOffS = kOffV + 2 * kTile;      // S^T hi (2 x 16 KB) | S^T lo; later Vn hi|Vn lo|Vs hi|Vs lo
 constexpr uint32_t kOffW = kOffS + 65536;          // W hi | W lo (16 KB each); before that N, then Ar/Ab tiles
-constexpr uint32_t kOffX = kOffW + 32768;          // X fp32 [64][65]
+constexpr uint32_t kOffX = kOffW + 32768;          // X fp32 [64][68]
 constexpr uint32_t kOffP = kOffX + 17408;          // P hi | P lo
 constexpr uint32_t kOffSmall = kOffP + 2 * kTile;
-constexpr int kXStride = 65;
-constexpr int kTStride = 17;
-// small area: 8 per-token float arrays, the off-diagonal solve scratch, barriers
-constexpr uint32_t kSmallFloats = 8 * kC + 3 * 16 * kTStride;
+constexpr int kNStride = 65;                       // N rows (written one row per thread)
+constexpr int kXStride = 68;                       // X rows (read as float4)
+constexpr uint32_t kOffTmp = kOffW + 16896;        // solve scratch after N: [2][16][20] then [32][36]
+constexpr int kT2Stride = 20;
+constexpr int kT3Stride = 36;
+// small area: two buffers (this chunk, next chunk) of 9 per-token float arrays, barriers
+constexpr int kTokArrays = 9;
+constexpr uint32_t kSmallFloats = 2 * kTokArrays * kC;
 constexpr uint32_t kOffBars = kOffSmall + kSmallFloats * 4;
 constexpr uint32_t kSmemBytes = kOffBars + 64 + 1024;  // + alignment slack
 
@@ -128,7 +132,7 @@ __device__ __forceinline__ void store_split32(uint8_t* hi, uint8_t* lo, uint32_t
 
 // Sum of squares of one 128-element bf16 row held as two swizzled 64-element halves.
 __device__ __forceinline__ float row_sumsq(const uint8_t* lo_half, const uint8_t* hi_half, uint32_t row) {
-  float ss = 0.0f;
+  float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const uint8_t* base = half ? hi_half : lo_half;
@@ -139,12 +143,12 @@ __device__ __forceinline__ float row_sumsq(const uint8_t* lo_half, const uint8_t
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
+        ss[i] = fmaf(f.x, f.x, ss[i]);
+        ss[i] = fmaf(f.y, f.y, ss[i]);
       }
     }
   }
-  return ss;
+  return (ss[0] + ss[1]) + (ss[2] + ss[3]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -153,22 +157,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sa = smem_addr(sm);
+  // per-token arrays of chunk c live in buffer c & 1:
+  // 0 g, 1 gc (in-chunk cumulative g), 2 beta, 3 dk, 4 dq (inverse L2 norms), 5 sfac = dk e^{gc_last - gc},
+  // 6 cq = scale dq e^{gc}, 7 rfac = beta e^{gc} dk, 8 gcl = gc log2(e)
   float* f_small = reinterpret_cast<float*>(sm + kOffSmall);
-  float* s_graw = f_small;
-  float* s_gc = f_small + kC;
-  float* s_beta = f_small + 2 * kC;
-  float* s_dk = f_small + 3 * kC;
-  float* s_dq = f_small + 4 * kC;
-  float* s_sfac = f_small + 5 * kC;  // dk e^{gc_last - gc}
-  float* s_cq = f_small + 6 * kC;    // scale dq e^{gc}
-  float* s_rfac = f_small + 7 * kC;  // beta e^{gc} dk
-  float* s_T = f_small + 8 * kC;     // [3][16][17]
+  auto tok = [&](int buf, int k) { return f_small + (buf * kTokArrays + k) * kC; };
+  float* s_T = reinterpret_cast<float*>(sm + kOffTmp);
   float* s_N = reinterpret_cast<float*>(sm + kOffW);
   float* s_X = reinterpret_cast<float*>(sm + kOffX);
   Bars* bars = reinterpret_cast<Bars*>(sm + kOffBars);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 127;  // TMEM lane served by this thread
+  const int half = tid >> 7;   // which half of the columns it takes
   const int h = blockIdx.x;
   const int b = blockIdx.y;
   const int H = p.num_heads;
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+  const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
 
   // Load schedule (identical in every thread; only thread 0 issues).
   int kq_issued[2] = {0, 0}, kq_waited[2] = {0, 0}, v_issued = 0, v_waited = 0;
@@ -224,19 +226,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (n_chunks > 1) issue_kq(1, 1);
   __syncwarp();  // tcgen05.ld / st below are warp-collective
 
-  // Initial state -> TMEM (S^T, lane = dv column l = tid) and the split S^T operand tiles.
+  // Initial state -> TMEM (S^T, lane = dv column l) and the split S^T operand tiles.
   uint8_t* st_hi = sm + kOffS;
   uint8_t* st_lo = sm + kOffS + 32768;
   const int64_t state_base = (int64_t(b) * H + h) * kD * kD;
 #pragma unroll 1
-  for (int q4 = 0; q4 < 4; ++q4) {
+  for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
     float sv[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      sv[j] = p.s_in != nullptr ? p.s_in[state_base + int64_t(32 * q4 + j) * kD + tid] : 0.0f;
+      sv[j] = p.s_in != nullptr ? p.s_in[state_base + int64_t(32 * q4 + j) * kD + lane] : 0.0f;
     }
     tmem_st32(lane_base + kColS + 32 * q4, sv);
-    store_split32(st_hi + (q4 >> 1) * 16384, st_lo + (q4 >> 1) * 16384, tid, (q4 & 1) * 4, sv);
+    store_split32(st_hi + (q4 >> 1) * 16384, st_lo + (q4 >> 1) * 16384, lane, (q4 & 1) * 4, sv);
   }
   tmem_wait_st();
   fence_proxy_async_smem();
@@ -256,99 +258,138 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!bad) tc_fence_after();
     return bad;
   };
+  // G = [K; Q] K^T of chunk cc (M = 128 rows: 64 keys then 64 queries; N = 64 keys; K = d); thread 0.
+  auto issue_gram = [&](int cc) {
+    const uint32_t kq_a = sa + (cc & 1) * kKQBytes;
+    tc_fence_after();
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t off = kq_a + (kk >> 2) * 2 * kTile + (kk & 3) * 32;
+      umma_bf16(tmem + kColG, smem_desc_sw128(off, 16, 1024), smem_desc_sw128(off, 16, 1024), kIdescN64, kk > 0);
+    }
+  };
+  // Per-token scalars of chunk cc (its inputs have landed): g, beta, norms, then the in-chunk
+  // cumulative decay (warp scan, two tokens per lane) and the derived factors.  Ends without a
+  // barrier after the scan; callers synchronise before reading.
+  // g and beta of token `t` of chunk cc (zero past the end), loaded ahead of use.
+  auto load_gb = [&](int cc, float& gv, float& bv) {
+    gv = 0.0f;
+    bv = 0.0f;
+    const int64_t t = int64_t(cc) * kC + tid;
+    if (tid < kC && t < T) {
+      const int64_t gi = (int64_t(b) * T + t) * H + h;
+      gv = load_as_float(p.g, p.g_dtype, gi);
+      bv = load_as_float(p.beta, p.beta_dtype, gi);
+    }
+  };
+  auto prep_scalars = [&](int cc, float gv, float bv) {
+    const uint8_t* kqc = sm + (cc & 1) * kKQBytes;
+    const int buf = cc & 1;
+    if (tid < kC) {
+      tok(buf, 0)[tid] = gv;
+      tok(buf, 2)[tid] = bv;
+      tok(buf, 3)[tid] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kqc, kqc + 2 * kTile, tid) + 1e-6f) : 1.0f;
+    } else if (tid < 2 * kC) {
+      const int r = tid - kC;
+      tok(buf, 4)[r] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kqc + kTile, kqc + 3 * kTile, r) + 1e-6f) : 1.0f;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float a0 = tok(buf, 0)[2 * tid], a1 = tok(buf, 0)[2 * tid + 1];
+      float incl = a0 + a1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+      if (tid == 0) excl = 0.0f;
+      const float gc[2] = {excl + a0, (excl + a0) + a1};
+      const float gl = __shfl_sync(0xffffffffu, gc[1], 31);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * tid + e;
+        const float dk = tok(buf, 3)[t];
+        tok(buf, 1)[t] = gc[e];
+        tok(buf, 8)[t] = gc[e] * 1.4426950408889634f;
+        tok(buf, 5)[t] = dk * expf(gl - gc[e]);
+        tok(buf, 6)[t] = p.scale * tok(buf, 4)[t] * expf(gc[e]);
+        tok(buf, 7)[t] = tok(buf, 2)[t] * expf(gc[e]) * dk;
+      }
+    }
+  };
+
+  if (n_chunks > 0) {
+    if (wait_all(&bars->kq[0], 0)) {
+      aborted = true;
+    } else {
+      ++kq_waited[0];
+      if (tid == 0) {
+        issue_gram(0);
+        umma_commit(&bars->mma);
+      }
+      float gv, bv;
+      load_gb(0, gv, bv);
+      prep_scalars(0, gv, bv);
+      aborted = mma_done();
+    }
+  }
 
 #pragma unroll 1
-  for (int c = 0; c < n_chunks; ++c) {
+  for (int c = 0; c < n_chunks && !aborted; ++c) {
     const int st = c & 1;
-    uint8_t* kq = sm + st * kKQBytes;
     const uint32_t kq_a = sa + st * kKQBytes;
     const int64_t t0 = int64_t(c) * kC;
+    const float* s_gc = tok(st, 1);
+    const float* s_beta = tok(st, 2);
+    const float* s_dk = tok(st, 3);
+    const float* s_dq = tok(st, 4);
+    const float* s_sfac = tok(st, 5);
+    const float* s_cq = tok(st, 6);
+    const float* s_rfac = tok(st, 7);
+    const float* s_gcl = tok(st, 8);
+    const bool last = c + 1 == n_chunks;
+    float g_next, b_next;
+    load_gb(c + 1, g_next, b_next);
 
-    if (wait_all(&bars->kq[st], kq_waited[st] & 1)) { aborted = true; break; }
-    ++kq_waited[st];
-    if (wait_all(&bars->v, v_waited & 1)) { aborted = true; break; }
-    ++v_waited;
-
-    // ---- G = [K; Q] K^T  (M = 128 rows: 64 keys then 64 queries; N = 64 keys; K = d)
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = kq_a + (kk >> 2) * 2 * kTile + (kk & 3) * 32;
-        umma_bf16(tmem + kColG, smem_desc_sw128(off, 16, 1024), smem_desc_sw128(off, 16, 1024), kIdescN64, kk > 0);
-      }
-      umma_commit(&bars->mma);
-    }
-
-    // ---- per-token scalars: g, beta, norms
-    if (tid < kC) {
-      float gv = 0.0f, bv = 0.0f;
-      if (t0 + tid < T) {
-        const int64_t gi = (int64_t(b) * T + t0 + tid) * H + h;
-        gv = load_as_float(p.g, p.g_dtype, gi);
-        bv = load_as_float(p.beta, p.beta_dtype, gi);
-      }
-      s_graw[tid] = gv;
-      s_beta[tid] = bv;
-      s_dk[tid] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kq, kq + 2 * kTile, tid) + 1e-6f) : 1.0f;
-    } else {
-      const int r = tid - kC;
-      s_dq[r] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kq + kTile, kq + 3 * kTile, r) + 1e-6f) : 1.0f;
-    }
-    __syncthreads();
-    if (tid == 0) {  // in-chunk cumulative decay, sequential like the reference's cumsum
-      float acc = 0.0f;
-#pragma unroll 8
-      for (int t = 0; t < kC; ++t) {
-        acc += s_graw[t];
-        s_gc[t] = acc;
-      }
-    }
-    __syncthreads();
-    if (tid < kC) {
-      const float gt = s_gc[tid];
-      s_sfac[tid] = s_dk[tid] * expf(s_gc[kC - 1] - gt);
-      s_cq[tid] = p.scale * s_dq[tid] * expf(gt);
-      s_rfac[tid] = s_beta[tid] * expf(gt) * s_dk[tid];
-    }
-    if (mma_done()) { aborted = true; break; }
-
-    // ---- rows of N (threads 0..63) and P (threads 64..127) from the Gram lanes
+    // (G of this chunk and its per-token scalars are ready.)
+    // ---- rows of N (lanes 0..63) and P (lanes 64..127) from the Gram lanes; each thread
+    // takes 32 of the 64 columns
     {
-      float g0[32], g1[32];
-      tmem_ld32(lane_base + kColG, g0);
-      tmem_ld32(lane_base + kColG + 32, g1);
-      if (tid < kC) {
-        const int i = tid;
+      float gr[32];
+      tmem_ld32(lane_base + kColG + 32 * half, gr);
+      const int j0 = 32 * half;
+      if (lane < kC) {
+        const int i = lane;
         const float fi = -s_beta[i] * s_dk[i];
-        const float gci = s_gc[i];
-        float* nrow = s_N + i * kXStride;
+        const float gli = s_gcl[i];
+        float* nrow = s_N + i * kNStride + j0;
 #pragma unroll
-        for (int j = 0; j < kC; ++j) {
-          const float gij = j < 32 ? g0[j] : g1[j - 32];
-          nrow[j] = j < i ? fi * s_dk[j] * gij * expf(gci - s_gc[j]) : 0.0f;
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = j0 + jj;
+          nrow[jj] = j < i ? fi * s_dk[j] * gr[jj] * exp2f(gli - s_gcl[j]) : 0.0f;
         }
       } else {
-        const int i = tid - kC;
+        const int i = lane - kC;
         const float fi = p.scale * s_dq[i];
-        const float gci = s_gc[i];
+        const float gli = s_gcl[i];
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int cc = 0; cc < 4; ++cc) {
           float pv[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const int j = 8 * c8 + e;
-            const float gij = j < 32 ? g0[j] : g1[j - 32];
-            pv[e] = j <= i ? fi * s_dk[j] * gij * expf(gci - s_gc[j]) : 0.0f;
+            const int j = j0 + 8 * cc + e;
+            pv[e] = j <= i ? fi * s_dk[j] * gr[8 * cc + e] * exp2f(gli - s_gcl[j]) : 0.0f;
           }
-          store_split8(sm + kOffP, sm + kOffP + kTile, swz(i, c8), pv);
+          store_split8(sm + kOffP, sm + kOffP + kTile, swz(i, 4 * half + cc), pv);
         }
       }
     }
     tc_fence_before();
     __syncthreads();
 
-    // ---- X = (I - N)^-1: 16x16 diagonal blocks by forward substitution ...
+    // ---- X = (I - N)^-1 by doubling.  16x16 diagonal blocks by forward substitution
+    // (one column per thread), zeroing the blocks right of blocks 0 and 2 ...
     if (tid < kC) {
       const int o = 16 * (tid >> 4), jj = tid & 15;
       float x[16];
@@ -358,51 +399,95 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ii = 1; ii < 16; ++ii) {
         float acc = 0.0f;
 #pragma unroll
-        for (int m = 0; m < ii; ++m) acc = fmaf(s_N[(o + ii) * kXStride + o + m], x[m], acc);
+        for (int m = 0; m < ii; ++m) acc = fmaf(s_N[(o + ii) * kNStride + o + m], x[m], acc);
         if (ii > jj) x[ii] = acc;
       }
 #pragma unroll
       for (int ii = 0; ii < 16; ++ii) s_X[(o + ii) * kXStride + o + jj] = x[ii];
+      if ((o & 16) == 0) {
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) s_X[(o + ii) * kXStride + o + 16 + jj] = 0.0f;
+      }
     }
     __syncthreads();
-    // ... then the blocks below the diagonal, nearest first: X_IJ = X_II sum_{M=J}^{I-1} N_IM X_MJ.
-#pragma unroll 1
-    for (int dist = 1; dist <= 3; ++dist) {
-      const int n_el = (4 - dist) * 256;
-      for (int e = tid; e < n_el; e += kThreads) {
-        const int J = e >> 8, I = J + dist, ii = (e >> 4) & 15, jj = e & 15;
-        float acc = 0.0f;
-        for (int M = J; M < I; ++M) {
+    // ... then the 32x32 diagonal blocks: X_10 = X_11 N_10 X_00 and X_32 = X_33 N_32 X_22
+    // (1x2 outputs per thread) ...
+    {
+      const int blk = tid >> 7, I = 16 * (1 + 2 * blk), J = 32 * blk;
+      const int r = (tid & 127) >> 3, c0 = (tid & 7) * 2;
+      float* tb = s_T + blk * 16 * kT2Stride;
+      float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-          for (int m = 0; m < 16; ++m) {
-            acc = fmaf(s_N[(16 * I + ii) * kXStride + 16 * M + m], s_X[(16 * M + m) * kXStride + 16 * J + jj], acc);
-          }
-        }
-        s_T[(J * 16 + ii) * kTStride + jj] = acc;
+      for (int m = 0; m < 16; ++m) {
+        const float n = s_N[(I + r) * kNStride + J + m];
+        const float2 x = *reinterpret_cast<const float2*>(&s_X[(J + m) * kXStride + J + c0]);
+        a0 = fmaf(n, x.x, a0);
+        a1 = fmaf(n, x.y, a1);
       }
+      *reinterpret_cast<float2*>(&tb[r * kT2Stride + c0]) = make_float2(a0, a1);
       __syncthreads();
-      for (int e = tid; e < n_el; e += kThreads) {
-        const int J = e >> 8, I = J + dist, ii = (e >> 4) & 15, jj = e & 15;
-        float acc = 0.0f;
-        for (int m = 0; m <= ii; ++m) {
-          acc = fmaf(s_X[(16 * I + ii) * kXStride + 16 * I + m], s_T[(J * 16 + m) * kTStride + jj], acc);
-        }
-        s_X[(16 * I + ii) * kXStride + 16 * J + jj] = acc;
+      a0 = a1 = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float x = s_X[(I + r) * kXStride + I + m];
+        const float2 t = *reinterpret_cast<const float2*>(&tb[m * kT2Stride + c0]);
+        a0 = fmaf(x, t.x, a0);
+        a1 = fmaf(x, t.y, a1);
       }
-      __syncthreads();
+      *reinterpret_cast<float2*>(&s_X[(I + r) * kXStride + J + c0]) = make_float2(a0, a1);
     }
+    __syncthreads();
+    // ... and the lower-left 32x32 block: X[32:, :32] = X[32:, 32:] N[32:, :32] X[:32, :32]
+    // Warp w computes columns 4w..4w+3 of T = N[32:, :32] X[:32, :32] (lane = row; X[m][c] = 0
+    // for m < c), then rows 4w..4w+3 of X[32:, 32:] T (lane = column; X[32 + r][32 + m] = 0 for m > r).
+    {
+      const int c0 = 4 * warp, r = tid & 31;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+      for (int m = c0; m < 32; ++m) {
+        const float n = s_N[(32 + r) * kNStride + m];
+        const float4 x = *reinterpret_cast<const float4*>(&s_X[m * kXStride + c0]);
+        acc[0] = fmaf(n, x.x, acc[0]);
+        acc[1] = fmaf(n, x.y, acc[1]);
+        acc[2] = fmaf(n, x.z, acc[2]);
+        acc[3] = fmaf(n, x.w, acc[3]);
+      }
+      *reinterpret_cast<float4*>(&s_T[r * kT3Stride + c0]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      __syncthreads();
+      const int r0 = 4 * warp, col = tid & 31;
+      float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+      for (int m0 = 0; m0 < r0 + 4; m0 += 4) {
+        float tcol[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tcol[i] = s_T[(m0 + i) * kT3Stride + col];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float4 x = *reinterpret_cast<const float4*>(&s_X[(32 + r0 + a) * kXStride + 32 + m0]);
+          o[a] = fmaf(x.x, tcol[0], o[a]);
+          o[a] = fmaf(x.y, tcol[1], o[a]);
+          o[a] = fmaf(x.z, tcol[2], o[a]);
+          o[a] = fmaf(x.w, tcol[3], o[a]);
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) s_X[(32 + r0 + a) * kXStride + col] = o[a];
+    }
+    __syncthreads();
 
     // ---- Ar = X diag(beta e^gc dk), Ab = X diag(beta): split K-major tiles [t][m] (over N)
     {
-      const int t = tid >> 1, half = tid & 1;
+      const int t = tid >> 2, qq = tid & 3;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int c8 = 4 * half + cc;
-        float ar[8], ab[8];
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c8 = 2 * qq + cc;
+        float xr[8], ar[8], ab[8];
+        *reinterpret_cast<float4*>(xr) = *reinterpret_cast<const float4*>(&s_X[t * kXStride + 8 * c8]);
+        *reinterpret_cast<float4*>(xr + 4) = *reinterpret_cast<const float4*>(&s_X[t * kXStride + 8 * c8 + 4]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int m = 8 * c8 + e;
-          const float xv = m > t ? 0.0f : (m == t ? 1.0f : s_X[t * kXStride + m]);
+          const float xv = m > t ? 0.0f : (m == t ? 1.0f : xr[e]);
           ar[e] = xv * s_rfac[m];
           ab[e] = xv * s_beta[m];
         }
@@ -414,6 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- W^T = K^T Ar^T (lanes = dk), U^T = V^T Ab^T (lanes = dv)
+    if (wait_all(&bars->v, v_waited & 1)) { aborted = true; break; }
+    ++v_waited;
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -436,17 +523,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- W tiles: MN-major [d][t] (row d = this thread's lane)
     {
-      float w0[32], w1[32];
-      tmem_ld32(lane_base + kColG, w0);
-      tmem_ld32(lane_base + kColG + 32, w1);
-      store_split32(sm + kOffW, sm + kOffW + 16384, tid, 0, w0);
-      store_split32(sm + kOffW, sm + kOffW + 16384, tid, 4, w1);
+      float w[32];
+      tmem_ld32(lane_base + kColG + 32 * half, w);
+      store_split32(sm + kOffW, sm + kOffW + 16384, lane, 4 * half, w);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
 
-    // ---- (WS)^T = S^T W^T (3 products), (QS)^T = S^T Q^T (2 products)
+    // ---- (WS)^T = S^T W^T (3 products), (QS)^T = S^T Q^T (2 products); meanwhile the state
+    // in TMEM is scaled by e^{gc_last} so that dS^T can accumulate onto it.
     if (tid == 0) {
       tc_fence_after();
       const uint32_t sh = sa + kOffS, sl = sa + kOffS + 32768;
@@ -466,6 +552,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(&bars->mma);
     }
+    __syncwarp();
+    {
+      const float gamma = expf(s_gc[kC - 1]);
+#pragma unroll 1
+      for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
+        float sv[32];
+        tmem_ld32(lane_base + kColS + 32 * q4, sv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[j] *= gamma;
+        tmem_st32(lane_base + kColS + 32 * q4, sv);
+      }
+      tmem_wait_st();
+    }
+    tc_fence_before();
     if (mma_done()) { aborted = true; break; }
 
     // ---- Vn^T = U^T - (WS)^T; Vs^T = Vn^T diag(sfac): split K-major tiles [l][t] over S^T's tiles
@@ -474,25 +574,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* vn_lo = sm + kOffS + 16384;
       uint8_t* vs_hi = sm + kOffS + 32768;
       uint8_t* vs_lo = sm + kOffS + 49152;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float ws[32], u[32];
-        tmem_ld32(lane_base + kColWS + 32 * half, ws);
-        tmem_ld32(lane_base + kColU + 32 * half, u);
+      float ws[32], u[32];
+      tmem_ld32(lane_base + kColWS + 32 * half, ws);
+      tmem_ld32(lane_base + kColU + 32 * half, u);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          ws[j] = u[j] - ws[j];                   // v_new
-          u[j] = ws[j] * s_sfac[32 * half + j];  // v_new scaled for the state update
-        }
-        store_split32(vn_hi, vn_lo, tid, 4 * half, ws);
-        store_split32(vs_hi, vs_lo, tid, 4 * half, u);
+      for (int j = 0; j < 32; ++j) {
+        ws[j] = u[j] - ws[j];                   // v_new
+        u[j] = ws[j] * s_sfac[32 * half + j];  // v_new scaled for the state update
       }
+      store_split32(vn_hi, vn_lo, lane, 4 * half, ws);
+      store_split32(vs_hi, vs_lo, lane, 4 * half, u);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
 
-    // ---- Vn^T P^T (3 products) and dS^T = Vs^T K (2 products)
+    // ---- Vn^T P^T (3 products) and S^T += Vs^T K (2 products); then the next chunk's G, whose
+    // per-token scalars are computed while the tensor cores run.
     if (tid == 0) {
       tc_fence_after();
       const uint32_t vnh = sa + kOffS, vnl = vnh + 16384, vsh = vnh + 32768, vsl = vnh + 49152;
@@ -503,52 +601,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t a_nl = smem_desc_sw128(vnl + kk * 32, 16, 1024);
         const uint64_t b_ph = smem_desc_sw128(ph + kk * 32, 16, 1024);
         const uint64_t b_pl = smem_desc_sw128(pl + kk * 32, 16, 1024);
-        umma_bf16(tmem + kColG, a_nh, b_ph, kIdescN64, kk > 0);
-        umma_bf16(tmem + kColG, a_nh, b_pl, kIdescN64, true);
-        umma_bf16(tmem + kColG, a_nl, b_ph, kIdescN64, true);
+        umma_bf16(tmem + kColPV, a_nh, b_ph, kIdescN64, kk > 0);
+        umma_bf16(tmem + kColPV, a_nh, b_pl, kIdescN64, true);
+        umma_bf16(tmem + kColPV, a_nl, b_ph, kIdescN64, true);
         const uint64_t a_sh = smem_desc_sw128(vsh + kk * 32, 16, 1024);
         const uint64_t a_sl = smem_desc_sw128(vsl + kk * 32, 16, 1024);
         const uint64_t b_k = smem_desc_sw128(kq_a + kk * 2048, 2 * kTile, 1024);
-        umma_bf16(tmem + kColDS, a_sh, b_k, kIdescN128BMn, kk > 0);
-        umma_bf16(tmem + kColDS, a_sl, b_k, kIdescN128BMn, true);
+        umma_bf16(tmem + kColS, a_sh, b_k, kIdescN128BMn, true);
+        umma_bf16(tmem + kColS, a_sl, b_k, kIdescN128BMn, true);
       }
-      umma_commit(&bars->mma);
     }
+    if (!last) {
+      if (wait_all(&bars->kq[st ^ 1], kq_waited[st ^ 1] & 1)) {
+        if (tid == 0) umma_commit(&bars->mma);
+        aborted = true;
+        break;
+      }
+      ++kq_waited[st ^ 1];
+      if (tid == 0) issue_gram(c + 1);
+    }
+    if (tid == 0) umma_commit(&bars->mma);
+    if (!last) prep_scalars(c + 1, g_next, b_next);
     if (mma_done()) { aborted = true; break; }
     if (c + 2 < n_chunks) issue_kq(c + 2, st);
     __syncwarp();
 
     // ---- outputs: o[t][l] = cq_t (QS)^T[l][t] + (Vn^T P^T)[l][t]
+    // (staged as [64][128] bf16 over the consumed P tiles, then written as 16-byte row pieces)
     {
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float qs[32], pv[32];
-        tmem_ld32(lane_base + kColQS + 32 * half, qs);
-        tmem_ld32(lane_base + kColG + 32 * half, pv);
+      __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(sm + kOffP);
+      float qs[32], pv[32];
+      tmem_ld32(lane_base + kColQS + 32 * half, qs);
+      tmem_ld32(lane_base + kColPV + 32 * half, pv);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int t = 32 * half + j;
-          if (t0 + t < T) {
-            p.out[((int64_t(b) * T + t0 + t) * H + h) * kD + tid] = __float2bfloat16_rn(fmaf(s_cq[t], qs[j], pv[j]));
-          }
+      for (int j = 0; j < 32; ++j) {
+        const int t = 32 * half + j;
+        ostage[t * kD + lane] = __float2bfloat16_rn(fmaf(s_cq[t], qs[j], pv[j]));
+      }
+      // ---- the updated state as the split S^T operand of the next chunk
+      if (!last) {
+#pragma unroll 1
+        for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
+          float sv[32];
+          tmem_ld32(lane_base + kColS + 32 * q4, sv);
+          store_split32(st_hi + (q4 >> 1) * 16384, st_lo + (q4 >> 1) * 16384, lane, (q4 & 1) * 4, sv);
         }
       }
-    }
-    // ---- state: S^T <- e^{gc_last} S^T + dS^T, and the split operand for the next chunk
-    {
-      const float gamma = expf(s_gc[kC - 1]);
-      const bool last = c + 1 == n_chunks;
-#pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float sv[32], ds[32];
-        tmem_ld32(lane_base + kColS + 32 * q4, sv);
-        tmem_ld32(lane_base + kColDS + 32 * q4, ds);
+      __syncthreads();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] = fmaf(gamma, sv[j], ds[j]);
-        tmem_st32(lane_base + kColS + 32 * q4, sv);
-        if (!last) store_split32(st_hi + (q4 >> 1) * 16384, st_lo + (q4 >> 1) * 16384, tid, (q4 & 1) * 4, sv);
+      for (int e = tid; e < kC * (kD / 8); e += kThreads) {
+        const int row = e >> 4, ch = e & 15;
+        if (t0 + row < T) {
+          *reinterpret_cast<uint4*>(p.out + ((int64_t(b) * T + t0 + row) * H + h) * kD + 8 * ch) =
+              *reinterpret_cast<const uint4*>(ostage + row * kD + 8 * ch);
+        }
       }
-      tmem_wait_st();
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -567,11 +674,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (p.s_out != nullptr) {
     tc_fence_after();
 #pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
+    for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
       float sv[32];
       tmem_ld32(lane_base + kColS + 32 * q4, sv);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) p.s_out[state_base + int64_t(32 * q4 + j) * kD + tid] = sv[j];
+      for (int j = 0; j < 32; ++j) p.s_out[state_base + int64_t(32 * q4 + j) * kD + lane] = sv[j];
     }
   }
   tc_fence_before();
