@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Decode throughput of the optiz-qwen hybrid hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload hybrid|serving]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload hybrid|serving|longctx|prefill]
 
 Workload "hybrid" (default): one decode token for B=64 sequences at context 4096
 through the 24-layer Qwen3.5 hybrid stack's hot path (18 Gated-DeltaNet
@@ -9,7 +10,10 @@ recurrent steps + 6 x [append-quantize + split-KV INT4 paged attention], 3:1
 interleave; Hq 8 / Hkv 2 / head_dim 256; GDN 16 heads x 128).  Each rank runs
 its own batch (weak scaling, no data-path collective).  Workload "serving":
 B=1024 ragged sequences, context U[256, 8192], sharded across ranks by byte
-cost (strong scaling).
+cost (strong scaling).  Workload "longctx": one sequence at context 131072 with
+the KV range split across ranks.  Workload "prefill": the chunked GDN prefill on
+the tensor cores (B=8, T=8192, 16 heads of 128, 18 layers) followed by 256
+recurrent decode steps from the resulting states.
 
 The timed region replays a CUDA graph of every launch of a step, with all
 inputs resident in HBM (the working set, ~2 GB, is far larger than the 126 MB
@@ -45,8 +49,10 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["hybrid", "serving", "longctx"], default="hybrid")
+    ap.add_argument("--workload", choices=["hybrid", "serving", "longctx", "prefill"], default="hybrid")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="prefill workload only: a reduced case (B=4, T=8192, 2 layers, 8 decode steps) for ncu captures")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
     return ap.parse_args(argv)
 
@@ -472,10 +478,198 @@ def run_longctx(args):
         dist.destroy_process_group()
 
 
+PREFILL_METRIC = "GDN chunked prefill tokens/s (tensor-core WY form, 18 layers) + recurrent decode tail"
+
+
+def _prefill_inputs(b, t, h, d, gen, device):
+    import torch
+
+    q, k, v = (torch.randn((b, t, h, d), generator=gen, device=device).to(torch.bfloat16) for _ in range(3))
+    beta = torch.sigmoid(torch.randn((b, t, h), generator=gen, device=device))
+    g = -torch.nn.functional.softplus(torch.randn((b, t, h), generator=gen, device=device))
+    return q, k, v, g, beta
+
+
+def prefill_cpu_baseline(budget_s: float, t: int = 512):
+    """The oracle's chunked form (numpy restatement of torch_chunk_gated_delta_rule) on one head; its
+    matrix products run on numpy's BLAS threads (all host cores)."""
+    import numpy as np
+
+    from oracle import gdn as ogdn
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except ImportError:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.standard_normal((1, t, 1, 128), dtype=np.float32) for _ in range(3))
+    g = -np.logaddexp(0, rng.standard_normal((1, t, 1))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((1, t, 1))))).astype(np.float32)
+    s0 = (0.02 * rng.standard_normal((1, 1, 128, 128))).astype(np.float32)
+    ogdn.chunk_gated_delta_rule(q, k, v, g, beta, 64, s0, True, True)
+    t0, n = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s or n == 0:
+        ogdn.chunk_gated_delta_rule(q, k, v, g, beta, 64, s0, True, True)
+        n += 1
+    sec = (time.perf_counter() - t0) / n                 # seconds per head-layer of t tokens
+    # whole workload: every token runs 16 heads x 18 layers
+    return {"value": round(t / sec / (16 * 18), 2), "unit": "prefill tokens/s", "cores": cores, "kind": "port",
+            "sample": f"one head, T={t}, {n} runs in {time.perf_counter() - t0:.1f} s (numpy BLAS on {cores} "
+                      "threads), scaled to 16 heads x 18 layers per token; numpy chunked oracle of "
+                      "torch_chunk_gated_delta_rule"}
+
+
+def run_prefill(args):
+    """Config 4: chunked GDN prefill (B=8, T=8192, H=16, d=128, 18 layers) on the tensor cores, then
+    256 recurrent decode steps from the prefill's final states.  Weak scaling: every rank runs its own
+    batch of 8 sequences, with no data-path collective."""
+    import torch
+
+    from optiz_qwen_b200 import cabi
+    from optiz_qwen_b200.gdn.gated_delta_rule import chunk_gated_delta_rule
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_pg(world, local)
+    hbm_peak, peak_src = peaks()
+    tflops_peak = None
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        d = json.loads(pk.read_text())
+        tflops_peak = float(d.get("bf16_tflops_sustained") or d.get("bf16_tflops") or 0) or None
+    b, t, h, d, layers, tail = (4, 8192, 16, 128, 2, 8) if args.small else (8, 8192, 16, 128, 18, 256)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4 * 1000 + rank)
+    ins = [_prefill_inputs(b, t, h, d, gen, device) for _ in range(layers)]
+    s0 = [0.02 * torch.randn((b, h, d, d), generator=gen, device=device) for _ in range(layers)]
+    states = [torch.empty_like(x) for x in s0]
+    out = torch.empty((b, t, h, d), dtype=torch.bfloat16, device=device)
+    dq = [_prefill_inputs(b, 1, h, d, gen, device) for _ in range(tail)]
+    dout = torch.empty((b, 1, h, d), dtype=torch.bfloat16, device=device)
+
+    def prefill():
+        for (q, k, v, g, beta), si, so in zip(ins, s0, states):
+            cabi.gdn_chunk_fwd(q, k, v, g, beta, initial_state=si, final_state=so, out=out, use_qk_l2norm=True)
+
+    def decode_tail():
+        for q, k, v, g, beta in dq:
+            for st in states:
+                cabi.gdn_recurrent(q, k, v, g, beta, initial_state=st, final_state=st, out=dout, use_qk_l2norm=True)
+
+    prefill()
+    decode_tail()
+    torch.cuda.synchronize(device)
+    graphs = {}
+    for name, fn in (("prefill", prefill), ("decode", decode_tail)):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        graphs[name] = gr
+    for _ in range(max(3, args.warmup)):
+        graphs["prefill"].replay()
+        graphs["decode"].replay()
+    barrier(dist, device)
+    steps = max(3, min(args.steps, 40))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with ClockSampler(device.index if world == 1 else local) as clocks:
+        ev[0].record()
+        for _ in range(steps):
+            graphs["prefill"].replay()
+        ev[1].record()
+        for _ in range(steps):
+            graphs["decode"].replay()
+        ev[2].record()
+        torch.cuda.synchronize(device)
+    barrier(dist, device)
+    pre_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / steps, dist, device)
+    dec_ms = max_over_ranks(ev[1].elapsed_time(ev[2]) / steps, dist, device)
+    layer_us = pre_ms * 1000.0 / layers
+    bytes_layer = b * t * h * 1032                       # q, k, v, o bf16 + g, beta fp32 per token-head
+    flops_layer = b * h * (t // 64) * (10 * 64 * 64 * d + 6 * 64 * d * d)
+    gbs = bytes_layer / layer_us / 1e3
+    tflops = flops_layer / layer_us / 1e6
+
+    # end to end, one layer through the hook: pinned host inputs -> device -> prefill -> output + state to host
+    q, k, v, g, beta = (x.cpu().pin_memory() for x in ins[0])
+    s_host = s0[0].cpu().pin_memory()
+    o_host = torch.empty((b, t, h, d), dtype=torch.bfloat16).pin_memory()
+    st_host = torch.empty((b, h, d, d), dtype=torch.float32).pin_memory()
+    def e2e_layer():
+        dev = [x.to(device, non_blocking=True) for x in (q, k, v, g, beta, s_host)]
+        o, st = chunk_gated_delta_rule(*dev[:3], g=dev[3], beta=dev[4], initial_state=dev[5], output_final_state=True,
+                                       use_qk_l2norm_in_kernel=True)
+        o_host.copy_(o, non_blocking=True)
+        st_host.copy_(st, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+    e2e_layer()
+    e_steps = 5
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e_steps):
+        e2e_layer()
+    e2.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e_steps, dist, device)
+    h2d = sum(x.numel() * x.element_size() for x in (q, k, v, g, beta, s_host))
+    d2h = o_host.numel() * 2 + st_host.numel() * 4
+
+    tokens = b * t * world
+    line = {
+        "metric": PREFILL_METRIC, "value": round(tokens * 1000.0 / pre_ms, 1), "unit": "prefill tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(pre_ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 q/k/v; fp32 state and WY factors as split bf16 hi+lo tensor-core operands, fp32 accumulate",
+        "data": "synthetic, seeded (config-0 distributions)",
+        "config": {"workload": f"GDN chunked prefill: B={b} x T={t} per GPU, {h} heads, dk=dv={d}, chunk 64, "
+                               f"{layers} layers; then {tail} recurrent decode steps x {layers} layers from the final "
+                               "states" + (" (reduced profiling case)" if args.small else ""),
+                   "global_batch": b * world, "seq_len": t, "l2": "inputs 805 MB per layer, far above L2"},
+        "clocks": clocks.summary(),
+        "decode_tail": {"ms_per_step": round(dec_ms / tail, 4), "tokens_per_s": round(b * world * tail * 1000.0 / dec_ms, 1),
+                        "state_GB_s": round(layers * b * h * d * d * 8 / (dec_ms / tail) / 1e6, 1)},
+        "e2e": {"value": round(b * t * world * 1000.0 / e2e_ms / layers, 1), "unit": "prefill tokens/s",
+                "h2d_bytes_per_step": h2d * layers, "d2h_bytes_per_step": d2h * layers,
+                "note": "one layer through chunk_gated_delta_rule with pinned host buffers, scaled to 18 layers"},
+        "gpu_launches": layers * steps,
+        "roofline": {"bound": "hbm", "kernel": "gdn_chunk", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(gbs / hbm_peak, 4), "traffic": dram_traffic("gdn_chunk"), "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": bytes_layer, "us_per_launch": round(layer_us, 1),
+                     "tensor": {"achieved_tflops": round(tflops, 1), "peak_tflops": tflops_peak,
+                                "frac": round(tflops / tflops_peak, 4) if tflops_peak else None,
+                                "algorithmic_flops_per_launch": flops_layer}},
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = prefill_cpu_baseline(min(args.cpu_seconds, 15.0))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graphs
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.workload == "longctx" and args.impl != "reference":
         run_longctx(args)
+        return
+    if args.workload == "prefill":
+        if args.impl != "reference":
+            run_prefill(args)
+        elif int(os.environ.get("RANK", "0")) == 0:
+            base = prefill_cpu_baseline(min(args.cpu_seconds, 60.0))
+            print(json.dumps({"impl": "reference", "metric": PREFILL_METRIC, "value": base["value"],
+                              "unit": base["unit"], "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+                              "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                              "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
+                              "data": "synthetic, seeded",
+                              "config": {"workload": "GDN chunked prefill (B=8, T=8192, 16 heads, 18 layers), "
+                                                     "sampled on the host CPU", "global_batch": 8},
+                              "cpu_baseline": base,
+                              "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
         return
     if args.impl == "reference":
         run_reference(args)
