@@ -555,9 +555,11 @@ def run_prefill(args):
             cabi.gdn_chunk_fwd(q, k, v, g, beta, initial_state=si, final_state=so, out=out, use_qk_l2norm=True)
 
     def decode_tail():
-        for q, k, v, g, beta in dq:
-            for st in states:
-                cabi.gdn_recurrent(q, k, v, g, beta, initial_state=st, final_state=st, out=dout, use_qk_l2norm=True)
+        for step, (q, k, v, g, beta) in enumerate(dq):
+            for li, st in enumerate(states):
+                # every launch but the first follows another layer's GDN step (see HybridDecodeStack)
+                cabi.gdn_recurrent(q, k, v, g, beta, initial_state=st, final_state=st, out=dout, use_qk_l2norm=True,
+                                   prefetch_state=layers > 1 and (step > 0 or li > 0))
 
     prefill()
     decode_tail()

@@ -49,6 +49,17 @@ enum oq_device_status {
   OQ_DEV_TIMEOUT = 4       /* a bounded wait on a copy ran out: the CTA gave up */
 };
 
+/* Flags of oq_gdn_recurrent. */
+enum oq_gdn_flags {
+  /* Launch with programmatic stream serialisation and read the state before the
+   * preceding kernel in the stream has finished: set only when no kernel still
+   * running ahead of this call writes initial_state (in a decode step the state of
+   * layer l is written only by layer l's previous step).  q/k/v/g/beta are always
+   * read after the preceding kernel finishes.  Pays off when the preceding kernel
+   * is another GDN step. */
+  OQ_GDN_STATE_PREFETCH = 1
+};
+
 /* Static description of an oq_status value. */
 const char* oq_status_string(int status);
 /* Detail of the last failing call on this host thread ("" when none). */
@@ -186,6 +197,7 @@ int oq_gather_dequant_int4(
  * Per token: S *= exp(g); kv = S^T k; delta = beta (v - kv); S += k delta^T;
  * o = S^T (scale q).  With use_qk_l2norm, q and k are first scaled by
  * 1/sqrt(sum(x^2) + 1e-6).  k_dim = v_dim = 128 in this build.
+ * flags: OQ_GDN_STATE_PREFETCH or 0.
  */
 int oq_gdn_recurrent(
     const void* q, const void* k, const void* v, int qkv_dtype,
@@ -195,7 +207,7 @@ int oq_gdn_recurrent(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, void* stream);
+    float scale, int use_qk_l2norm, int flags, void* stream);
 
 /* Chunked gated delta rule (GDN prefill) on the tensor cores (tcgen05 / TMEM).
  * Replaces the hook chunk_gated_delta_rule (transformers models/qwen3_5/modeling_qwen3_5.py:466-476;

@@ -44,7 +44,7 @@ SIGNATURES = {
     "oq_lse_merge": (i32, [p, p, i64, i64, i64, p, i32, p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
-                               p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, p]),
+                               p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p]),
     "oq_gdn_chunk_fwd": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i64, p, p]),
 }

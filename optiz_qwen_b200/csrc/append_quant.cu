@@ -56,6 +56,8 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.y;
+  pdl_wait();
+  pdl_allow_next();
   const int32_t start = p.seq_lens[b];
   const int64_t jobs = p.num_kv_heads * p.num_new * 2;
   constexpr int kHeadDim = EPL * 32;
@@ -136,6 +138,8 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
 }
 
 __global__ void advance_kernel(int32_t* seq_lens, int64_t batch, int32_t delta) {
+  pdl_wait();
+  pdl_allow_next();
   int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < batch) seq_lens[i] += delta;
 }
@@ -143,9 +147,9 @@ __global__ void advance_kernel(int32_t* seq_lens, int64_t batch, int32_t delta) 
 template <typename T, int EPL>
 void launch_append(const AppendParams& p, bool vec, dim3 grid, cudaStream_t s) {
   if (vec) {
-    append_quant_kernel<T, EPL, true><<<grid, kWarps * 32, 0, s>>>(p);
+    launch_plain(append_quant_kernel<T, EPL, true>, grid, dim3(kWarps * 32), 0, s, p);
   } else {
-    append_quant_kernel<T, EPL, false><<<grid, kWarps * 32, 0, s>>>(p);
+    launch_plain(append_quant_kernel<T, EPL, false>, grid, dim3(kWarps * 32), 0, s, p);
   }
 }
 
@@ -167,8 +171,8 @@ extern "C" int oq_advance_seq_lens(int32_t* seq_lens, int64_t batch, int32_t del
   if (seq_lens == nullptr || batch < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "advance_seq_lens: bad arguments");
   if (batch == 0) return ok();
   const int threads = 256;
-  advance_kernel<<<unsigned((batch + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      seq_lens, batch, delta);
+  launch_plain(advance_kernel, dim3(unsigned((batch + threads - 1) / threads)), dim3(threads), 0,
+             static_cast<cudaStream_t>(stream), seq_lens, batch, int32_t(delta));
   return check_launch("advance_seq_lens");
 }
 

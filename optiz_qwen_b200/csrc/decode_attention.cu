@@ -178,11 +178,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int64_t b = blockIdx.z;
   const int G = p.group;
 
+  pdl_wait();  // (one long wave: the successor is allowed to launch only after the page loop)
   const int len = max(p.seq_lens[b], 0);
   const int len_pages = (len + kPage - 1) / kPage;
   const int npages_b = int(min(int64_t(len_pages), p.max_pages));
   const int nsplit_b = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
-  if (split >= nsplit_b) return;
+  if (split >= nsplit_b) {
+    pdl_allow_next();
+    return;
+  }
   if (len_pages > p.max_pages && tid == 0 && split == 0) report(p.status, OQ_DEV_OVERFLOW);
   const int page_begin = split * p.pages_per_split;
   const int n = max(0, min(npages_b, page_begin + p.pages_per_split) - page_begin);
@@ -511,6 +515,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   }
 
+  pdl_allow_next();
   if (aborted) {
     // Leave no copy in flight before the CTA exits: wait (bounded) for every issued stage.
     if (tid == 0) {
@@ -683,6 +688,8 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
   const int G = p.group;
   const int64_t b = unit / p.num_kv_heads;
   const int kvh = int(unit - b * p.num_kv_heads);
+  pdl_wait();
+  pdl_allow_next();
   const int len = max(p.seq_lens[b], 0);
   const int npages_b = int(min(int64_t((len + kPage - 1) / kPage), p.max_pages));
   const int nsplit = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
@@ -885,13 +892,13 @@ extern "C" int oq_decode_attn_int4_paged(
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  kernel<<<grid, kThreads, kSmemBytes, s>>>(tmap, p);
+  launch_plain(kernel, grid, dim3(kThreads), kSmemBytes, s, tmap, p);
   if (p.defer_merge) {
     const dim3 mgrid((unsigned)units, (unsigned)group);
     if (dtype == OQ_BF16) {
-      split_merge_kernel<__nv_bfloat16><<<mgrid, kMergeThreads, 0, s>>>(p);
+      launch_plain(split_merge_kernel<__nv_bfloat16>, mgrid, dim3(kMergeThreads), 0, s, p);
     } else {
-      split_merge_kernel<__half><<<mgrid, kMergeThreads, 0, s>>>(p);
+      launch_plain(split_merge_kernel<__half>, mgrid, dim3(kMergeThreads), 0, s, p);
     }
   }
   return check_launch("decode_attn_int4_paged");

@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+  pdl_wait();  // (one long wave: the successor is allowed to launch only after the chunk loop)
 
   // Load schedule (identical in every thread; only thread 0 issues).
   int kq_issued[2] = {0, 0}, kq_waited[2] = {0, 0}, v_issued = 0, v_waited = 0;
@@ -662,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   }
 
+  pdl_allow_next();
   if (aborted) {
     if (tid == 0) report(p.status, OQ_DEV_TIMEOUT);
     // Let every issued MMA and copy land before TMEM and shared memory go away.
@@ -772,6 +774,7 @@ extern "C" int oq_gdn_chunk_fwd(
   p.l2norm = use_qk_l2norm;
   p.status = device_status;
   dim3 grid((unsigned)num_heads, (unsigned)batch);
-  gdn_chunk_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(maps[0], maps[1], maps[2], p);
+  launch_plain(gdn_chunk_kernel, grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), maps[0], maps[1],
+             maps[2], p);
   return check_launch("gdn_chunk_fwd");
 }

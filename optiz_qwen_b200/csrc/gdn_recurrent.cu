@@ -34,6 +34,7 @@ struct GdnParams {
   int64_t seq_len, num_heads;
   float scale;
   int l2norm;
+  int prefetch_state;  // read the state before waiting for the preceding kernel
 };
 
 template <typename T>
@@ -54,6 +55,10 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
 
   float S[kRowsPerThread][4];
   const int64_t state_off = ((b * H + h) * kDk) * kDv + v0 + 4 * cg;
+  // The state is the dominant traffic.  With prefetch_state the caller guarantees no
+  // kernel still running ahead of this one writes it, so its loads are issued before
+  // the dependency wait and overlap the previous kernel's tail.
+  if (!p.prefetch_state) pdl_wait();
   if (p.s_in != nullptr) {
 #pragma unroll
     for (int i = 0; i < kRowsPerThread; ++i) {
@@ -67,6 +72,8 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
 #pragma unroll
     for (int i = 0; i < kRowsPerThread; ++i) S[i][0] = S[i][1] = S[i][2] = S[i][3] = 0.0f;
   }
+  if (p.prefetch_state) pdl_wait();
+  pdl_allow_next();
 
   for (int64_t t = 0; t < p.seq_len; ++t) {
     const T* qrow = static_cast<const T*>(p.q) + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
@@ -167,6 +174,15 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
   }
 }
 
+// Early (programmatic) launch only when the caller allows the state prefetch.
+void launch_gdn(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
+  if (p.prefetch_state) {
+    launch_pdl(kernel, grid, dim3(kThreads), 0, s, p);
+  } else {
+    launch_plain(kernel, grid, dim3(kThreads), 0, s, p);
+  }
+}
+
 }  // namespace
 }  // namespace oq
 
@@ -178,7 +194,7 @@ extern "C" int oq_gdn_recurrent(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, void* stream) {
+    float scale, int use_qk_l2norm, int flags, void* stream) {
   using namespace oq;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
@@ -212,12 +228,13 @@ extern "C" int oq_gdn_recurrent(
   p.num_heads = num_heads;
   p.scale = scale;
   p.l2norm = use_qk_l2norm;
+  p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (qkv_dtype) {
-    case OQ_F32: gdn_recurrent_kernel<float><<<grid, kThreads, 0, s>>>(p); break;
-    case OQ_F16: gdn_recurrent_kernel<__half><<<grid, kThreads, 0, s>>>(p); break;
-    default: gdn_recurrent_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(p); break;
+    case OQ_F32: launch_gdn(gdn_recurrent_kernel<float>, grid, s, p); break;
+    case OQ_F16: launch_gdn(gdn_recurrent_kernel<__half>, grid, s, p); break;
+    default: launch_gdn(gdn_recurrent_kernel<__nv_bfloat16>, grid, s, p); break;
   }
   return check_launch("gdn_recurrent");
 }

@@ -15,6 +15,8 @@ __global__ void lse_merge_kernel(const float* __restrict__ part_out, const float
                                  float* __restrict__ out_lse) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_allow_next();
   if (row >= rows) return;
   float m = -INFINITY;
   for (int64_t i = 0; i < num_parts; ++i) m = fmaxf(m, part_lse[i * rows + row]);
@@ -45,6 +47,8 @@ __global__ void gather_dequant_kernel(const uint8_t* __restrict__ kv_codes, cons
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int64_t total = batch * num_kv_heads * max_len * 2;
+  pdl_wait();
+  pdl_allow_next();
   if (row >= total) return;
   const int kv = int(row & 1);
   int64_t rest = row >> 1;
@@ -93,16 +97,16 @@ extern "C" int oq_lse_merge(const float* part_out, const float* part_lse, int64_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case OQ_F32:
-      lse_merge_kernel<float><<<blocks, warps * 32, 0, s>>>(part_out, part_lse, num_parts, rows, head_dim,
-                                                            static_cast<float*>(out), out_lse);
+      launch_plain(lse_merge_kernel<float>, dim3(blocks), dim3(warps * 32), 0, s, part_out, part_lse, num_parts, rows,
+                 head_dim, static_cast<float*>(out), out_lse);
       break;
     case OQ_F16:
-      lse_merge_kernel<__half><<<blocks, warps * 32, 0, s>>>(part_out, part_lse, num_parts, rows, head_dim,
-                                                             static_cast<__half*>(out), out_lse);
+      launch_plain(lse_merge_kernel<__half>, dim3(blocks), dim3(warps * 32), 0, s, part_out, part_lse, num_parts, rows,
+                 head_dim, static_cast<__half*>(out), out_lse);
       break;
     default:
-      lse_merge_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, s>>>(part_out, part_lse, num_parts, rows, head_dim,
-                                                                    static_cast<__nv_bfloat16*>(out), out_lse);
+      launch_plain(lse_merge_kernel<__nv_bfloat16>, dim3(blocks), dim3(warps * 32), 0, s, part_out, part_lse, num_parts,
+                 rows, head_dim, static_cast<__nv_bfloat16*>(out), out_lse);
   }
   return check_launch("lse_merge");
 }
@@ -129,9 +133,9 @@ extern "C" int oq_gather_dequant_int4(
   if (blocks > 0x7fffffff) return fail(OQ_ERR_UNSUPPORTED, "gather_dequant_int4: too many rows");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define OQ_GATHER(T)                                                                                             \
-  gather_dequant_kernel<T><<<unsigned(blocks), warps * 32, 0, s>>>(                                               \
-      kv_codes, kv_meta, num_pages, page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, \
-      num_kv_heads, head_dim, max_len, static_cast<T*>(keys), static_cast<T*>(values), device_status)
+  launch_plain(gather_dequant_kernel<T>, dim3(unsigned(blocks)), dim3(warps * 32), 0, s, kv_codes, kv_meta, num_pages, \
+             page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_kv_heads, head_dim,  \
+             max_len, static_cast<T*>(keys), static_cast<T*>(values), device_status)
   switch (dtype) {
     case OQ_F32: OQ_GATHER(float); break;
     case OQ_F16: OQ_GATHER(__half); break;

@@ -62,4 +62,4 @@ extern "C" const char* oq_status_string(int status) {
 
 extern "C" const char* oq_last_error(void) { return g_last_error; }
 
-extern "C" int oq_abi_version(void) { return 1; }
+extern "C" int oq_abi_version(void) { return 2; }

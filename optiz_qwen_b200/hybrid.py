@@ -212,6 +212,7 @@ class HybridDecodeStack:
     def step_device(self, kinds=("attn", "gdn", "append")) -> None:
         s = self.shape
         scaling = s.head_dim ** -0.5
+        prev = None  # (kind, index) of the previous launch in this step
         for kind, i in self.order:
             if kind == "attn":
                 layer = self.attn[i]
@@ -219,13 +220,21 @@ class HybridDecodeStack:
                 if "append" in kinds:
                     cabi.append_quant_int4(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
                                            advance=not self.hold_context)
+                    prev = ("append", i)
                 if "attn" in kinds:
                     cabi.decode_attention_int4(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
                                                out=layer.out, workspace=layer.workspace)
+                    prev = ("attn", i)
             elif "gdn" in kinds:
                 layer = self.gdn[i]
+                # A layer's state is written only by its own launch one step earlier, so when the
+                # launch right before this one is another layer's GDN step, this one may start
+                # early and load its state during that step's tail.
+                chained = prev is not None and prev[0] == "gdn" and prev[1] != i
                 cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
-                                   final_state=layer.state, out=layer.out, use_qk_l2norm=True)
+                                   final_state=layer.state, out=layer.out, use_qk_l2norm=True,
+                                   prefetch_state=chained)
+                prev = ("gdn", i)
 
     def capture(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
         """Capture one step's launches in a CUDA graph (after one eager warm-up step)."""

@@ -1,0 +1,60 @@
+"""One decode step of the hybrid stack (the graph bench.py times), against the oracle.
+
+An 8-layer stack (6 GDN + 2 full-attention layers, 3:1 as in Qwen3.5) over three
+ragged sequences: after one graph replay, every GDN layer's state and output and
+every attention layer's output match the oracle run on the same inputs, and the new
+token's codes in each attention cache are the reference quantiser's.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn as ogdn
+from oracle import kv_quant as kq
+from tests._util import assert_attn_close, assert_gdn_close, oracle_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def test_graph_step_matches_oracle():
+    from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
+
+    shape = HybridShape(batch=3, context=[70, 130, 5], num_layers=8)
+    stack = HybridDecodeStack(shape, device="cuda", seed=3)
+    stack.fill_inputs()
+    states0 = [layer.state.cpu().numpy().copy() for layer in stack.gdn]
+    graph = stack.capture()          # (the capture runs one eager step first)
+    # restore the states the eager step advanced, then run the captured step once
+    for layer, s0 in zip(stack.gdn, states0):
+        layer.state.copy_(torch.from_numpy(s0))
+    graph.replay()
+    torch.cuda.synchronize()
+
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    for layer, s0 in zip(stack.gdn, states0):
+        ro, rs = ogdn.recurrent_gated_delta_rule(f(layer.q), f(layer.k), f(layer.v), f(layer.g), f(layer.beta), s0,
+                                                 True, True)
+        assert_gdn_close(layer.state.cpu().numpy(), rs)
+        got = f(layer.out)
+        assert np.all(np.abs(got - ro) <= 2.0 ** -8 * np.abs(ro) + 1e-4 * np.abs(ro).max())
+
+    for layer in stack.attn:
+        p = layer.paged
+        lens = layer.attend_lens.cpu().numpy()
+        table = p.block_table.cpu().numpy()
+        cache = kq.PagedKvOracle(p.pool.kv_codes.shape[0], shape.num_kv_heads, shape.head_dim, shape.page_size,
+                                 table, lens)
+        cache.kv_codes[...] = p.pool.kv_codes.cpu().numpy()
+        cache.kv_meta[...] = p.pool.kv_meta.cpu().numpy()
+        # the appended token (slot = context) holds the reference quantiser's codes of k / v
+        kp, ks, km = kq.quantize_tokens_int4(f(layer.k))
+        for b, pos in enumerate(shape.lengths):
+            page, slot = table[b, pos // shape.page_size], pos % shape.page_size
+            assert np.array_equal(cache.kv_codes[page, :, 0, slot], kp[b, :, 0])
+            assert np.array_equal(cache.kv_meta[page, :, 0, slot], ks[b, :, 0])
+            assert np.array_equal(cache.kv_meta[page, :, 1, slot], km[b, :, 0])
+        ref, _ = oracle_attention(cache, f(layer.q), shape.head_dim ** -0.5)
+        assert_attn_close(f(layer.out), ref)
