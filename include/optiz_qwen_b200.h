@@ -209,6 +209,40 @@ int oq_gdn_recurrent(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int flags, void* stream);
 
+/* One GDN decode token with the layer's causal conv1d update fused in front of it.
+ * Replaces, for the decode branch of Qwen3_5GatedDeltaNet.forward
+ * (transformers models/qwen3_5/modeling_qwen3_5.py:454-520), the pair
+ * causal_conv1d_update (:210-225) + recurrent_gated_delta_rule, reading the
+ * projection output directly.
+ * qkv [batch, C] in qkv_dtype (row stride qkv_stride_b, channels contiguous), with
+ * C = num_heads * (2 k_dim + v_dim) ordered q heads | k heads | v heads;
+ * conv_state [batch, C, conv_width] contiguous in qkv_dtype, updated in place;
+ * conv_weight [C, conv_kernel_size], conv_bias [C] or NULL, in conv_w_dtype.
+ * q, k, v = silu(conv) rounded to qkv_dtype, then the recurrent step of
+ * oq_gdn_recurrent (same state / out / flags contract, seq_len = 1). */
+int oq_gdn_conv_step(
+    const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
+    void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
+    int64_t conv_width, int64_t conv_kernel_size,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, void* stream);
+
+/* Causal depthwise conv1d update (the GDN layer's short convolution).
+ * Replaces the hook causal_conv1d_update (transformers torch_causal_conv1d_update,
+ * models/qwen3_5/modeling_qwen3_5.py:210-225; causal-conv1d 1.6.2).
+ * x [batch, channels, seq_len] with element strides (b, c, t), in dtype;
+ * conv_state [batch, channels, state_width] contiguous in dtype, updated in place to
+ * the last state_width inputs of [state | x]; weight [channels, kernel_size] and bias
+ * [channels] (or NULL) in w_dtype; out [batch, channels, seq_len] contiguous in dtype:
+ * out[t] = act(bias + sum_k weight[k] * [state | x][state_width + t - kernel_size + 1 + k]),
+ * act = silu when silu != 0.  1 <= kernel_size - 1 <= state_width <= 8. */
+int oq_causal_conv1d_update(const void* x, int dtype, int64_t x_stride_b, int64_t x_stride_c, int64_t x_stride_t,
+                            void* conv_state, const void* weight, const void* bias, int w_dtype, void* out,
+                            int64_t batch, int64_t channels, int64_t seq_len, int64_t state_width,
+                            int64_t kernel_size, int silu, void* stream);
+
 /* Chunked gated delta rule (GDN prefill) on the tensor cores (tcgen05 / TMEM).
  * Replaces the hook chunk_gated_delta_rule (transformers models/qwen3_5/modeling_qwen3_5.py:466-476;
  * torch_chunk_gated_delta_rule :234-311; fla chunk_gated_delta_rule, fla/ops/gated_delta_rule/chunk.py:365).

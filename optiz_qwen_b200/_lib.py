@@ -45,6 +45,9 @@ SIGNATURES = {
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p]),
+    "oq_causal_conv1d_update": (i32, [p, i32, i64, i64, i64, p, p, p, i32, p, i64, i64, i64, i64, i64, i32, p]),
+    "oq_gdn_conv_step": (i32, [p, i32, i64, p, p, p, i32, i64, i64, p, i32, p, i32, p, p, p, i64, i64, i64, i64,
+                               f32, i32, i32, p]),
     "oq_gdn_chunk_fwd": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i64, p, p]),
 }

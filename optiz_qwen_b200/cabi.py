@@ -225,6 +225,63 @@ GDN_STATE_PREFETCH = 1
 CHUNK_SIZE = 64
 
 
+def causal_conv1d_update(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
+                         bias: torch.Tensor | None = None, silu: bool = True,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal depthwise conv1d update: x ``[B, C, T]``, conv_state ``[B, C, W]`` (updated in place),
+    weight ``[C, K]``; returns ``[B, C, T]`` in x's dtype."""
+    require_cuda(x, conv_state, weight, bias)
+    if x.dim() != 3 or conv_state.dim() != 3 or conv_state.shape[:2] != x.shape[:2]:
+        raise ValueError("x must be [B, C, T] and conv_state [B, C, W]")
+    if conv_state.dtype != x.dtype or not conv_state.is_contiguous():
+        raise ValueError("conv_state must be contiguous in x's dtype")
+    bsz, ch, t = x.shape
+    weight = weight.reshape(ch, -1).contiguous()
+    if bias is not None:
+        bias = bias.to(weight.dtype).contiguous()
+    if out is None:
+        out = torch.empty((bsz, ch, t), dtype=x.dtype, device=x.device)
+    call("oq_causal_conv1d_update", ptr(x), dtype_code(x.dtype), x.stride(0), x.stride(1), x.stride(2),
+         ptr(conv_state), ptr(weight), ptr(bias), dtype_code(weight.dtype), ptr(out), bsz, ch, t,
+         conv_state.shape[-1], weight.shape[-1], int(silu), stream_ptr(x.device))
+    return out
+
+
+def gdn_conv_step(qkv: torch.Tensor, conv_state: torch.Tensor, conv_weight: torch.Tensor,
+                  conv_bias: torch.Tensor | None, g: torch.Tensor, beta: torch.Tensor, *, num_heads: int,
+                  scale: float | None = None, initial_state: torch.Tensor | None = None,
+                  final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  use_qk_l2norm: bool = True, prefetch_state: bool = False) -> torch.Tensor:
+    """One GDN decode token with the causal conv1d update fused in: qkv ``[B, C]`` (the projection
+    output, q heads | k heads | v heads), conv_state ``[B, C, W]`` and the recurrent state are updated
+    in place; returns ``out`` ``[B, 1, H, 128]``."""
+    require_cuda(qkv, conv_state, conv_weight, conv_bias, g, beta, initial_state, final_state)
+    dk = dv = 128
+    bsz = qkv.shape[0]
+    ch = num_heads * (2 * dk + dv)
+    if qkv.dim() != 2 or qkv.shape[1] != ch or qkv.stride(1) != 1:
+        raise ValueError(f"qkv must be [B, {ch}] with contiguous channels")
+    if conv_state.shape[:2] != (bsz, ch) or conv_state.dtype != qkv.dtype or not conv_state.is_contiguous():
+        raise ValueError("conv_state must be contiguous [B, C, W] in qkv's dtype")
+    conv_weight = conv_weight.reshape(ch, -1).contiguous()
+    if conv_bias is not None:
+        conv_bias = conv_bias.to(conv_weight.dtype).contiguous()
+    g, beta = g.contiguous(), beta.contiguous()
+    for s in (initial_state, final_state):
+        if s is not None and (s.dtype != torch.float32 or tuple(s.shape) != (bsz, num_heads, dk, dv)
+                              or not s.is_contiguous()):
+            raise ValueError("states must be contiguous fp32 [B, H, Dk, Dv]")
+    if out is None:
+        out = torch.empty((bsz, 1, num_heads, dv), dtype=qkv.dtype, device=qkv.device)
+    scale = dk ** -0.5 if scale is None else float(scale)
+    call("oq_gdn_conv_step", ptr(qkv), dtype_code(qkv.dtype), qkv.stride(0), ptr(conv_state), ptr(conv_weight),
+         ptr(conv_bias), dtype_code(conv_weight.dtype), conv_state.shape[-1], conv_weight.shape[-1],
+         ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype), ptr(initial_state), ptr(final_state),
+         ptr(out), bsz, num_heads, dk, dv, float(scale), int(use_qk_l2norm),
+         GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(qkv.device))
+    return out
+
+
 def gdn_chunk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,

@@ -35,9 +35,57 @@ struct GdnParams {
   float scale;
   int l2norm;
   int prefetch_state;  // read the state before waiting for the preceding kernel
+  // fused causal conv1d update (decode, T = 1): q, k, v = silu(conv(state | x)) of the
+  // projection output x = qkv [B, C] (channels: q heads, k heads, v heads)
+  const void* qkv;
+  int64_t qkv_sb;
+  void* conv_state;  // [B, C, W] in T
+  const void* conv_w;  // [C, K]
+  const void* conv_b;  // [C] or null
+  int conv_w_dtype, conv_width, conv_ksize;
+  int64_t conv_channels;
 };
 
+constexpr int kConvMaxWidth = 8;
+
+// One channel of the causal conv1d update for the single new token: the output
+// (rounded to the input dtype, as the unfused layer hands it on) and the shifted
+// window, which becomes the channel's new state.
 template <typename T>
+__device__ __forceinline__ float conv_channel(const GdnParams& p, int64_t b, int64_t c, float (&hist)[kConvMaxWidth]) {
+  const int W = p.conv_width, K = p.conv_ksize;
+  const T* st = static_cast<const T*>(p.conv_state) + (b * p.conv_channels + c) * W;
+  const float x = to_float<T>(static_cast<const T*>(p.qkv)[b * p.qkv_sb + c]);
+#pragma unroll
+  for (int j = 0; j < kConvMaxWidth; ++j) {
+    const float nxt = j + 1 < W ? to_float<T>(st[j + 1 < kConvMaxWidth ? j + 1 : j]) : x;
+    hist[j] = j < W ? nxt : 0.0f;
+  }
+  float acc = p.conv_b != nullptr ? load_as_float(p.conv_b, p.conv_w_dtype, c) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < kConvMaxWidth; ++j) {
+#pragma unroll
+    for (int k = 0; k < kConvMaxWidth; ++k) {
+      if (k < K && j == W - K + k) acc = fmaf(load_as_float(p.conv_w, p.conv_w_dtype, c * K + k), hist[j], acc);
+    }
+  }
+  return to_float<T>(from_float<T>(acc / (1.0f + expf(-acc))));
+}
+
+template <typename T>
+__device__ __forceinline__ void conv_store(const GdnParams& p, int64_t b, int64_t c, const float (&hist)[kConvMaxWidth]) {
+  T* st = static_cast<T*>(p.conv_state) + (b * p.conv_channels + c) * p.conv_width;
+#pragma unroll
+  for (int j = 0; j < kConvMaxWidth; ++j) {
+    if (j < p.conv_width) st[j] = from_float<T>(hist[j]);
+  }
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.aligned;\nbarrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
+template <typename T, bool kConv>
 __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
   __shared__ float q_s[kDk], k_s[kDk], v_s[kCols];
   __shared__ float red_kv[4][kCols], red_o[4][kCols];
@@ -79,11 +127,31 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
     const T* qrow = static_cast<const T*>(p.q) + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
     const T* krow = static_cast<const T*>(p.k) + b * p.ks[0] + t * p.ks[1] + h * p.ks[2];
     const T* vrow = static_cast<const T*>(p.v) + b * p.vs[0] + t * p.vs[1] + h * p.vs[2];
-    const float qv = to_float<T>(qrow[tid]);
-    const float kvv = to_float<T>(krow[tid]);
+    float qv, kvv;
+    if constexpr (kConv) {
+      // q / k channels of this head and v channels of this slice through the conv; the
+      // four slice CTAs of a head form a cluster: all read the old state, then rank 0
+      // writes the q / k state and every CTA its own v channels.
+      float hq[kConvMaxWidth], hk[kConvMaxWidth], hv[kConvMaxWidth];
+      const int64_t ch_q = h * kDk + tid, ch_k = H * kDk + h * kDk + tid, ch_v = 2 * H * kDk + h * kDv + v0 + tid;
+      qv = conv_channel<T>(p, b, ch_q, hq);
+      kvv = conv_channel<T>(p, b, ch_k, hk);
+      float vv = 0.0f;
+      if (tid < kCols) vv = conv_channel<T>(p, b, ch_v, hv);
+      if (tid < kCols) v_s[tid] = vv;
+      cluster_sync();
+      if (blockIdx.x == 0) {
+        conv_store<T>(p, b, ch_q, hq);
+        conv_store<T>(p, b, ch_k, hk);
+      }
+      if (tid < kCols) conv_store<T>(p, b, ch_v, hv);
+    } else {
+      qv = to_float<T>(qrow[tid]);
+      kvv = to_float<T>(krow[tid]);
+      if (tid < kCols) v_s[tid] = to_float<T>(vrow[v0 + tid]);
+    }
     q_s[tid] = qv;
     k_s[tid] = kvv;
-    if (tid < kCols) v_s[tid] = to_float<T>(vrow[v0 + tid]);
     if (p.l2norm) {
       float sq = qv * qv, sk = kvv * kvv;
 #pragma unroll
@@ -183,6 +251,24 @@ void launch_gdn(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnP
   }
 }
 
+// The fused conv variant runs the four column slices of a head as one cluster.
+cudaError_t launch_gdn_conv(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kDv / kCols;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = p.prefetch_state ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 }  // namespace
 }  // namespace oq
 
@@ -232,9 +318,68 @@ extern "C" int oq_gdn_recurrent(
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (qkv_dtype) {
-    case OQ_F32: launch_gdn(gdn_recurrent_kernel<float>, grid, s, p); break;
-    case OQ_F16: launch_gdn(gdn_recurrent_kernel<__half>, grid, s, p); break;
-    default: launch_gdn(gdn_recurrent_kernel<__nv_bfloat16>, grid, s, p); break;
+    case OQ_F32: launch_gdn(gdn_recurrent_kernel<float, false>, grid, s, p); break;
+    case OQ_F16: launch_gdn(gdn_recurrent_kernel<__half, false>, grid, s, p); break;
+    default: launch_gdn(gdn_recurrent_kernel<__nv_bfloat16, false>, grid, s, p); break;
   }
   return check_launch("gdn_recurrent");
+}
+
+extern "C" int oq_gdn_conv_step(
+    const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
+    void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
+    int64_t conv_width, int64_t conv_kernel_size,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, void* stream) {
+  using namespace oq;
+  if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype) || !valid_dtype(conv_w_dtype)) {
+    return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: unknown dtype");
+  }
+  if (k_dim != kDk || v_dim != kDv) return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: k_dim = v_dim = 128 required");
+  if (conv_kernel_size < 1 || conv_width < conv_kernel_size - 1 || conv_width < 1 || conv_width > kConvMaxWidth ||
+      conv_kernel_size > kConvMaxWidth) {
+    return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: need 1 <= kernel_size - 1 <= width <= %d", kConvMaxWidth);
+  }
+  if (batch < 0 || num_heads <= 0) return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_conv_step: bad sizes");
+  if (batch == 0) return ok();
+  if (batch > 65535 || num_heads > 65535) return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: grid too large");
+  if (!qkv || !conv_state || !conv_weight || !g || !beta || !out) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_conv_step: null pointer");
+  }
+  if ((initial_state && reinterpret_cast<uintptr_t>(initial_state) % 16) ||
+      (final_state && reinterpret_cast<uintptr_t>(final_state) % 16)) {
+    return fail(OQ_ERR_MISALIGNED, "gdn_conv_step: state must be 16-byte aligned");
+  }
+  GdnParams p = {};
+  p.g = g;
+  p.beta = beta;
+  p.g_dtype = g_dtype;
+  p.beta_dtype = beta_dtype;
+  p.s_in = initial_state;
+  p.s_out = final_state;
+  p.out = out;
+  p.seq_len = 1;
+  p.num_heads = num_heads;
+  p.scale = scale;
+  p.l2norm = use_qk_l2norm;
+  p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
+  p.qkv = qkv;
+  p.qkv_sb = qkv_stride_b;
+  p.conv_state = conv_state;
+  p.conv_w = conv_weight;
+  p.conv_b = conv_bias;
+  p.conv_w_dtype = conv_w_dtype;
+  p.conv_width = int(conv_width);
+  p.conv_ksize = int(conv_kernel_size);
+  p.conv_channels = num_heads * (2 * kDk + kDv);
+  dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (qkv_dtype) {
+    case OQ_F32: launch_gdn_conv(gdn_recurrent_kernel<float, true>, grid, s, p); break;
+    case OQ_F16: launch_gdn_conv(gdn_recurrent_kernel<__half, true>, grid, s, p); break;
+    default: launch_gdn_conv(gdn_recurrent_kernel<__nv_bfloat16, true>, grid, s, p); break;
+  }
+  return check_launch("gdn_conv_step");
 }

@@ -104,6 +104,23 @@ def chunk_gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g:
     return out, final
 
 
+def causal_conv1d_update(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
+                         bias: torch.Tensor | None = None, activation: str | None = None, cache_seqlens=None,
+                         conv_state_indices=None, **kwargs) -> torch.Tensor:
+    """The layer's short convolution on the decode path (causal-conv1d 1.6.2 ``causal_conv1d_update``
+    signature; transformers torch_causal_conv1d_update, modeling_qwen3_5.py:210-225): x ``[B, C, T]``,
+    conv_state ``[B, C, W]`` updated in place, weight ``[C, K]``; activation None or "silu"/"swish"."""
+    if cache_seqlens is not None or conv_state_indices is not None:
+        raise NotImplementedError("cache_seqlens / conv_state_indices are not supported")
+    if activation not in (None, "silu", "swish"):
+        raise NotImplementedError(f"activation {activation!r} is not supported")
+    squeeze = x.dim() == 2
+    if squeeze:
+        x = x.unsqueeze(-1)
+    out = cabi.causal_conv1d_update(x, conv_state, weight, bias, silu=activation is not None)
+    return out.squeeze(-1) if squeeze else out
+
+
 def install_gdn_fastpath(model) -> int:
     """Bind the hooks on every Gated-DeltaNet module of ``model``; returns how many were patched.
 
@@ -115,5 +132,6 @@ def install_gdn_fastpath(model) -> int:
         if "GatedDeltaNet" in type(module).__name__ and hasattr(module, "recurrent_gated_delta_rule"):
             module.recurrent_gated_delta_rule = fused_recurrent_gated_delta_rule
             module.chunk_gated_delta_rule = chunk_gated_delta_rule
+            module.causal_conv1d_update = causal_conv1d_update
             patched += 1
     return patched

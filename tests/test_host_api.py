@@ -199,17 +199,32 @@ def test_attention_launchers_error_behaviour():
 
 def test_install_gdn_fastpath_binds_hooks():
     from optiz_qwen_b200.gdn import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule, install_gdn_fastpath
+    from optiz_qwen_b200.gdn.gated_delta_rule import causal_conv1d_update
 
     class Qwen3_5GatedDeltaNet(torch.nn.Module):
         def __init__(self):
             super().__init__()
             self.recurrent_gated_delta_rule = None
             self.chunk_gated_delta_rule = None
+            self.causal_conv1d_update = None
 
     model = torch.nn.Sequential(Qwen3_5GatedDeltaNet(), torch.nn.Linear(2, 2), Qwen3_5GatedDeltaNet())
     assert install_gdn_fastpath(model) == 2
     assert model[0].recurrent_gated_delta_rule is fused_recurrent_gated_delta_rule
     assert model[2].chunk_gated_delta_rule is chunk_gated_delta_rule
+    assert model[2].causal_conv1d_update is causal_conv1d_update
+
+
+def test_conv_hook_rejects_unsupported_arguments():
+    from optiz_qwen_b200.gdn.gated_delta_rule import causal_conv1d_update
+
+    x, st, w = torch.zeros(1, 4, 1), torch.zeros(1, 4, 4), torch.zeros(4, 4)
+    with pytest.raises(NotImplementedError):
+        causal_conv1d_update(x, st, w, None, "gelu")
+    with pytest.raises(NotImplementedError):
+        causal_conv1d_update(x, st, w, None, "silu", cache_seqlens=torch.zeros(1))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        causal_conv1d_update(x, st, w, None, "silu")
 
 
 def test_workspace_split_heuristic_matches_the_c_side():
