@@ -51,6 +51,9 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["hybrid", "serving", "longctx", "prefill"], default="hybrid")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--conv", choices=["separate", "fused"], default=None,
+                    help="hybrid/serving: feed each GDN layer its raw projection output and run its causal conv1d "
+                         "update (separate kernel, or fused into the GDN step)")
     ap.add_argument("--small", action="store_true",
                     help="prefill workload only: a reduced case (B=4, T=8192, 2 layers, 8 decode steps) for ncu captures")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
@@ -178,8 +181,9 @@ def build_stack(args, world, rank, device):
 
     if args.workload == "hybrid":
         shape = HybridShape(batch=64, context=4096)
-        stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1)
-        desc = {"workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
+        stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv)
+        desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+                "workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
                             "INT4 paged KV, page 64, permuted pages), 3:1 interleave, hidden 2048",
                 "batch_per_gpu": 64, "global_batch": 64 * world, "context": 4096, "layers": 24,
@@ -190,8 +194,9 @@ def build_stack(args, world, rank, device):
     shards = shard_by_cost(lengths, world)
     mine = [lengths[i] for i in shards[rank]]
     shape = HybridShape(batch=len(mine), context=mine)
-    stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3)
-    desc = {"workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
+    stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv)
+    desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+            "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
                         "cost across GPUs, 24-layer hybrid hot path", "global_batch": 1024,
             "batch_this_rank": len(mine), "layers": 24, "l2": "no flush: working set far above L2",
             "parallelism": f"sequence-sharded x{world}"}

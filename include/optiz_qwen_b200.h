@@ -217,7 +217,8 @@ int oq_gdn_recurrent(
  * qkv [batch, C] in qkv_dtype (row stride qkv_stride_b, channels contiguous), with
  * C = num_heads * (2 k_dim + v_dim) ordered q heads | k heads | v heads;
  * conv_state [batch, C, conv_width] contiguous in qkv_dtype, updated in place;
- * conv_weight [C, conv_kernel_size], conv_bias [C] or NULL, in conv_w_dtype.
+ * conv_weight [C, conv_kernel_size], conv_bias [C] or NULL, in conv_w_dtype; this fused
+ * form needs conv_kernel_size = conv_width = 4 and conv_w_dtype = qkv_dtype.
  * q, k, v = silu(conv) rounded to qkv_dtype, then the recurrent step of
  * oq_gdn_recurrent (same state / out / flags contract, seq_len = 1). */
 int oq_gdn_conv_step(
@@ -237,7 +238,8 @@ int oq_gdn_conv_step(
  * the last state_width inputs of [state | x]; weight [channels, kernel_size] and bias
  * [channels] (or NULL) in w_dtype; out [batch, channels, seq_len] contiguous in dtype:
  * out[t] = act(bias + sum_k weight[k] * [state | x][state_width + t - kernel_size + 1 + k]),
- * act = silu when silu != 0.  1 <= kernel_size - 1 <= state_width <= 8. */
+ * act = silu when silu != 0.  kernel_size 2..4 with state_width kernel_size - 1 or
+ * kernel_size; w_dtype is dtype or OQ_F32. */
 int oq_causal_conv1d_update(const void* x, int dtype, int64_t x_stride_b, int64_t x_stride_c, int64_t x_stride_t,
                             void* conv_state, const void* weight, const void* bias, int w_dtype, void* out,
                             int64_t batch, int64_t channels, int64_t seq_len, int64_t state_width,

@@ -11,8 +11,6 @@
 namespace oq {
 namespace {
 
-constexpr int kMaxWidth = 8;
-constexpr int kMaxKernel = 8;
 constexpr int kThreads = 256;
 
 struct ConvParams {
@@ -21,56 +19,59 @@ struct ConvParams {
   void* state;    // [B, C, W] contiguous, in x's dtype
   const void* weight;
   const void* bias;
-  int w_dtype;
   void* out;      // [B, C, T] contiguous, in x's dtype
   int64_t batch, channels, seq_len;
-  int width, ksize, silu;
+  int silu;
 };
 
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
-template <typename T>
+// Window W and kernel size K are compile-time so that every load of a thread is
+// unconditional and all of them are in flight together.
+template <typename T, typename TW, int W, int K>
 __global__ void __launch_bounds__(kThreads) conv1d_update_kernel(ConvParams p) {
+  static_assert(K >= 1 && W >= K - 1 && W >= 1, "window must hold K - 1 past inputs");
   const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   pdl_wait();
   pdl_allow_next();
   if (i >= p.batch * p.channels) return;
   const int64_t b = i / p.channels, c = i - b * p.channels;
-  const int W = p.width, K = p.ksize;
   T* st = static_cast<T*>(p.state) + i * W;
-  float hist[kMaxWidth], w[kMaxKernel];
+  const TW* wr = static_cast<const TW*>(p.weight) + c * K;
+  float hist[W], w[K];
 #pragma unroll
-  for (int j = 0; j < kMaxWidth; ++j) hist[j] = j < W ? to_float<T>(st[j]) : 0.0f;
+  for (int j = 0; j < W; ++j) hist[j] = to_float<T>(st[j]);
 #pragma unroll
-  for (int k = 0; k < kMaxKernel; ++k) w[k] = k < K ? load_as_float(p.weight, p.w_dtype, c * K + k) : 0.0f;
-  const float bias = p.bias != nullptr ? load_as_float(p.bias, p.w_dtype, c) : 0.0f;
+  for (int k = 0; k < K; ++k) w[k] = to_float<TW>(wr[k]);
+  const float bias = p.bias != nullptr ? to_float<TW>(static_cast<const TW*>(p.bias)[c]) : 0.0f;
   const T* xr = static_cast<const T*>(p.x) + b * p.xs[0] + c * p.xs[1];
   T* orow = static_cast<T*>(p.out) + i * p.seq_len;
   for (int64_t t = 0; t < p.seq_len; ++t) {
-    const float xt = to_float<T>(xr[t * p.xs[2]]);
     // slide the window: hist holds the W most recent inputs, oldest first
 #pragma unroll
-    for (int j = 0; j < kMaxWidth; ++j) {
-      const float nxt = j + 1 < kMaxWidth ? hist[j + 1] : 0.0f;
-      if (j < W - 1) hist[j] = nxt;
-      if (j == W - 1) hist[j] = xt;
-    }
+    for (int j = 0; j + 1 < W; ++j) hist[j] = hist[j + 1];
+    hist[W - 1] = to_float<T>(xr[t * p.xs[2]]);
     float acc = bias;
 #pragma unroll
-    for (int j = 0; j < kMaxWidth; ++j) {
-      // tap k = j - (W - K) multiplies hist[j] (the K most recent inputs)
-#pragma unroll
-      for (int k = 0; k < kMaxKernel; ++k) {
-        if (k < K && j == W - K + k) acc = fmaf(w[k], hist[j], acc);
-      }
-    }
+    for (int k = 0; k < K; ++k) acc = fmaf(w[k], hist[W - K + k], acc);
     orow[t] = from_float<T>(p.silu ? silu(acc) : acc);
   }
   // the window is the last W of [state | x]: the new state (exact: values round-trip through fp32)
 #pragma unroll
-  for (int j = 0; j < kMaxWidth; ++j) {
-    if (j < W) st[j] = from_float<T>(hist[j]);
+  for (int j = 0; j < W; ++j) st[j] = from_float<T>(hist[j]);
+}
+
+template <typename T, typename TW>
+int launch_conv(const ConvParams& p, int64_t width, int64_t ksize, dim3 grid, cudaStream_t s) {
+#define OQ_CONV(W, K)                                                                          \
+  if (width == W && ksize == K) {                                                              \
+    launch_plain(conv1d_update_kernel<T, TW, W, K>, grid, dim3(kThreads), 0, s, p);           \
+    return OQ_OK;                                                                              \
   }
+  OQ_CONV(4, 4) OQ_CONV(3, 4) OQ_CONV(3, 3) OQ_CONV(2, 3) OQ_CONV(2, 2) OQ_CONV(1, 2)
+#undef OQ_CONV
+  return fail(OQ_ERR_UNSUPPORTED, "causal_conv1d_update: kernel_size must be 2..4 with state_width kernel_size - 1 "
+              "or kernel_size (got %lld, %lld)", (long long)ksize, (long long)width);
 }
 
 }  // namespace
@@ -82,11 +83,10 @@ extern "C" int oq_causal_conv1d_update(const void* x, int dtype, int64_t x_strid
                                        int64_t state_width, int64_t kernel_size, int silu, void* stream) {
   using namespace oq;
   if (!valid_dtype(dtype) || !valid_dtype(w_dtype)) return fail(OQ_ERR_UNSUPPORTED, "causal_conv1d_update: unknown dtype");
-  if (batch < 0 || channels <= 0 || seq_len < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "causal_conv1d_update: bad sizes");
-  if (kernel_size < 1 || kernel_size > kMaxKernel || state_width < kernel_size - 1 || state_width < 1 ||
-      state_width > kMaxWidth) {
-    return fail(OQ_ERR_UNSUPPORTED, "causal_conv1d_update: need 1 <= kernel_size - 1 <= state_width <= %d", kMaxWidth);
+  if (w_dtype != dtype && w_dtype != OQ_F32) {
+    return fail(OQ_ERR_UNSUPPORTED, "causal_conv1d_update: weight/bias must be fp32 or x's dtype");
   }
+  if (batch < 0 || channels <= 0 || seq_len < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "causal_conv1d_update: bad sizes");
   if (batch == 0 || seq_len == 0) return ok();
   if (!x || !conv_state || !weight || !out) return fail(OQ_ERR_INVALID_ARGUMENT, "causal_conv1d_update: null pointer");
   ConvParams p;
@@ -97,21 +97,27 @@ extern "C" int oq_causal_conv1d_update(const void* x, int dtype, int64_t x_strid
   p.state = conv_state;
   p.weight = weight;
   p.bias = bias;
-  p.w_dtype = w_dtype;
   p.out = out;
   p.batch = batch;
   p.channels = channels;
   p.seq_len = seq_len;
-  p.width = int(state_width);
-  p.ksize = int(kernel_size);
   p.silu = silu;
   const int64_t blocks = (batch * channels + kThreads - 1) / kThreads;
   if (blocks > 0x7fffffff) return fail(OQ_ERR_UNSUPPORTED, "causal_conv1d_update: too many channels");
+  const dim3 grid((unsigned)blocks);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st;
+  const bool wf = w_dtype == OQ_F32;
   switch (dtype) {
-    case OQ_F32: launch_plain(conv1d_update_kernel<float>, dim3(unsigned(blocks)), dim3(kThreads), 0, s, p); break;
-    case OQ_F16: launch_plain(conv1d_update_kernel<__half>, dim3(unsigned(blocks)), dim3(kThreads), 0, s, p); break;
-    default: launch_plain(conv1d_update_kernel<__nv_bfloat16>, dim3(unsigned(blocks)), dim3(kThreads), 0, s, p); break;
+    case OQ_F32: st = launch_conv<float, float>(p, state_width, kernel_size, grid, s); break;
+    case OQ_F16:
+      st = wf ? launch_conv<__half, float>(p, state_width, kernel_size, grid, s)
+              : launch_conv<__half, __half>(p, state_width, kernel_size, grid, s);
+      break;
+    default:
+      st = wf ? launch_conv<__nv_bfloat16, float>(p, state_width, kernel_size, grid, s)
+              : launch_conv<__nv_bfloat16, __nv_bfloat16>(p, state_width, kernel_size, grid, s);
   }
+  if (st != OQ_OK) return st;
   return check_launch("causal_conv1d_update");
 }

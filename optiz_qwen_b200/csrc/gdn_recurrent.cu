@@ -41,44 +41,34 @@ struct GdnParams {
   int64_t qkv_sb;
   void* conv_state;  // [B, C, W] in T
   const void* conv_w;  // [C, K]
-  const void* conv_b;  // [C] or null
-  int conv_w_dtype, conv_width, conv_ksize;
+  const void* conv_b;  // [C] or null, in T
   int64_t conv_channels;
 };
 
-constexpr int kConvMaxWidth = 8;
+constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
 
 // One channel of the causal conv1d update for the single new token: the output
 // (rounded to the input dtype, as the unfused layer hands it on) and the shifted
-// window, which becomes the channel's new state.
+// window [state[1..3], x], which becomes the channel's new state.  Every load is
+// unconditional, so all of them are in flight together.
 template <typename T>
-__device__ __forceinline__ float conv_channel(const GdnParams& p, int64_t b, int64_t c, float (&hist)[kConvMaxWidth]) {
-  const int W = p.conv_width, K = p.conv_ksize;
-  const T* st = static_cast<const T*>(p.conv_state) + (b * p.conv_channels + c) * W;
-  const float x = to_float<T>(static_cast<const T*>(p.qkv)[b * p.qkv_sb + c]);
+__device__ __forceinline__ float conv_channel(const GdnParams& p, int64_t b, int64_t c, float (&hist)[kConvWidth]) {
+  const T* st = static_cast<const T*>(p.conv_state) + (b * p.conv_channels + c) * kConvWidth;
+  const T* wr = static_cast<const T*>(p.conv_w) + c * kConvWidth;
 #pragma unroll
-  for (int j = 0; j < kConvMaxWidth; ++j) {
-    const float nxt = j + 1 < W ? to_float<T>(st[j + 1 < kConvMaxWidth ? j + 1 : j]) : x;
-    hist[j] = j < W ? nxt : 0.0f;
-  }
-  float acc = p.conv_b != nullptr ? load_as_float(p.conv_b, p.conv_w_dtype, c) : 0.0f;
+  for (int j = 0; j + 1 < kConvWidth; ++j) hist[j] = to_float<T>(st[j + 1]);
+  hist[kConvWidth - 1] = to_float<T>(static_cast<const T*>(p.qkv)[b * p.qkv_sb + c]);
+  float acc = p.conv_b != nullptr ? to_float<T>(static_cast<const T*>(p.conv_b)[c]) : 0.0f;
 #pragma unroll
-  for (int j = 0; j < kConvMaxWidth; ++j) {
-#pragma unroll
-    for (int k = 0; k < kConvMaxWidth; ++k) {
-      if (k < K && j == W - K + k) acc = fmaf(load_as_float(p.conv_w, p.conv_w_dtype, c * K + k), hist[j], acc);
-    }
-  }
+  for (int k = 0; k < kConvWidth; ++k) acc = fmaf(to_float<T>(wr[k]), hist[k], acc);
   return to_float<T>(from_float<T>(acc / (1.0f + expf(-acc))));
 }
 
 template <typename T>
-__device__ __forceinline__ void conv_store(const GdnParams& p, int64_t b, int64_t c, const float (&hist)[kConvMaxWidth]) {
-  T* st = static_cast<T*>(p.conv_state) + (b * p.conv_channels + c) * p.conv_width;
+__device__ __forceinline__ void conv_store(const GdnParams& p, int64_t b, int64_t c, const float (&hist)[kConvWidth]) {
+  T* st = static_cast<T*>(p.conv_state) + (b * p.conv_channels + c) * kConvWidth;
 #pragma unroll
-  for (int j = 0; j < kConvMaxWidth; ++j) {
-    if (j < p.conv_width) st[j] = from_float<T>(hist[j]);
-  }
+  for (int j = 0; j < kConvWidth; ++j) st[j] = from_float<T>(hist[j]);
 }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -132,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
       // q / k channels of this head and v channels of this slice through the conv; the
       // four slice CTAs of a head form a cluster: all read the old state, then rank 0
       // writes the q / k state and every CTA its own v channels.
-      float hq[kConvMaxWidth], hk[kConvMaxWidth], hv[kConvMaxWidth];
+      float hq[kConvWidth], hk[kConvWidth], hv[kConvWidth];
       const int64_t ch_q = h * kDk + tid, ch_k = H * kDk + h * kDk + tid, ch_v = 2 * H * kDk + h * kDv + v0 + tid;
       qv = conv_channel<T>(p, b, ch_q, hq);
       kvv = conv_channel<T>(p, b, ch_k, hk);
@@ -338,9 +328,9 @@ extern "C" int oq_gdn_conv_step(
     return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: unknown dtype");
   }
   if (k_dim != kDk || v_dim != kDv) return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: k_dim = v_dim = 128 required");
-  if (conv_kernel_size < 1 || conv_width < conv_kernel_size - 1 || conv_width < 1 || conv_width > kConvMaxWidth ||
-      conv_kernel_size > kConvMaxWidth) {
-    return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: need 1 <= kernel_size - 1 <= width <= %d", kConvMaxWidth);
+  if (conv_kernel_size != kConvWidth || conv_width != kConvWidth || conv_w_dtype != qkv_dtype) {
+    return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: fused conv needs kernel_size = state width = 4 and weights in "
+                "the qkv dtype (use oq_causal_conv1d_update + oq_gdn_recurrent otherwise)");
   }
   if (batch < 0 || num_heads <= 0) return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_conv_step: bad sizes");
   if (batch == 0) return ok();
@@ -370,9 +360,6 @@ extern "C" int oq_gdn_conv_step(
   p.conv_state = conv_state;
   p.conv_w = conv_weight;
   p.conv_b = conv_bias;
-  p.conv_w_dtype = conv_w_dtype;
-  p.conv_width = int(conv_width);
-  p.conv_ksize = int(conv_kernel_size);
   p.conv_channels = num_heads * (2 * kDk + kDv);
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

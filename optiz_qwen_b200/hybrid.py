@@ -66,7 +66,11 @@ class _AttnLayer:
 @dataclass
 class _GdnLayer:
     state: torch.Tensor
-    q: torch.Tensor = None
+    conv_state: torch.Tensor = None  # [B, C, 4] with the fused causal conv1d update
+    conv_w: torch.Tensor = None
+    conv_b: torch.Tensor = None
+    qkv: torch.Tensor = None         # [B, C] projection output (fused conv) ...
+    q: torch.Tensor = None           # ... or q / k / v after the conv
     k: torch.Tensor = None
     v: torch.Tensor = None
     g: torch.Tensor = None
@@ -92,13 +96,25 @@ class HybridDecodeStack:
     step quantises the new token into slot ``context`` of its page and attends
     over ``context + 1`` tokens, so repeated steps measure the same workload.
     With ``hold_context=False`` the caches grow by one token per step.
+    ``conv`` feeds every GDN layer its raw q/k/v projection output and runs the layer's
+    causal conv1d update (kernel 4) as the decode branch of Qwen3_5GatedDeltaNet does:
+    ``"separate"`` launches ``oq_causal_conv1d_update`` then the GDN step on its output,
+    ``"fused"`` the single-launch ``oq_gdn_conv_step`` (slower on B200, measured: the four
+    column-slice CTAs of a head each convolve q/k and synchronise as a cluster).  With
+    ``conv=None`` q/k/v are given post-conv.
     """
+
+    CONV_KERNEL = 4
 
     KV_BYTES_PER_TOKEN_HEAD = 264  # 2 x 128 B codes + 4 x 2 B fp16 scale/min
 
     def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
-                 hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16):
+                 hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16,
+                 conv: str | None = None):
+        if conv not in (None, "separate", "fused"):
+            raise ValueError("conv must be None, 'separate' or 'fused'")
         self.shape = shape
+        self.conv = conv
         self.device = torch.device(device)
         self.dtype = dtype
         self.hold_context = hold_context
@@ -117,10 +133,21 @@ class HybridDecodeStack:
                 self.order.append(("gdn", len(self.gdn)))
                 state = torch.randn((b, shape.gdn_heads, shape.gdn_dim, shape.gdn_dim), generator=self.gen,
                                     device=self.device, dtype=torch.float32).mul_(0.02)
-                self.gdn.append(_GdnLayer(state=state))
+                layer = _GdnLayer(state=state)
+                if conv:
+                    ch = self.conv_channels
+                    rnd = lambda *shp: torch.randn(shp, generator=self.gen, device=self.device)  # noqa: E731
+                    layer.conv_state = rnd(b, ch, self.CONV_KERNEL).to(dtype)
+                    layer.conv_w = (0.5 * rnd(ch, self.CONV_KERNEL)).to(dtype)
+                    layer.conv_b = (0.1 * rnd(ch)).to(dtype)
+                self.gdn.append(layer)
         self._alloc_io()
         self.graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(self.device)
+
+    @property
+    def conv_channels(self) -> int:
+        return self.shape.gdn_heads * 3 * self.shape.gdn_dim
 
     # ------------------------------------------------------------------ setup
     def _make_attn_layer(self, lengths, extra_tokens, page_seed) -> _AttnLayer:
@@ -162,6 +189,7 @@ class HybridDecodeStack:
         s = self.shape
         b = s.batch
         in_specs, out_specs = [], []
+        self._conv_out: list[torch.Tensor] = []
         for kind, i in self.order:
             if kind == "attn":
                 in_specs += [(("attn", i, "q"), (b, s.num_heads, s.head_dim)),
@@ -170,8 +198,14 @@ class HybridDecodeStack:
                 out_specs += [(("attn", i, "out"), (b, s.num_heads, s.head_dim))]
             else:
                 shp = (b, 1, s.gdn_heads, s.gdn_dim)
-                in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp),
-                             (("gdn", i, "beta"), (b, 1, s.gdn_heads))]
+                if self.conv:
+                    in_specs += [(("gdn", i, "qkv"), (b, self.conv_channels))]
+                    if self.conv == "separate":  # the conv kernel's output, read by the GDN step
+                        self._conv_out.append(torch.empty((b, self.conv_channels, 1), dtype=self.dtype,
+                                                          device=self.device))
+                else:
+                    in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp)]
+                in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
                 out_specs += [(("gdn", i, "out"), shp)]
         n_in = sum(math.prod(shp) for _, shp in in_specs)
         n_out = sum(math.prod(shp) for _, shp in out_specs)
@@ -231,9 +265,22 @@ class HybridDecodeStack:
                 # launch right before this one is another layer's GDN step, this one may start
                 # early and load its state during that step's tail.
                 chained = prev is not None and prev[0] == "gdn" and prev[1] != i
-                cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
-                                   final_state=layer.state, out=layer.out, use_qk_l2norm=True,
-                                   prefetch_state=chained)
+                if self.conv == "fused":
+                    cabi.gdn_conv_step(layer.qkv, layer.conv_state, layer.conv_w, layer.conv_b, layer.g, layer.beta,
+                                       num_heads=s.gdn_heads, initial_state=layer.state, final_state=layer.state,
+                                       out=layer.out, prefetch_state=chained)
+                elif self.conv == "separate":
+                    y = self._conv_out[i]
+                    cabi.causal_conv1d_update(layer.qkv.unsqueeze(-1), layer.conv_state, layer.conv_w, layer.conv_b,
+                                              out=y)
+                    hd = s.gdn_heads * s.gdn_dim
+                    q, k, v = (y[:, j * hd:(j + 1) * hd, 0].view(s.batch, 1, s.gdn_heads, s.gdn_dim) for j in range(3))
+                    cabi.gdn_recurrent(q, k, v, layer.g, layer.beta, initial_state=layer.state,
+                                       final_state=layer.state, out=layer.out, use_qk_l2norm=True)
+                else:
+                    cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
+                                       final_state=layer.state, out=layer.out, use_qk_l2norm=True,
+                                       prefetch_state=chained)
                 prev = ("gdn", i)
 
     def capture(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
@@ -265,11 +312,15 @@ class HybridDecodeStack:
         attend = lengths + 1 if self.hold_context else lengths
         attn_bytes_layer = int(attend.sum()) * s.num_kv_heads * self.KV_BYTES_PER_TOKEN_HEAD
         gdn_bytes_layer = 2 * s.batch * s.gdn_heads * s.gdn_dim * s.gdn_dim * 4
+        if self.conv:  # conv state read + written, plus the weights
+            esz = torch.tensor([], dtype=self.dtype).element_size()
+            gdn_bytes_layer += (2 * s.batch * self.conv_channels * self.CONV_KERNEL
+                                + self.conv_channels * (self.CONV_KERNEL + 1)) * esz
         append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.KV_BYTES_PER_TOKEN_HEAD)
         n_attn, n_gdn = len(self.attn), len(self.gdn)
         esize = self.in_dev.element_size()
         return StepCounts(
-            launches=2 * n_attn + n_gdn,
+            launches=2 * n_attn + n_gdn * (2 if self.conv == "separate" else 1),
             attn_bytes=attn_bytes_layer * n_attn,
             gdn_bytes=gdn_bytes_layer * n_gdn,
             append_bytes=append_bytes_layer * n_attn,

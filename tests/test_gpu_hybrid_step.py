@@ -58,3 +58,36 @@ def test_graph_step_matches_oracle():
             assert np.array_equal(cache.kv_meta[page, :, 1, slot], km[b, :, 0])
         ref, _ = oracle_attention(cache, f(layer.q), shape.head_dim ** -0.5)
         assert_attn_close(f(layer.out), ref)
+
+
+@pytest.mark.parametrize("conv", ["separate", "fused"])
+def test_graph_step_with_conv_matches_conv_then_recurrence(conv):
+    """Same step with every GDN layer fed its raw projection output: the conv states and the
+    GDN states / outputs match the oracle's conv update followed by its recurrence."""
+    from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
+
+    shape = HybridShape(batch=2, context=[40, 90], num_layers=4)
+    stack = HybridDecodeStack(shape, device="cuda", seed=5, conv=conv)
+    stack.fill_inputs()
+    states0 = [layer.state.cpu().numpy().copy() for layer in stack.gdn]
+    conv0 = [layer.conv_state.float().cpu().numpy().copy() for layer in stack.gdn]
+    graph = stack.capture()
+    for layer, s0, c0 in zip(stack.gdn, states0, conv0):
+        layer.state.copy_(torch.from_numpy(s0))
+        layer.conv_state.copy_(torch.from_numpy(c0).to(layer.conv_state.dtype))
+    graph.replay()
+    torch.cuda.synchronize()
+
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    h, d = shape.gdn_heads, shape.gdn_dim
+    for layer, s0, c0 in zip(stack.gdn, states0, conv0):
+        cst = c0.copy()
+        conv = kq.round_bf16(ogdn.causal_conv1d_update(f(layer.qkv)[:, :, None], cst, f(layer.conv_w), f(layer.conv_b),
+                                                       silu=True)[:, :, 0])
+        b = conv.shape[0]
+        q, k, v = (conv[:, i * h * d:(i + 1) * h * d].reshape(b, 1, h, d) for i in range(3))
+        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, f(layer.g), f(layer.beta), s0, True, True)
+        assert np.array_equal(f(layer.conv_state), cst)
+        assert_gdn_close(layer.state.cpu().numpy(), rs)
+        got = f(layer.out)
+        assert np.all(np.abs(got - ro) <= 2.0 ** -8 * np.abs(ro) + 1e-4 * np.abs(ro).max())
