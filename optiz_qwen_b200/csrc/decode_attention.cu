@@ -25,45 +25,14 @@
 #include <cmath>
 #include <mutex>
 
-#include "common.cuh"
+#include "decode_attention.cuh"
 
 namespace oq {
 namespace {
 
-constexpr int kHeadDim = 256;
-constexpr int kPage = 64;
-constexpr int kRowBytes = kHeadDim / 2;                // 128 bytes of codes per token
-constexpr int kStageCodeBytes = 2 * kPage * kRowBytes;  // K rows then V rows: 16 KB
-constexpr int kStageMetaBytes = 4 * kPage * 2;          // 512 B of fp16 scale/min
 constexpr int kStages = 4;
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxGroup = 8;
-constexpr int kMaxSplits = 512;
-constexpr int kMinPagesPerSplit = 8;
-constexpr int kInLaunchMergeSplits = 8;
-
-struct AttnParams {
-  const void* query;
-  int64_t q_sb, q_sh;
-  const uint16_t* kv_meta;
-  int64_t num_pages, num_kv_heads;
-  const int32_t* block_table;
-  int64_t bt_stride, max_pages;
-  const int32_t* seq_lens;
-  int group;
-  float scale_log2;  // scaling * log2(e)
-  void* out;
-  int64_t o_sb, o_sh;
-  float* out_f32;
-  float* out_lse;
-  float* partials;
-  int* counters;
-  int max_splits;
-  int pages_per_split;
-  int defer_merge;  // 1: write partials only, a separate merge kernel combines them
-  int32_t* status;
-};
 
 constexpr int kPageIdSlots = 1024;  // page ids of a CTA's range kept in shared memory
 
@@ -130,33 +99,9 @@ __device__ __forceinline__ const uint4* swz(const uint8_t* base, int row, int ch
   return reinterpret_cast<const uint4*>(base + row * kRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
-// Bounded wait for a stage: the thread sleeps in try_wait (up to 20 us per poll) and
-// gives up after kWaitPolls polls (~2 s): a copy that has not landed by then never will.
-constexpr uint32_t kWaitHintNs = 20000;
-constexpr int kWaitPolls = 100000;
-__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < kWaitPolls; ++i) {
-    if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
-  }
-  return false;
-}
-
-__device__ __forceinline__ float lse_nat(float m_log2, float l) {
-  return l > 0.0f ? (m_log2 + log2f(l)) * 0.69314718055994531f : -INFINITY;
-}
-
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
          ((uint32_t(d) & 0xFFu) << 24);
-}
-
-template <typename T>
-__device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
-                                          float l) {
-  const int64_t hq_total = p.num_kv_heads * p.group;
-  if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(o);
-  if (p.out_f32) p.out_f32[(b * hq_total + hq) * kHeadDim + d] = o;
-  if (p.out_lse && d == 0) p.out_lse[b * hq_total + hq] = lse_nat(m, l);
 }
 
 template <typename T, bool kDual>
@@ -608,69 +553,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   if (single || p.defer_merge) return;
 
   // ---- split-KV merge by the last CTA of this (sequence, KV head)
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int done = atomicAdd(&p.counters[unit], 1);
-    tail->is_last = done == nsplit_b - 1;
-  }
-  __syncthreads();
-  if (!tail->is_last) return;
-  __threadfence();
-  const float* recs = p.partials + unit * p.max_splits * rec_floats;
-  // stage every split's (M, L) in shared memory, then turn M into merge weights
-  float* wm = reinterpret_cast<float*>(codes);  // [nsplit_b][G]
-  float* wl = wm + nsplit_b * G;                // [nsplit_b][G]
-  float* head_m = wl + nsplit_b * G;            // [G]
-  float* head_l = head_m + kMaxGroup;           // [G]
-  for (int idx = tid; idx < nsplit_b * G; idx += kThreads) {
-    const int s = idx / G, h = idx - (idx / G) * G;
-    wm[idx] = __ldcg(recs + s * rec_floats + outputs + h);
-    wl[idx] = __ldcg(recs + s * rec_floats + outputs + G + h);
-  }
-  __syncthreads();
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit_b; ++s) M = fmaxf(M, wm[s * G + tid]);
-    float L = 0.0f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < nsplit_b; ++s) L += wl[s * G + tid] * exp2f(wm[s * G + tid] - M);
-    }
-    head_m[tid] = M;
-    head_l[tid] = L;
-  }
-  __syncthreads();
-  for (int idx = tid; idx < nsplit_b * G; idx += kThreads) {
-    const int h = idx - (idx / G) * G;
-    const float M = head_m[h];
-    wm[idx] = M == -INFINITY ? 0.0f : exp2f(wm[idx] - M);
-  }
-  __syncthreads();
-  constexpr int kMaxPer = kMaxGroup * kHeadDim / kThreads;  // 16 outputs per thread at most
-  const int per = outputs / kThreads;
-  float num[kMaxPer];
-#pragma unroll
-  for (int j = 0; j < kMaxPer; ++j) num[j] = 0.0f;
-  for (int s = 0; s < nsplit_b; ++s) {
-    const float* rec = recs + s * rec_floats;
-#pragma unroll
-    for (int j = 0; j < kMaxPer; ++j) {
-      if (j < per) {
-        const int e = tid + j * kThreads;
-        num[j] = fmaf(wm[s * G + e / kHeadDim], __ldcg(rec + e), num[j]);
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < kMaxPer; ++j) {
-    if (j < per) {
-      const int e = tid + j * kThreads;
-      const int h = e / kHeadDim;
-      const float L = head_l[h];
-      store_out<T>(p, b, int64_t(kvh) * G + h, e - h * kHeadDim, L > 0.0f ? num[j] / L : 0.0f, head_m[h], L);
-    }
-  }
-  if (tid == 0) p.counters[unit] = 0;  // ready for the next launch
+  merge_splits_last_cta<T, kThreads>(p, b, kvh, nsplit_b, tid, reinterpret_cast<float*>(codes), &tail->is_last, 1);
 }
 
 // ---- split-KV merge for many splits: one CTA per (sequence x KV head, query head),
@@ -743,22 +626,22 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
 size_t counters_bytes(int64_t units) { return size_t((units * sizeof(int) + 255) / 256 * 256); }
 
 // SMs x resident CTAs per SM of `kernel` on the current device (cached per device and kernel).
-int64_t resident_slots(const void* kernel) {
+int64_t resident_slots(const void* kernel, int threads, size_t smem) {
   static std::mutex mu;
-  static int64_t cache[64][4] = {};
-  static const void* kernels[4] = {};
+  static int64_t cache[64][8] = {};
+  static const void* kernels[8] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 3;
   std::lock_guard<std::mutex> lock(mu);
   int k = 0;
-  for (; k < 4 && kernels[k] != nullptr && kernels[k] != kernel; ++k) {
+  for (; k < 8 && kernels[k] != nullptr && kernels[k] != kernel; ++k) {
   }
-  if (k == 4) return 148 * 3;
+  if (k == 8) return 148 * 3;
   kernels[k] = kernel;
   if (cache[dev][k] == 0) {
     int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
     cache[dev][k] = int64_t(std::max(1, sms)) * std::max(1, per_sm);
   }
   return cache[dev][k];
@@ -838,7 +721,7 @@ extern "C" int oq_decode_attn_int4_paged(
   const int64_t units = batch * num_kv_heads;
   int splits = num_splits;
   if (splits <= 0) {
-    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel));
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), kThreads, kSmemBytes);
     // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
     splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
                                    std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
