@@ -131,6 +131,25 @@ int oq_decode_attn_int4_paged(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream);
 
+/* Same attention with the decode forward's output gate fused into the store:
+ * out = rnd(rnd(o) * rnd(sigmoid(gate))) in the query dtype (rnd = rounding to it),
+ * replacing ``attn_output * torch.sigmoid(gate)`` after the kernel
+ * (optiz_qwen/kernels/qwen35_fused_attention.py:96-97).  gate [batch, num_heads, head_dim]
+ * in the query dtype with element strides (b, h), the half of q_proj's output that is
+ * not the query.  out is required; no fp32 / lse outputs (they feed merges, which
+ * must see the ungated values). */
+int oq_decode_attn_int4_paged_gated(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream);
+
 /* Same attention, for callers that cannot allocate device memory (no counterpart
  * in the reference, which only runs inside PyTorch's allocator).  A decode loop
  * embedded in a host runtime whose arena owns all device memory, or a
@@ -209,6 +228,24 @@ int oq_gdn_recurrent(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int flags, void* stream);
 
+/* oq_gdn_recurrent with the GDN layer's output norm fused into the store:
+ * out = Qwen3_5RMSNormGated(o, z) per head (transformers models/qwen3_5/modeling_qwen3_5.py:175-190,
+ * applied at :527-529) = rnd(rnd(rnd(o * rsqrt(mean(o^2) + norm_eps)) * w) * silu(z)), with o
+ * first rounded to qkv_dtype as the unfused layer hands it on.  z [batch, seq_len, num_heads,
+ * v_dim] in qkv_dtype (element strides b, t, h; unit stride along v_dim), norm_weight [v_dim]
+ * in qkv_dtype.  The four column-slice CTAs of a head run as one thread-block cluster. */
+int oq_gdn_recurrent_norm(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm,
+    const void* z, int64_t z_stride_b, int64_t z_stride_t, int64_t z_stride_h,
+    const void* norm_weight, float norm_eps, int flags, void* stream);
+
 /* One GDN decode token with the layer's causal conv1d update fused in front of it.
  * Replaces, for the decode branch of Qwen3_5GatedDeltaNet.forward
  * (transformers models/qwen3_5/modeling_qwen3_5.py:454-520), the pair
@@ -229,6 +266,29 @@ int oq_gdn_conv_step(
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int flags, void* stream);
+
+/* oq_gdn_conv_step with the output norm of oq_gdn_recurrent_norm (z [batch, num_heads,
+ * v_dim] with element strides b, h): conv update, recurrent step and gated RMSNorm of
+ * the decode branch (modeling_qwen3_5.py:454-529) in one launch. */
+int oq_gdn_conv_step_norm(
+    const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
+    void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
+    int64_t conv_width, int64_t conv_kernel_size,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm,
+    const void* z, int64_t z_stride_b, int64_t z_stride_h, const void* norm_weight, float norm_eps,
+    int flags, void* stream);
+
+/* Gated RMSNorm as a standalone op: replaces Qwen3_5RMSNormGated.forward
+ * (transformers models/qwen3_5/modeling_qwen3_5.py:175-190) for callers that keep the
+ * norm a separate module.  rows of dim elements: x, z, out with row strides (elements,
+ * rows contiguous along dim), weight [dim]; all in dtype.  dim <= 1024.
+ * out = rnd(rnd(rnd(x * rsqrt(mean(x^2) + eps)) * weight) * silu(z)). */
+int oq_rmsnorm_gated(const void* x, int64_t x_stride, const void* z, int64_t z_stride, const void* weight,
+                     void* out, int64_t out_stride, int dtype, int64_t rows, int64_t dim, float eps,
+                     void* stream);
 
 /* Causal depthwise conv1d update (the GDN layer's short convolution).
  * Replaces the hook causal_conv1d_update (transformers torch_causal_conv1d_update,

@@ -41,10 +41,19 @@ SIGNATURES = {
                                         i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, p]),
     "oq_decode_attn_int4_paged_noalloc": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                                 i64, i64, i64, i64, f32, p, i64, i64, p, p, i32, p, p]),
+    "oq_decode_attn_int4_paged_gated": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
+                                              i64, i64, i64, i64, f32, p, i64, i64, p, i64, i64, p, sz, i32, p,
+                                              p]),
     "oq_lse_merge": (i32, [p, p, i64, i64, i64, p, i32, p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p]),
+    "oq_gdn_recurrent_norm": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                    p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32,
+                                    p, i64, i64, i64, p, f32, i32, p]),
+    "oq_gdn_conv_step_norm": (i32, [p, i32, i64, p, p, p, i32, i64, i64, p, i32, p, i32, p, p, p, i64, i64, i64,
+                                    i64, f32, i32, p, i64, i64, p, f32, i32, p]),
+    "oq_rmsnorm_gated": (i32, [p, i64, p, i64, p, p, i64, i32, i64, i64, f32, p]),
     "oq_causal_conv1d_update": (i32, [p, i32, i64, i64, i64, p, p, p, i32, p, i64, i64, i64, i64, i64, i32, p]),
     "oq_gdn_conv_step": (i32, [p, i32, i64, p, p, p, i32, i64, i64, p, i32, p, i32, p, p, p, i64, i64, i64, i64,
                                f32, i32, i32, p]),

@@ -118,10 +118,14 @@ def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: t
                           seq_lens: torch.Tensor, scaling: float, *, out: torch.Tensor | None = None,
                           out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
                           workspace: torch.Tensor | None = None, num_splits: int = 0,
-                          device_status: torch.Tensor | None = None, want_out: bool = True):
+                          device_status: torch.Tensor | None = None, want_out: bool = True,
+                          gate: torch.Tensor | None = None):
     """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache.
 
-    Returns ``out`` (query dtype, ``[B, Hq, D]``) unless ``want_out`` is False.
+    Returns ``out`` (query dtype, ``[B, Hq, D]``) unless ``want_out`` is False.  With
+    ``gate`` ``[B, Hq, D]`` (query dtype, unit stride along D) the output is gated in the
+    kernel: ``out = attn * sigmoid(gate)`` (``oq_decode_attn_int4_paged_gated``); fp32 /
+    lse outputs are not available then.
     """
     require_cuda(query, block_table, seq_lens)
     if query.dim() != 3:
@@ -141,6 +145,19 @@ def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: t
     for t, shape in ((out_f32, (b, hq, d)), (out_lse, (b, hq))):
         if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous()):
             raise ValueError("out_f32 / out_lse must be contiguous fp32 of shape [B, Hq, D] / [B, Hq]")
+    if gate is not None:
+        require_cuda(gate)
+        if gate.dtype != query.dtype or tuple(gate.shape) != (b, hq, d) or gate.stride(2) != 1:
+            raise ValueError("gate must be [B, Hq, D] in the query dtype with unit stride along D")
+        if out is None or out_f32 is not None or out_lse is not None:
+            raise ValueError("a gated call writes the query-dtype output only")
+        call("oq_decode_attn_int4_paged_gated", ptr(query), dtype_code(query.dtype), query.stride(0),
+             query.stride(1), ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+             ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
+             b, hq, pool.num_kv_heads, d, float(scaling), ptr(gate), gate.stride(0), gate.stride(1),
+             ptr(out), out.stride(0), out.stride(1), ptr(workspace), workspace.numel(), int(num_splits),
+             ptr(device_status), stream_ptr(query.device))
+        return out
     call("oq_decode_attn_int4_paged", ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
          ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
          ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
@@ -187,10 +204,13 @@ def gather_dequant_int4(pool: PagedKvPool, block_table: torch.Tensor, seq_lens: 
 def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                  use_qk_l2norm: bool = False, prefetch_state: bool = False) -> torch.Tensor:
+                  use_qk_l2norm: bool = False, prefetch_state: bool = False, z: torch.Tensor | None = None,
+                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6) -> torch.Tensor:
     """Gated delta rule over ``T`` tokens: q, k ``[B, T, H, Dk]``, v ``[B, T, H, Dv]``, g/beta ``[B, T, H]``.
 
     Writes ``final_state`` (may alias ``initial_state``) and returns ``out`` ``[B, T, H, Dv]``.
+    With ``z`` ``[B, T, H, Dv]`` and ``norm_weight`` ``[Dv]`` (qkv dtype) the layer's gated
+    RMSNorm is fused into the store (``oq_gdn_recurrent_norm``): ``out = RMSNormGated(o, z)``.
     ``prefetch_state`` (``OQ_GDN_STATE_PREFETCH``) lets the kernel read the state while the
     preceding kernel in the stream is still running: only for callers that know no such
     kernel writes it (a decode step, where layer l's state was written one step earlier).
@@ -212,6 +232,21 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
     if out is None:
         out = torch.empty((bsz, t, h, dv), dtype=q.dtype, device=q.device)
     scale = dk ** -0.5 if scale is None else float(scale)
+    if (z is None) != (norm_weight is None):
+        raise ValueError("z and norm_weight come together")
+    if z is not None:
+        require_cuda(z, norm_weight)
+        if z.dtype != q.dtype or tuple(z.shape) != (bsz, t, h, dv) or z.stride(3) != 1:
+            raise ValueError("z must be [B, T, H, Dv] in the qkv dtype with unit stride along Dv")
+        norm_weight = norm_weight.to(q.dtype).contiguous()
+        call("oq_gdn_recurrent_norm", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
+             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+             v.stride(0), v.stride(1), v.stride(2),
+             ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
+             ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
+             ptr(z), z.stride(0), z.stride(1), z.stride(2), ptr(norm_weight), float(norm_eps),
+             GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(q.device))
+        return out
     call("oq_gdn_recurrent", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
          q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
          v.stride(0), v.stride(1), v.stride(2),
@@ -251,10 +286,12 @@ def gdn_conv_step(qkv: torch.Tensor, conv_state: torch.Tensor, conv_weight: torc
                   conv_bias: torch.Tensor | None, g: torch.Tensor, beta: torch.Tensor, *, num_heads: int,
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                  use_qk_l2norm: bool = True, prefetch_state: bool = False) -> torch.Tensor:
+                  use_qk_l2norm: bool = True, prefetch_state: bool = False, z: torch.Tensor | None = None,
+                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6) -> torch.Tensor:
     """One GDN decode token with the causal conv1d update fused in: qkv ``[B, C]`` (the projection
     output, q heads | k heads | v heads), conv_state ``[B, C, W]`` and the recurrent state are updated
-    in place; returns ``out`` ``[B, 1, H, 128]``."""
+    in place; returns ``out`` ``[B, 1, H, 128]``.  With ``z`` ``[B, H, 128]`` and ``norm_weight`` the
+    layer's gated RMSNorm is fused in as well (``oq_gdn_conv_step_norm``)."""
     require_cuda(qkv, conv_state, conv_weight, conv_bias, g, beta, initial_state, final_state)
     dk = dv = 128
     bsz = qkv.shape[0]
@@ -274,11 +311,47 @@ def gdn_conv_step(qkv: torch.Tensor, conv_state: torch.Tensor, conv_weight: torc
     if out is None:
         out = torch.empty((bsz, 1, num_heads, dv), dtype=qkv.dtype, device=qkv.device)
     scale = dk ** -0.5 if scale is None else float(scale)
+    if (z is None) != (norm_weight is None):
+        raise ValueError("z and norm_weight come together")
+    if z is not None:
+        require_cuda(z, norm_weight)
+        if z.dtype != qkv.dtype or tuple(z.shape) != (bsz, num_heads, dv) or z.stride(2) != 1:
+            raise ValueError("z must be [B, H, 128] in the qkv dtype with unit stride along the last dim")
+        norm_weight = norm_weight.to(qkv.dtype).contiguous()
+        call("oq_gdn_conv_step_norm", ptr(qkv), dtype_code(qkv.dtype), qkv.stride(0), ptr(conv_state),
+             ptr(conv_weight), ptr(conv_bias), dtype_code(conv_weight.dtype), conv_state.shape[-1],
+             conv_weight.shape[-1], ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
+             ptr(initial_state), ptr(final_state), ptr(out), bsz, num_heads, dk, dv, float(scale),
+             int(use_qk_l2norm), ptr(z), z.stride(0), z.stride(1), ptr(norm_weight), float(norm_eps),
+             GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(qkv.device))
+        return out
     call("oq_gdn_conv_step", ptr(qkv), dtype_code(qkv.dtype), qkv.stride(0), ptr(conv_state), ptr(conv_weight),
          ptr(conv_bias), dtype_code(conv_weight.dtype), conv_state.shape[-1], conv_weight.shape[-1],
          ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype), ptr(initial_state), ptr(final_state),
          ptr(out), bsz, num_heads, dk, dv, float(scale), int(use_qk_l2norm),
          GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(qkv.device))
+    return out
+
+
+def rmsnorm_gated(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3_5RMSNormGated over the last dim: ``x``, ``z`` ``[..., D]`` (same dtype, D <= 1024),
+    ``weight`` ``[D]``; returns ``rnd(rnd(rnd(x * rsqrt(mean(x^2) + eps)) * w) * silu(z))``."""
+    require_cuda(x, z, weight)
+    if z.shape != x.shape or z.dtype != x.dtype:
+        raise ValueError("x and z must share shape and dtype")
+    d = x.shape[-1]
+    x2, z2 = x.reshape(-1, d), z.reshape(-1, d)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    if z2.stride(1) != 1:
+        z2 = z2.contiguous()
+    weight = weight.to(x.dtype).contiguous()
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    o2 = out.view(-1, d)
+    call("oq_rmsnorm_gated", ptr(x2), x2.stride(0), ptr(z2), z2.stride(0), ptr(weight), ptr(o2), o2.stride(0),
+         dtype_code(x.dtype), x2.shape[0], d, float(eps), stream_ptr(x.device))
     return out
 
 

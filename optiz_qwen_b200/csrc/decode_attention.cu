@@ -673,7 +673,10 @@ extern "C" size_t oq_decode_attn_workspace_bytes(int64_t batch, int64_t num_head
   return oq::counters_bytes(units) + size_t(units * max_splits * group * (head_dim + 2) * sizeof(float));
 }
 
-extern "C" int oq_decode_attn_int4_paged(
+namespace oq {
+namespace {
+
+int decode_attn_impl(
     const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
     const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
@@ -683,8 +686,9 @@ extern "C" int oq_decode_attn_int4_paged(
     void* out, int64_t out_stride_b, int64_t out_stride_h,
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
     int32_t* device_status, void* stream) {
-  using namespace oq;
+  if (gate && !out) return fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged: a gate needs the model-dtype output");
   if (dtype != OQ_BF16 && dtype != OQ_F16) {
     return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: query dtype must be bf16 or fp16");
   }
@@ -772,6 +776,9 @@ extern "C" int oq_decode_attn_int4_paged(
   // few splits: the last CTA of each (sequence, KV head) merges in-launch; many: a merge kernel
   p.defer_merge = splits > kInLaunchMergeSplits ? 1 : 0;
   p.status = device_status;
+  p.gate = gate;
+  p.g_sb = gate_stride_b;
+  p.g_sh = gate_stride_h;
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -785,4 +792,43 @@ extern "C" int oq_decode_attn_int4_paged(
     }
   }
   return check_launch("decode_attn_int4_paged");
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_decode_attn_int4_paged(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream) {
+  return oq::decode_attn_impl(query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages, page_size,
+                              block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_heads,
+                              num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32, out_lse,
+                              workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream);
+}
+
+extern "C" int oq_decode_attn_int4_paged_gated(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream) {
+  if (gate == nullptr) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged_gated: null gate");
+  return oq::decode_attn_impl(query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages, page_size,
+                              block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_heads,
+                              num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, nullptr, nullptr,
+                              workspace, workspace_bytes, num_splits, gate, gate_stride_b, gate_stride_h,
+                              device_status, stream);
 }

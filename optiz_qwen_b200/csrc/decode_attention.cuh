@@ -40,6 +40,9 @@ struct AttnParams {
   int pages_per_split;
   int defer_merge;  // 1: write partials only, a separate merge kernel combines them
   int32_t* status;
+  // optional output gate: out = o * sigmoid(gate), gate [B, Hq, 256] in the query dtype
+  const void* gate;
+  int64_t g_sb, g_sh;
 };
 
 // Bounded wait for a stage: the thread sleeps in try_wait (up to 20 us per poll) and
@@ -57,11 +60,22 @@ __device__ __forceinline__ float lse_nat(float m_log2, float l) {
   return l > 0.0f ? (m_log2 + log2f(l)) * 0.69314718055994531f : -INFINITY;
 }
 
+// The model-dtype output, gated if asked: the decode forward's
+// ``attn_output * torch.sigmoid(gate)`` (optiz_qwen/kernels/qwen35_fused_attention.py:96-97)
+// with each operand rounded to the model dtype as the unfused ops leave it.
 template <typename T>
 __device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
                                           float l) {
   const int64_t hq_total = p.num_kv_heads * p.group;
-  if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(o);
+  if (p.out) {
+    T y = from_float<T>(o);
+    if (p.gate) {
+      const float g = to_float<T>(static_cast<const T*>(p.gate)[b * p.g_sb + hq * p.g_sh + d]);
+      const float sg = to_float<T>(from_float<T>(1.0f / (1.0f + expf(-g))));
+      y = from_float<T>(to_float<T>(y) * sg);
+    }
+    static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = y;
+  }
   if (p.out_f32) p.out_f32[(b * hq_total + hq) * kHeadDim + d] = o;
   if (p.out_lse && d == 0) p.out_lse[b * hq_total + hq] = lse_nat(m, l);
 }

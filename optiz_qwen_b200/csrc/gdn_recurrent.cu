@@ -10,6 +10,11 @@
 //   S *= exp(g);  kv = S^T k;  delta = beta (v - kv);  S += k delta^T;  o = S^T q.
 // Column sums over the 128 state rows are reduced with warp shuffles and a
 // 4-warp shared-memory step.
+//
+// Optional gated RMSNorm epilogue: the GDN layer's Qwen3_5RMSNormGated(o, z)
+// (modeling_qwen3_5.py:175-190, call site :527-529) applied to each head's 128 outputs
+// before they are stored.  The four column-slice CTAs of a head then run as one cluster
+// and add their partial sums of squares through distributed shared memory.
 #include <cmath>
 
 #include "common.cuh"
@@ -43,6 +48,11 @@ struct GdnParams {
   const void* conv_w;  // [C, K]
   const void* conv_b;  // [C] or null, in T
   int64_t conv_channels;
+  // gated RMSNorm epilogue: out = rnd(rnd(rnd(o * rsqrt(mean(o^2) + eps)) * w) * silu(z))
+  const void* z;       // [B, T, H, Dv] gate in T (strides b, t, h)
+  int64_t zs[3];
+  const void* norm_w;  // [Dv] in T
+  float norm_eps;
 };
 
 constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
@@ -75,11 +85,24 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.aligned;\nbarrier.cluster.wait.aligned;\n" ::: "memory");
 }
 
-template <typename T, bool kConv>
+// Shared-memory address of `p` in the CTA of cluster rank `rank`, and a load from it.
+__device__ __forceinline__ uint32_t cluster_map_shared(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+template <typename T, bool kConv, bool kNorm>
 __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
   __shared__ float q_s[kDk], k_s[kDk], v_s[kCols];
   __shared__ float red_kv[4][kCols], red_o[4][kCols];
   __shared__ float norm_q[4], norm_k[4];
+  __shared__ float norm_part;  // this slice's sum of squares of the (model-dtype) outputs
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -216,10 +239,39 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) red_o[warp][4 * cg + j] = o[j];
     }
+    float zv = 0.0f, wv = 0.0f;
+    if (kNorm && tid < kCols) {
+      zv = to_float<T>(static_cast<const T*>(p.z)[b * p.zs[0] + t * p.zs[1] + h * p.zs[2] + v0 + tid]);
+      wv = to_float<T>(static_cast<const T*>(p.norm_w)[v0 + tid]);
+    }
     __syncthreads();
-    if (tid < kCols) {
-      const float ov = (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]);
-      static_cast<T*>(p.out)[((b * p.seq_len + t) * H + h) * kDv + v0 + tid] = from_float<T>(ov);
+    T* orow = static_cast<T*>(p.out) + ((b * p.seq_len + t) * H + h) * kDv + v0;
+    const float ov = tid < kCols ? (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]) : 0.0f;
+    if constexpr (!kNorm) {
+      if (tid < kCols) orow[tid] = from_float<T>(ov);
+    } else {
+      // o in the model dtype (as the unfused layer hands it to the norm), its squares summed
+      // over the head's 128 columns by the 4 CTAs of the cluster
+      const float orr = to_float<T>(from_float<T>(ov));
+      if (warp == 0) {
+        float ss = orr * orr;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) norm_part = ss;
+      }
+      cluster_sync();
+      float tot = 0.0f;
+      if (warp == 0) {
+#pragma unroll
+        for (uint32_t rank = 0; rank < kDv / kCols; ++rank) tot += ld_shared_cluster_f32(cluster_map_shared(&norm_part, rank));
+      }
+      cluster_sync();  // every CTA has read the partials: they may change (next token) or go (exit)
+      if (tid < kCols) {
+        const float inv = 1.0f / sqrtf(tot * (1.0f / kDv) + p.norm_eps);
+        const float nrm = to_float<T>(from_float<T>(orr * inv));
+        const float y = to_float<T>(from_float<T>(wv * nrm));
+        orow[tid] = from_float<T>(y * (zv / (1.0f + expf(-zv))));
+      }
     }
   }
 
@@ -241,8 +293,8 @@ void launch_gdn(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnP
   }
 }
 
-// The fused conv variant runs the four column slices of a head as one cluster.
-cudaError_t launch_gdn_conv(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
+// The fused conv and norm variants run the four column slices of a head as one cluster.
+cudaError_t launch_gdn_cluster(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
@@ -259,10 +311,46 @@ cudaError_t launch_gdn_conv(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-}  // namespace
-}  // namespace oq
+// Gated RMSNorm epilogue arguments (null: plain output).
+struct NormArgs {
+  const void* z;
+  int64_t zs[3];
+  const void* weight;
+  float eps;
+};
 
-extern "C" int oq_gdn_recurrent(
+template <bool kConv>
+void (*gdn_kernel_for(int dtype, bool norm))(GdnParams) {
+  if (norm) {
+    switch (dtype) {
+      case OQ_F32: return gdn_recurrent_kernel<float, kConv, true>;
+      case OQ_F16: return gdn_recurrent_kernel<__half, kConv, true>;
+      default: return gdn_recurrent_kernel<__nv_bfloat16, kConv, true>;
+    }
+  }
+  switch (dtype) {
+    case OQ_F32: return gdn_recurrent_kernel<float, kConv, false>;
+    case OQ_F16: return gdn_recurrent_kernel<__half, kConv, false>;
+    default: return gdn_recurrent_kernel<__nv_bfloat16, kConv, false>;
+  }
+}
+
+int check_norm(const NormArgs* norm, const char* what) {
+  if (norm && (!norm->z || !norm->weight)) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: null gate or norm weight", what);
+  if (norm && !(norm->eps >= 0.0f)) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: norm eps must be >= 0", what);
+  return OQ_OK;
+}
+
+void set_norm(GdnParams& p, const NormArgs* norm) {
+  p.z = norm ? norm->z : nullptr;
+  p.zs[0] = norm ? norm->zs[0] : 0;
+  p.zs[1] = norm ? norm->zs[1] : 0;
+  p.zs[2] = norm ? norm->zs[2] : 0;
+  p.norm_w = norm ? norm->weight : nullptr;
+  p.norm_eps = norm ? norm->eps : 0.0f;
+}
+
+int gdn_recurrent_impl(
     const void* q, const void* k, const void* v, int qkv_dtype,
     int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
     int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
@@ -270,8 +358,8 @@ extern "C" int oq_gdn_recurrent(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, int flags, void* stream) {
-  using namespace oq;
+    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, void* stream) {
+  if (int st = check_norm(norm, "gdn_recurrent"); st != OQ_OK) return st;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
   }
@@ -286,7 +374,7 @@ extern "C" int oq_gdn_recurrent(
       (final_state && reinterpret_cast<uintptr_t>(final_state) % 16)) {
     return fail(OQ_ERR_MISALIGNED, "gdn_recurrent: state must be 16-byte aligned");
   }
-  GdnParams p;
+  GdnParams p = {};
   p.q = q;
   p.k = k;
   p.v = v;
@@ -305,25 +393,26 @@ extern "C" int oq_gdn_recurrent(
   p.scale = scale;
   p.l2norm = use_qk_l2norm;
   p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
+  set_norm(p, norm);
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (qkv_dtype) {
-    case OQ_F32: launch_gdn(gdn_recurrent_kernel<float, false>, grid, s, p); break;
-    case OQ_F16: launch_gdn(gdn_recurrent_kernel<__half, false>, grid, s, p); break;
-    default: launch_gdn(gdn_recurrent_kernel<__nv_bfloat16, false>, grid, s, p); break;
+  if (norm) {
+    launch_gdn_cluster(gdn_kernel_for<false>(qkv_dtype, true), grid, s, p);
+  } else {
+    launch_gdn(gdn_kernel_for<false>(qkv_dtype, false), grid, s, p);
   }
   return check_launch("gdn_recurrent");
 }
 
-extern "C" int oq_gdn_conv_step(
+int gdn_conv_step_impl(
     const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
     void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
     int64_t conv_width, int64_t conv_kernel_size,
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, int flags, void* stream) {
-  using namespace oq;
+    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, void* stream) {
+  if (int st = check_norm(norm, "gdn_conv_step"); st != OQ_OK) return st;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype) || !valid_dtype(conv_w_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: unknown dtype");
   }
@@ -361,12 +450,76 @@ extern "C" int oq_gdn_conv_step(
   p.conv_w = conv_weight;
   p.conv_b = conv_bias;
   p.conv_channels = num_heads * (2 * kDk + kDv);
+  set_norm(p, norm);
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (qkv_dtype) {
-    case OQ_F32: launch_gdn_conv(gdn_recurrent_kernel<float, true>, grid, s, p); break;
-    case OQ_F16: launch_gdn_conv(gdn_recurrent_kernel<__half, true>, grid, s, p); break;
-    default: launch_gdn_conv(gdn_recurrent_kernel<__nv_bfloat16, true>, grid, s, p); break;
-  }
+  launch_gdn_cluster(gdn_kernel_for<true>(qkv_dtype, norm != nullptr), grid, s, p);
   return check_launch("gdn_conv_step");
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_gdn_recurrent(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, void* stream) {
+  return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
+                                k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
+                                initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
+                                use_qk_l2norm, nullptr, flags, stream);
+}
+
+extern "C" int oq_gdn_recurrent_norm(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm,
+    const void* z, int64_t z_stride_b, int64_t z_stride_t, int64_t z_stride_h,
+    const void* norm_weight, float norm_eps, int flags, void* stream) {
+  const oq::NormArgs norm = {z, {z_stride_b, z_stride_t, z_stride_h}, norm_weight, norm_eps};
+  return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
+                                k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
+                                initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
+                                use_qk_l2norm, &norm, flags, stream);
+}
+
+extern "C" int oq_gdn_conv_step(
+    const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
+    void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
+    int64_t conv_width, int64_t conv_kernel_size,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, void* stream) {
+  return oq::gdn_conv_step_impl(qkv, qkv_dtype, qkv_stride_b, conv_state, conv_weight, conv_bias, conv_w_dtype,
+                                conv_width, conv_kernel_size, g, g_dtype, beta, beta_dtype, initial_state,
+                                final_state, out, batch, num_heads, k_dim, v_dim, scale, use_qk_l2norm, nullptr,
+                                flags, stream);
+}
+
+extern "C" int oq_gdn_conv_step_norm(
+    const void* qkv, int qkv_dtype, int64_t qkv_stride_b,
+    void* conv_state, const void* conv_weight, const void* conv_bias, int conv_w_dtype,
+    int64_t conv_width, int64_t conv_kernel_size,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm,
+    const void* z, int64_t z_stride_b, int64_t z_stride_h, const void* norm_weight, float norm_eps,
+    int flags, void* stream) {
+  const oq::NormArgs norm = {z, {z_stride_b, 0, z_stride_h}, norm_weight, norm_eps};
+  return oq::gdn_conv_step_impl(qkv, qkv_dtype, qkv_stride_b, conv_state, conv_weight, conv_bias, conv_w_dtype,
+                                conv_width, conv_kernel_size, g, g_dtype, beta, beta_dtype, initial_state,
+                                final_state, out, batch, num_heads, k_dim, v_dim, scale, use_qk_l2norm, &norm, flags,
+                                stream);
 }

@@ -121,17 +121,35 @@ def causal_conv1d_update(x: torch.Tensor, conv_state: torch.Tensor, weight: torc
     return out.squeeze(-1) if squeeze else out
 
 
+def rmsnorm_gated_forward(self, hidden_states: torch.Tensor, gate: torch.Tensor | None = None) -> torch.Tensor:
+    """``Qwen3_5RMSNormGated.forward`` (transformers models/qwen3_5/modeling_qwen3_5.py:181-190) on
+    the ``oq_rmsnorm_gated`` kernel: same dtype steps, bound per module by :func:`install_gdn_fastpath`."""
+    if gate is None:
+        raise NotImplementedError("the gated RMSNorm hook needs the gate (the GDN layer always passes z)")
+    if not hidden_states.is_cuda:
+        raise RuntimeError("rmsnorm_gated requires CUDA tensors")
+    return cabi.rmsnorm_gated(hidden_states, gate.to(hidden_states.dtype), self.weight,
+                              float(self.variance_epsilon))
+
+
 def install_gdn_fastpath(model) -> int:
     """Bind the hooks on every Gated-DeltaNet module of ``model``; returns how many were patched.
 
     This replaces the reference's PYTHONPATH overlay that makes fla importable
     before transformers binds its fast path (scripts/run_v11_cuda_matrix.py:285-289).
+    The module's output norm (a Qwen3_5RMSNormGated at ``module.norm``) gets the gated
+    RMSNorm kernel as its forward.
     """
+    from types import MethodType
+
     patched = 0
     for module in model.modules():
         if "GatedDeltaNet" in type(module).__name__ and hasattr(module, "recurrent_gated_delta_rule"):
             module.recurrent_gated_delta_rule = fused_recurrent_gated_delta_rule
             module.chunk_gated_delta_rule = chunk_gated_delta_rule
             module.causal_conv1d_update = causal_conv1d_update
+            norm = getattr(module, "norm", None)
+            if norm is not None and "RMSNormGated" in type(norm).__name__:
+                norm.forward = MethodType(rmsnorm_gated_forward, norm)
             patched += 1
     return patched

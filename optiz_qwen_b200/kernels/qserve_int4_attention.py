@@ -27,7 +27,8 @@ def triton_int4_decode_available(query: torch.Tensor) -> bool:
 int4_decode_available = triton_int4_decode_available
 
 
-def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: int, what: str) -> torch.Tensor:
+def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: int, what: str,
+                  gate: torch.Tensor | None = None) -> torch.Tensor:
     if not (query.is_cuda and query.shape[-2] == 1):
         raise RuntimeError(f"{what} requires a CUDA query with sequence length 1.")
     paged = getattr(layer, "paged", None)
@@ -38,19 +39,28 @@ def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: i
     if num_heads % num_kv_heads:
         raise ValueError("Qwen GQA decode requires an integer query-to-KV head ratio.")
     q = query[:, :, 0, :]
+    if gate is not None:  # the decode forward's output gate, [B, 1, Hq * D] -> [B, Hq, D]
+        gate = gate.reshape(batch, num_heads, head_dim)
     out = cabi.decode_attention_int4(q, paged.pool, paged.block_table, paged.seq_lens, scaling,
-                                     workspace=layer.decode_workspace(num_heads), num_splits=num_splits)
+                                     workspace=layer.decode_workspace(num_heads), num_splits=num_splits, gate=gate)
     return out.unsqueeze(1)
 
 
-def qserve_int4_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
-    """Attend to the packed cache with one KV range per (sequence, KV head)."""
-    return _paged_decode(query, layer, scaling, 1, "INT4 decode attention")
+def qserve_int4_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float,
+                                 gate: torch.Tensor | None = None) -> torch.Tensor:
+    """Attend to the packed cache with one KV range per (sequence, KV head).
+
+    ``gate`` (``[B, 1, Hq * D]``, optional, an addition to the reference's signature)
+    fuses the decode forward's ``* sigmoid(gate)`` into the kernel's output store."""
+    return _paged_decode(query, layer, scaling, 1, "INT4 decode attention", gate)
 
 
-def qserve_int4_split_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
-    """Split-KV decode: KV ranges spread over the SMs, partials merged by log-sum-exp in-launch."""
-    return _paged_decode(query, layer, scaling, 0, "INT4 split decode")
+def qserve_int4_split_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float,
+                                       gate: torch.Tensor | None = None) -> torch.Tensor:
+    """Split-KV decode: KV ranges spread over the SMs, partials merged by log-sum-exp in-launch.
+
+    ``gate``: as for :func:`qserve_int4_decode_attention`."""
+    return _paged_decode(query, layer, scaling, 0, "INT4 split decode", gate)
 
 
 def qserve_int8_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:

@@ -3,7 +3,8 @@
 Prefill (``seq_len != 1``) is delegated to the module's original forward.  A
 decode step runs the module's own projections, norms and RoPE, appends the new
 token to the paged INT4 cache (``past_key_values.update``), then the sm_100a
-decode attention on the pool, the sigmoid output gate and ``o_proj``.
+decode attention on the pool with the sigmoid output gate fused into its store, and
+``o_proj``.
 """
 
 from __future__ import annotations
@@ -54,14 +55,19 @@ def _qserve_fused_forward(self, hidden_states: torch.Tensor, position_embeddings
             and bool(getattr(past_key_values, "_optiz_dense_decode_mask", False))
         )
 
+    gated = False
     if fused_decode:
         backend = getattr(past_key_values, "attention_backend", "triton_int4_decode")
         if backend == "triton_int4_split_decode":
-            attn_output = qserve_int4_split_decode_attention(query_states, cache_layer, scaling=self.scaling)
+            # the output gate rides in the kernel's store
+            attn_output = qserve_int4_split_decode_attention(query_states, cache_layer, scaling=self.scaling,
+                                                             gate=gate)
+            gated = True
         elif backend == "triton_int8_decode":
             attn_output = qserve_int8_decode_attention(query_states, cache_layer, scaling=self.scaling)
         else:
-            attn_output = qserve_int4_decode_attention(query_states, cache_layer, scaling=self.scaling)
+            attn_output = qserve_int4_decode_attention(query_states, cache_layer, scaling=self.scaling, gate=gate)
+            gated = True
         attn_weights = None
         past_key_values.kernel_calls += 1
     else:
@@ -75,7 +81,8 @@ def _qserve_fused_forward(self, hidden_states: torch.Tensor, position_embeddings
             dropout=0.0 if not self.training else self.attention_dropout, scaling=self.scaling, **kwargs)
 
     attn_output = attn_output.reshape(*input_shape, -1).contiguous()
-    attn_output = attn_output * torch.sigmoid(gate)
+    if not gated:
+        attn_output = attn_output * torch.sigmoid(gate)
     return self.o_proj(attn_output), attn_weights
 
 

@@ -138,9 +138,36 @@ def make_gdn(torch):
     np.savez_compressed(HERE / "gdn_golden.npz", **out)
 
 
+def make_epilogue(torch):
+    """The output epilogues around the two decode kernels, in bf16 as the model runs them:
+    Qwen3_5RMSNormGated on the GDN output (transformers modeling_qwen3_5.py:175-190, call
+    site :527-529) and the attention output gate ``attn_output * torch.sigmoid(gate)``
+    (optiz_qwen/kernels/qwen35_fused_attention.py:96-97)."""
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as m
+
+    rng = np.random.default_rng(5)
+    out = {}
+    rows, dim = 48, 128
+    x = torch.from_numpy(rng.standard_normal((rows, dim), dtype=np.float32)).to(torch.bfloat16)
+    z = torch.from_numpy(rng.standard_normal((rows, dim), dtype=np.float32)).to(torch.bfloat16)
+    norm = m.Qwen3_5RMSNormGated(dim, eps=1e-6).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(torch.from_numpy(1.0 + 0.1 * rng.standard_normal(dim, dtype=np.float32)))
+        y = norm(x, z)
+    out.update(norm_x=_bf16_bits(x), norm_z=_bf16_bits(z), norm_w=_bf16_bits(norm.weight.detach()),
+               norm_y=_bf16_bits(y), norm_eps=np.float32(1e-6))
+    attn = torch.from_numpy(rng.standard_normal((3, 1, 8 * 256), dtype=np.float32)).to(torch.bfloat16)
+    gate = torch.from_numpy(2.0 * rng.standard_normal((3, 1, 8 * 256), dtype=np.float32)).to(torch.bfloat16)
+    gated = attn * torch.sigmoid(gate)
+    out.update(gate_attn=_bf16_bits(attn), gate_g=_bf16_bits(gate), gate_y=_bf16_bits(gated))
+    np.savez_compressed(HERE / "epilogue_golden.npz", **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["quant", "attention", "gdn", "epilogue"], default=None,
+                    help="regenerate one fixture file only")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     import torch
@@ -148,9 +175,14 @@ def main() -> None:
     torch.manual_seed(0)
     from optiz_qwen.compression.qserve_kv_cache import QServeAttentionLayer
 
-    make_quant(QServeAttentionLayer, torch)
-    make_attention(QServeAttentionLayer, torch)
-    make_gdn(torch)
+    if args.only in (None, "quant"):
+        make_quant(QServeAttentionLayer, torch)
+    if args.only in (None, "attention"):
+        make_attention(QServeAttentionLayer, torch)
+    if args.only in (None, "gdn"):
+        make_gdn(torch)
+    if args.only in (None, "epilogue"):
+        make_epilogue(torch)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -208,11 +208,17 @@ def test_install_gdn_fastpath_binds_hooks():
             self.chunk_gated_delta_rule = None
             self.causal_conv1d_update = None
 
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNormGated
+
     model = torch.nn.Sequential(Qwen3_5GatedDeltaNet(), torch.nn.Linear(2, 2), Qwen3_5GatedDeltaNet())
+    model[2].norm = Qwen3_5RMSNormGated(8)
     assert install_gdn_fastpath(model) == 2
     assert model[0].recurrent_gated_delta_rule is fused_recurrent_gated_delta_rule
     assert model[2].chunk_gated_delta_rule is chunk_gated_delta_rule
     assert model[2].causal_conv1d_update is causal_conv1d_update
+    # the output norm now runs the kernel: on CPU tensors it refuses loudly
+    with pytest.raises(RuntimeError, match="CUDA"):
+        model[2].norm(torch.zeros(2, 8), torch.zeros(2, 8))
 
 
 def test_conv_hook_rejects_unsupported_arguments():

@@ -128,3 +128,29 @@ def test_causal_conv1d_update_matches_transformers(gdn_gold):
     y = ogdn.causal_conv1d_update(g["conv_x"], state, g["conv_w"])
     np.testing.assert_allclose(y, g["conv_y"], rtol=1e-5, atol=1e-6)
     np.testing.assert_array_equal(state, g["conv_state_after"])
+
+
+# ---- output epilogues (gated RMSNorm of the GDN output, sigmoid gate of the attention output)
+def _bf16_from_bits(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_rmsnorm_gated_matches_transformers():
+    from oracle import epilogue as ep
+    from oracle import kv_quant as kq
+
+    g = np.load(GOLD / "epilogue_golden.npz")
+    x, z, w = (_bf16_from_bits(g[k]) for k in ("norm_x", "norm_z", "norm_w"))
+    want = _bf16_from_bits(g["norm_y"])
+    got = ep.rmsnorm_gated(x, z, w, float(g["norm_eps"]), rnd=kq.round_bf16)
+    assert np.array_equal(got, want)
+
+
+def test_sigmoid_gate_matches_reference_expression():
+    from oracle import epilogue as ep
+    from oracle import kv_quant as kq
+
+    g = np.load(GOLD / "epilogue_golden.npz")
+    got = ep.sigmoid_gate(_bf16_from_bits(g["gate_attn"]), _bf16_from_bits(g["gate_g"]), rnd=kq.round_bf16)
+    want = _bf16_from_bits(g["gate_y"])
+    assert np.array_equal(got, want)
