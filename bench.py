@@ -43,6 +43,9 @@ FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tokens/s (hybrid 24-layer hot path: GDN step + INT4 paged attention)"
 
 
+EPILOGUES = "attention * sigmoid(gate) and GDN gated RMSNorm, fused into the kernels' stores"
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -54,6 +57,9 @@ def parse_args(argv=None):
     ap.add_argument("--conv", choices=["separate", "fused"], default=None,
                     help="hybrid/serving: feed each GDN layer its raw projection output and run its causal conv1d "
                          "update (separate kernel, or fused into the GDN step)")
+    ap.add_argument("--epilogues", action="store_true",
+                    help="hybrid/serving: include the layers' output epilogues (attention * sigmoid(gate), GDN "
+                         "gated RMSNorm), fused into the kernels' stores; the CPU legs run them too")
     ap.add_argument("--small", action="store_true",
                     help="prefill workload only: a reduced case (B=4, T=8192, 2 layers, 8 decode steps) for ncu captures")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
@@ -181,8 +187,10 @@ def build_stack(args, world, rank, device):
 
     if args.workload == "hybrid":
         shape = HybridShape(batch=64, context=4096)
-        stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv)
+        stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv,
+                                  epilogues=args.epilogues)
         desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+                "epilogues": EPILOGUES if args.epilogues else "none",
                 "workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
                             "INT4 paged KV, page 64, permuted pages), 3:1 interleave, hidden 2048",
@@ -194,8 +202,10 @@ def build_stack(args, world, rank, device):
     shards = shard_by_cost(lengths, world)
     mine = [lengths[i] for i in shards[rank]]
     shape = HybridShape(batch=len(mine), context=mine)
-    stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv)
+    stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv,
+                              epilogues=args.epilogues)
     desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+            "epilogues": EPILOGUES if args.epilogues else "none",
             "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
                         "cost across GPUs, 24-layer hybrid hot path", "global_batch": 1024,
             "batch_this_rank": len(mine), "layers": 24, "l2": "no flush: working set far above L2",
@@ -301,7 +311,7 @@ def run_b200(args):
                      "frac": round(step_bytes / ms_local / 1e6 / hbm_peak, 4)},
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(stack.shape, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(stack.shape, args.cpu_seconds, args.epilogues)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph, stack
@@ -315,11 +325,12 @@ class OracleStep:
     per attention layer the reference quantiser on the new token, dequantisation of the whole
     INT4 cache and fp32 attention; per GDN layer the recurrent gated delta rule."""
 
-    def __init__(self, shape, seqs: int, layer_fraction: float = 1.0, seed: int = 0):
+    def __init__(self, shape, seqs: int, layer_fraction: float = 1.0, seed: int = 0, epilogues: bool = False):
         import numpy as np
 
         rng = np.random.default_rng(seed)
         self.shape = shape
+        self.epilogues = epilogues
         self.seqs = seqs
         ctx = max(shape.lengths)
         hkv, d, h, dk = shape.num_kv_heads, shape.head_dim, shape.gdn_heads, shape.gdn_dim
@@ -335,9 +346,13 @@ class OracleStep:
         self.gq = rng.standard_normal((1, 1, h, dk)).astype(np.float32)
         self.gg = -np.logaddexp(0, rng.standard_normal((1, 1, h))).astype(np.float32)
         self.gb = (1 / (1 + np.exp(-rng.standard_normal((1, 1, h))))).astype(np.float32)
+        self.gate = rng.standard_normal((1, shape.num_heads, d)).astype(np.float32)
+        self.z = rng.standard_normal((1, 1, h, dk)).astype(np.float32)
+        self.norm_w = (1.0 + 0.1 * rng.standard_normal(dk)).astype(np.float32)
 
     def one_sequence(self) -> None:
         from oracle import attention as oattn
+        from oracle import epilogue as ep
         from oracle import gdn as ogdn
         from oracle import kv_quant as kq
 
@@ -345,9 +360,13 @@ class OracleStep:
             kq.quantize_tokens_int4(self.knew)
             k = kq.dequantize_tokens_int4(self.codes[:, 0], self.meta[:, 0], self.meta[:, 1])
             v = kq.dequantize_tokens_int4(self.codes[:, 1], self.meta[:, 2], self.meta[:, 3])
-            oattn.decode_attention(self.q, [k], [v], self.shape.head_dim ** -0.5)
+            o, _ = oattn.decode_attention(self.q, [k], [v], self.shape.head_dim ** -0.5)
+            if self.epilogues:
+                ep.sigmoid_gate(o, self.gate, rnd=kq.round_bf16)
         for _ in range(self.n_gdn):
-            ogdn.recurrent_gated_delta_rule(self.gq, self.gq, self.gq, self.gg, self.gb, self.state, True, True)
+            o, _ = ogdn.recurrent_gated_delta_rule(self.gq, self.gq, self.gq, self.gg, self.gb, self.state, True, True)
+            if self.epilogues:
+                ep.rmsnorm_gated(kq.round_bf16(o), self.z, self.norm_w, 1e-6, rnd=kq.round_bf16)
 
     def run(self, pool) -> float:
         """Process `seqs` sequences on the thread pool; return seconds per full 24-layer token."""
@@ -356,11 +375,11 @@ class OracleStep:
         return (time.perf_counter() - t0) * self.scale_layers / self.seqs
 
 
-def cpu_baseline(shape, budget_s: float):
+def cpu_baseline(shape, budget_s: float, epilogues: bool = False):
     import concurrent.futures as cf
 
     cores = os.cpu_count() or 1
-    step = OracleStep(shape, seqs=cores)
+    step = OracleStep(shape, seqs=cores, epilogues=epilogues)
     with cf.ThreadPoolExecutor(cores) as pool:
         step.run(pool)                                     # warm-up
         t0, times = time.perf_counter(), []
@@ -384,20 +403,21 @@ def run_reference(args):
     if args.workload == "hybrid":
         shape = HybridShape(batch=64, context=4096)
         desc = {"workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers (18 GDN + 6 full "
-                            "attention), sampled on the host CPU", "global_batch": 64 * world}
+                            "attention), sampled on the host CPU", "global_batch": 64 * world,
+                "epilogues": EPILOGUES if args.epilogues else "none"}
     else:
         shape = HybridShape(batch=1024, context=serving_lengths())
         desc = {"workload": "batched serving: B=1024 ragged, context U[256,8192], sampled on the host CPU",
                 "global_batch": 1024}
     cores = os.cpu_count() or 1
     # size the per-step sample so warmup + steps stay within ~3 minutes
-    probe = OracleStep(shape, seqs=1)
+    probe = OracleStep(shape, seqs=1, epilogues=args.epilogues)
     with cf.ThreadPoolExecutor(cores) as pool:
         t_seq = probe.run(pool)
         budget_per_step = 150.0 / max(1, args.steps + args.warmup)
         frac = min(1.0, budget_per_step / max(t_seq, 1e-9))
         seqs = max(1, min(cores, int(budget_per_step / max(t_seq, 1e-9))))
-        step = OracleStep(shape, seqs=seqs, layer_fraction=frac if seqs == 1 else 1.0)
+        step = OracleStep(shape, seqs=seqs, layer_fraction=frac if seqs == 1 else 1.0, epilogues=args.epilogues)
         for _ in range(args.warmup):
             step.run(pool)
         times = [step.run(pool) for _ in range(args.steps)]

@@ -228,12 +228,17 @@ int oq_gdn_recurrent(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int flags, void* stream);
 
-/* oq_gdn_recurrent with the GDN layer's output norm fused into the store:
+/* oq_gdn_recurrent with the GDN layer's output norm fused in:
  * out = Qwen3_5RMSNormGated(o, z) per head (transformers models/qwen3_5/modeling_qwen3_5.py:175-190,
  * applied at :527-529) = rnd(rnd(rnd(o * rsqrt(mean(o^2) + norm_eps)) * w) * silu(z)), with o
  * first rounded to qkv_dtype as the unfused layer hands it on.  z [batch, seq_len, num_heads,
  * v_dim] in qkv_dtype (element strides b, t, h; unit stride along v_dim), norm_weight [v_dim]
- * in qkv_dtype.  The four column-slice CTAs of a head run as one thread-block cluster. */
+ * in qkv_dtype.  norm_workspace: oq_gdn_norm_workspace_bytes(batch, num_heads) bytes,
+ * zero-filled once before first use; every launch leaves it zero (launches sharing one must
+ * be ordered on a stream).  The last of a head's four column-slice CTAs to finish normalises
+ * the head's outputs, so none waits for another. */
+size_t oq_gdn_norm_workspace_bytes(int64_t batch, int64_t num_heads);
+
 int oq_gdn_recurrent_norm(
     const void* q, const void* k, const void* v, int qkv_dtype,
     int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
@@ -244,7 +249,8 @@ int oq_gdn_recurrent_norm(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm,
     const void* z, int64_t z_stride_b, int64_t z_stride_t, int64_t z_stride_h,
-    const void* norm_weight, float norm_eps, int flags, void* stream);
+    const void* norm_weight, float norm_eps, void* norm_workspace, size_t norm_workspace_bytes,
+    int flags, void* stream);
 
 /* One GDN decode token with the layer's causal conv1d update fused in front of it.
  * Replaces, for the decode branch of Qwen3_5GatedDeltaNet.forward
@@ -279,7 +285,7 @@ int oq_gdn_conv_step_norm(
     int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm,
     const void* z, int64_t z_stride_b, int64_t z_stride_h, const void* norm_weight, float norm_eps,
-    int flags, void* stream);
+    void* norm_workspace, size_t norm_workspace_bytes, int flags, void* stream);
 
 /* Gated RMSNorm as a standalone op: replaces Qwen3_5RMSNormGated.forward
  * (transformers models/qwen3_5/modeling_qwen3_5.py:175-190) for callers that keep the

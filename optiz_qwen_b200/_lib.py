@@ -50,9 +50,10 @@ SIGNATURES = {
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p]),
     "oq_gdn_recurrent_norm": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                     p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32,
-                                    p, i64, i64, i64, p, f32, i32, p]),
+                                    p, i64, i64, i64, p, f32, p, sz, i32, p]),
+    "oq_gdn_norm_workspace_bytes": (sz, [i64, i64]),
     "oq_gdn_conv_step_norm": (i32, [p, i32, i64, p, p, p, i32, i64, i64, p, i32, p, i32, p, p, p, i64, i64, i64,
-                                    i64, f32, i32, p, i64, i64, p, f32, i32, p]),
+                                    i64, f32, i32, p, i64, i64, p, f32, p, sz, i32, p]),
     "oq_rmsnorm_gated": (i32, [p, i64, p, i64, p, p, i64, i32, i64, i64, f32, p]),
     "oq_causal_conv1d_update": (i32, [p, i32, i64, i64, i64, p, p, p, i32, p, i64, i64, i64, i64, i64, i32, p]),
     "oq_gdn_conv_step": (i32, [p, i32, i64, p, p, p, i32, i64, i64, p, i32, p, i32, p, p, p, i64, i64, i64, i64,

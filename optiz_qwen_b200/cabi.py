@@ -205,12 +205,14 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
                   use_qk_l2norm: bool = False, prefetch_state: bool = False, z: torch.Tensor | None = None,
-                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6) -> torch.Tensor:
+                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+                  norm_workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Gated delta rule over ``T`` tokens: q, k ``[B, T, H, Dk]``, v ``[B, T, H, Dv]``, g/beta ``[B, T, H]``.
 
     Writes ``final_state`` (may alias ``initial_state``) and returns ``out`` ``[B, T, H, Dv]``.
     With ``z`` ``[B, T, H, Dv]`` and ``norm_weight`` ``[Dv]`` (qkv dtype) the layer's gated
-    RMSNorm is fused into the store (``oq_gdn_recurrent_norm``): ``out = RMSNormGated(o, z)``.
+    RMSNorm is fused in (``oq_gdn_recurrent_norm``): ``out = RMSNormGated(o, z)``; its zeroed
+    counter workspace (:func:`new_gdn_norm_workspace`) is allocated when not given.
     ``prefetch_state`` (``OQ_GDN_STATE_PREFETCH``) lets the kernel read the state while the
     preceding kernel in the stream is still running: only for callers that know no such
     kernel writes it (a decode step, where layer l's state was written one step earlier).
@@ -239,13 +241,16 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
         if z.dtype != q.dtype or tuple(z.shape) != (bsz, t, h, dv) or z.stride(3) != 1:
             raise ValueError("z must be [B, T, H, Dv] in the qkv dtype with unit stride along Dv")
         norm_weight = norm_weight.to(q.dtype).contiguous()
+        if norm_workspace is None:
+            norm_workspace = new_gdn_norm_workspace(bsz, h, q.device)
         call("oq_gdn_recurrent_norm", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
              q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
              v.stride(0), v.stride(1), v.stride(2),
              ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
              ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
              ptr(z), z.stride(0), z.stride(1), z.stride(2), ptr(norm_weight), float(norm_eps),
-             GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(q.device))
+             ptr(norm_workspace), norm_workspace.numel(), GDN_STATE_PREFETCH if prefetch_state else 0,
+             stream_ptr(q.device))
         return out
     call("oq_gdn_recurrent", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
          q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
@@ -258,6 +263,12 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
 
 GDN_STATE_PREFETCH = 1
 CHUNK_SIZE = 64
+
+
+def new_gdn_norm_workspace(batch: int, num_heads: int, device: torch.device) -> torch.Tensor:
+    """Zeroed counters for the fused gated-RMSNorm epilogue of ``batch x num_heads`` heads."""
+    nbytes = int(_lib.load().oq_gdn_norm_workspace_bytes(batch, num_heads))
+    return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
 
 
 def causal_conv1d_update(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
@@ -287,7 +298,8 @@ def gdn_conv_step(qkv: torch.Tensor, conv_state: torch.Tensor, conv_weight: torc
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
                   use_qk_l2norm: bool = True, prefetch_state: bool = False, z: torch.Tensor | None = None,
-                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6) -> torch.Tensor:
+                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+                  norm_workspace: torch.Tensor | None = None) -> torch.Tensor:
     """One GDN decode token with the causal conv1d update fused in: qkv ``[B, C]`` (the projection
     output, q heads | k heads | v heads), conv_state ``[B, C, W]`` and the recurrent state are updated
     in place; returns ``out`` ``[B, 1, H, 128]``.  With ``z`` ``[B, H, 128]`` and ``norm_weight`` the
@@ -318,12 +330,15 @@ def gdn_conv_step(qkv: torch.Tensor, conv_state: torch.Tensor, conv_weight: torc
         if z.dtype != qkv.dtype or tuple(z.shape) != (bsz, num_heads, dv) or z.stride(2) != 1:
             raise ValueError("z must be [B, H, 128] in the qkv dtype with unit stride along the last dim")
         norm_weight = norm_weight.to(qkv.dtype).contiguous()
+        if norm_workspace is None:
+            norm_workspace = new_gdn_norm_workspace(bsz, num_heads, qkv.device)
         call("oq_gdn_conv_step_norm", ptr(qkv), dtype_code(qkv.dtype), qkv.stride(0), ptr(conv_state),
              ptr(conv_weight), ptr(conv_bias), dtype_code(conv_weight.dtype), conv_state.shape[-1],
              conv_weight.shape[-1], ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
              ptr(initial_state), ptr(final_state), ptr(out), bsz, num_heads, dk, dv, float(scale),
              int(use_qk_l2norm), ptr(z), z.stride(0), z.stride(1), ptr(norm_weight), float(norm_eps),
-             GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(qkv.device))
+             ptr(norm_workspace), norm_workspace.numel(), GDN_STATE_PREFETCH if prefetch_state else 0,
+             stream_ptr(qkv.device))
         return out
     call("oq_gdn_conv_step", ptr(qkv), dtype_code(qkv.dtype), qkv.stride(0), ptr(conv_state), ptr(conv_weight),
          ptr(conv_bias), dtype_code(conv_weight.dtype), conv_state.shape[-1], conv_weight.shape[-1],

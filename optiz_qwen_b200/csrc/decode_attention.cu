@@ -537,11 +537,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     const int h = e / kHeadDim;
     const int d = e - h * kHeadDim;
     const float M = tail->head_m[h], L = tail->head_l[h];
+    const float gv = single ? gate_value<T>(p, b, int64_t(kvh) * G + h, d) : 0.0f;
     float num = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) num += red[red_index(w, h, d)];
     if (single) {
-      store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
+      store_out_g<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L, gv);
     } else {
       my_rec[e] = num;
       if (d == 0) {

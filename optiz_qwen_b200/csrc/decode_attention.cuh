@@ -60,17 +60,23 @@ __device__ __forceinline__ float lse_nat(float m_log2, float l) {
   return l > 0.0f ? (m_log2 + log2f(l)) * 0.69314718055994531f : -INFINITY;
 }
 
-// The model-dtype output, gated if asked: the decode forward's
-// ``attn_output * torch.sigmoid(gate)`` (optiz_qwen/kernels/qwen35_fused_attention.py:96-97)
-// with each operand rounded to the model dtype as the unfused ops leave it.
+// Gate element of output (b, hq, d), 0 without a gate.
 template <typename T>
-__device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
-                                          float l) {
+__device__ __forceinline__ float gate_value(const AttnParams& p, int64_t b, int64_t hq, int d) {
+  return p.gate ? to_float<T>(static_cast<const T*>(p.gate)[b * p.g_sb + hq * p.g_sh + d]) : 0.0f;
+}
+
+// The model-dtype output, gated if asked (g = the gate element, loaded ahead): the decode
+// forward's ``attn_output * torch.sigmoid(gate)``
+// (optiz_qwen/kernels/qwen35_fused_attention.py:96-97) with each operand rounded to the
+// model dtype as the unfused ops leave it.
+template <typename T>
+__device__ __forceinline__ void store_out_g(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
+                                            float l, float g) {
   const int64_t hq_total = p.num_kv_heads * p.group;
   if (p.out) {
     T y = from_float<T>(o);
     if (p.gate) {
-      const float g = to_float<T>(static_cast<const T*>(p.gate)[b * p.g_sb + hq * p.g_sh + d]);
       const float sg = to_float<T>(from_float<T>(1.0f / (1.0f + expf(-g))));
       y = from_float<T>(to_float<T>(y) * sg);
     }
@@ -78,6 +84,12 @@ __device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_
   }
   if (p.out_f32) p.out_f32[(b * hq_total + hq) * kHeadDim + d] = o;
   if (p.out_lse && d == 0) p.out_lse[b * hq_total + hq] = lse_nat(m, l);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int64_t hq, int d, float o, float m,
+                                          float l) {
+  store_out_g<T>(p, b, hq, d, o, m, l, gate_value<T>(p, b, hq, d));
 }
 
 // Split-KV merge, run by the kNT threads [0, kNT) of every CTA of a (sequence, KV head)
@@ -93,6 +105,14 @@ __device__ void merge_splits_last_cta(const AttnParams& p, int64_t b, int kvh, i
   const int outputs = G * kHeadDim;
   const int64_t unit = b * p.num_kv_heads + kvh;
   const int rec_floats = G * (kHeadDim + 2);
+  constexpr int kMaxPer = kMaxGroup * kHeadDim / kNT;
+  const int per = outputs / kNT;
+  float gv[kMaxPer];  // gate elements of this thread's outputs, in flight across the atomic
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const int e = tid + j * kNT;
+    gv[j] = j < per ? gate_value<T>(p, b, int64_t(kvh) * G + e / kHeadDim, e % kHeadDim) : 0.0f;
+  }
   __threadfence();
   named_bar_sync(bar_id, kNT);
   if (tid == 0) {
@@ -131,8 +151,6 @@ __device__ void merge_splits_last_cta(const AttnParams& p, int64_t b, int kvh, i
     wm[idx] = M == -INFINITY ? 0.0f : exp2f(wm[idx] - M);
   }
   named_bar_sync(bar_id, kNT);
-  constexpr int kMaxPer = kMaxGroup * kHeadDim / kNT;
-  const int per = outputs / kNT;
   float num[kMaxPer];
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) num[j] = 0.0f;
@@ -152,7 +170,8 @@ __device__ void merge_splits_last_cta(const AttnParams& p, int64_t b, int kvh, i
       const int e = tid + j * kNT;
       const int h = e / kHeadDim;
       const float L = head_l[h];
-      store_out<T>(p, b, int64_t(kvh) * G + h, e - h * kHeadDim, L > 0.0f ? num[j] / L : 0.0f, head_m[h], L);
+      store_out_g<T>(p, b, int64_t(kvh) * G + h, e - h * kHeadDim, L > 0.0f ? num[j] / L : 0.0f, head_m[h], L,
+                     gv[j]);
     }
   }
   if (tid == 0) p.counters[unit] = 0;  // ready for the next launch

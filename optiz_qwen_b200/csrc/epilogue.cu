@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(kNormWarps * 32) rmsnorm_gated_kernel(const T*
                                                                         int dim, float eps) {
   const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  pdl_wait();        // x comes from the preceding kernel
+  pdl_allow_next();  // the successor may launch: this kernel is a few microseconds of tail
   if (row >= rows) return;
   const T* xr = x + row * xs;
   const T* zr = z + row * zs;
@@ -53,7 +55,7 @@ template <typename T>
 void launch_norm(const void* x, int64_t xs, const void* z, int64_t zs, const void* w, void* out, int64_t os,
                  int64_t rows, int64_t dim, float eps, cudaStream_t s) {
   const dim3 grid(unsigned((rows + kNormWarps - 1) / kNormWarps));
-  launch_plain(rmsnorm_gated_kernel<T>, grid, dim3(kNormWarps * 32), 0, s, static_cast<const T*>(x), xs,
+  launch_pdl(rmsnorm_gated_kernel<T>, grid, dim3(kNormWarps * 32), 0, s, static_cast<const T*>(x), xs,
                static_cast<const T*>(z), zs, static_cast<const T*>(w), static_cast<T*>(out), os, rows, int(dim), eps);
 }
 

@@ -12,9 +12,11 @@
 // 4-warp shared-memory step.
 //
 // Optional gated RMSNorm epilogue: the GDN layer's Qwen3_5RMSNormGated(o, z)
-// (modeling_qwen3_5.py:175-190, call site :527-529) applied to each head's 128 outputs
-// before they are stored.  The four column-slice CTAs of a head then run as one cluster
-// and add their partial sums of squares through distributed shared memory.
+// (modeling_qwen3_5.py:175-190, call site :527-529) over each head's 128 outputs.  The
+// four column-slice CTAs of a head store their outputs as usual and count themselves in
+// on a per-(sequence, head) counter; the last to arrive reads the head's outputs back
+// (from L2) and rewrites them normalised.  No CTA waits for another (a cluster-wide
+// exchange measured ~8 us slower per launch on B200).
 #include <cmath>
 
 #include "common.cuh"
@@ -53,6 +55,7 @@ struct GdnParams {
   int64_t zs[3];
   const void* norm_w;  // [Dv] in T
   float norm_eps;
+  int* norm_counters;  // [B * H] zeroed; every launch leaves them zero
 };
 
 constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
@@ -85,24 +88,13 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.aligned;\nbarrier.cluster.wait.aligned;\n" ::: "memory");
 }
 
-// Shared-memory address of `p` in the CTA of cluster rank `rank`, and a load from it.
-__device__ __forceinline__ uint32_t cluster_map_shared(const void* p, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
-  return out;
-}
-__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
 template <typename T, bool kConv, bool kNorm>
 __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
   __shared__ float q_s[kDk], k_s[kDk], v_s[kCols];
   __shared__ float red_kv[4][kCols], red_o[4][kCols];
   __shared__ float norm_q[4], norm_k[4];
-  __shared__ float norm_part;  // this slice's sum of squares of the (model-dtype) outputs
+  __shared__ float norm_red[4];
+  __shared__ int norm_last;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -239,39 +231,43 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) red_o[warp][4 * cg + j] = o[j];
     }
-    float zv = 0.0f, wv = 0.0f;
-    if (kNorm && tid < kCols) {
-      zv = to_float<T>(static_cast<const T*>(p.z)[b * p.zs[0] + t * p.zs[1] + h * p.zs[2] + v0 + tid]);
-      wv = to_float<T>(static_cast<const T*>(p.norm_w)[v0 + tid]);
+    __syncthreads();
+    if (tid < kCols) {
+      const float ov = (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]);
+      static_cast<T*>(p.out)[((b * p.seq_len + t) * H + h) * kDv + v0 + tid] = from_float<T>(ov);
+    }
+  }
+
+  if constexpr (kNorm) {
+    // ---- gated RMSNorm by the last of the head's four slice CTAs: its outputs, in the model
+    // dtype as the unfused layer hands them to the norm, are read back for every token
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int done = atomicAdd(&p.norm_counters[b * H + h], 1);
+      norm_last = done == kDv / kCols - 1;
     }
     __syncthreads();
-    T* orow = static_cast<T*>(p.out) + ((b * p.seq_len + t) * H + h) * kDv + v0;
-    const float ov = tid < kCols ? (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]) : 0.0f;
-    if constexpr (!kNorm) {
-      if (tid < kCols) orow[tid] = from_float<T>(ov);
-    } else {
-      // o in the model dtype (as the unfused layer hands it to the norm), its squares summed
-      // over the head's 128 columns by the 4 CTAs of the cluster
-      const float orr = to_float<T>(from_float<T>(ov));
-      if (warp == 0) {
-        float ss = orr * orr;
+    if (norm_last) {
+      __threadfence();
+      const float wv = to_float<T>(static_cast<const T*>(p.norm_w)[tid]);
+      for (int64_t t = 0; t < p.seq_len; ++t) {
+        T* orow = static_cast<T*>(p.out) + ((b * p.seq_len + t) * H + h) * kDv;
+        const float zv = to_float<T>(static_cast<const T*>(p.z)[b * p.zs[0] + t * p.zs[1] + h * p.zs[2] + tid]);
+        const float ov = to_float<T>(__ldcg(orow + tid));
+        float ss = ov * ov;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) norm_part = ss;
-      }
-      cluster_sync();
-      float tot = 0.0f;
-      if (warp == 0) {
-#pragma unroll
-        for (uint32_t rank = 0; rank < kDv / kCols; ++rank) tot += ld_shared_cluster_f32(cluster_map_shared(&norm_part, rank));
-      }
-      cluster_sync();  // every CTA has read the partials: they may change (next token) or go (exit)
-      if (tid < kCols) {
+        if (lane == 0) norm_red[warp] = ss;
+        __syncthreads();
+        const float tot = (norm_red[0] + norm_red[1]) + (norm_red[2] + norm_red[3]);
         const float inv = 1.0f / sqrtf(tot * (1.0f / kDv) + p.norm_eps);
-        const float nrm = to_float<T>(from_float<T>(orr * inv));
+        const float nrm = to_float<T>(from_float<T>(ov * inv));
         const float y = to_float<T>(from_float<T>(wv * nrm));
         orow[tid] = from_float<T>(y * (zv / (1.0f + expf(-zv))));
+        __syncthreads();  // norm_red is reused by the next token
       }
+      if (tid == 0) p.norm_counters[b * H + h] = 0;  // ready for the next launch
     }
   }
 
@@ -293,7 +289,7 @@ void launch_gdn(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnP
   }
 }
 
-// The fused conv and norm variants run the four column slices of a head as one cluster.
+// The fused conv variant runs the four column slices of a head as one cluster.
 cudaError_t launch_gdn_cluster(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -317,6 +313,8 @@ struct NormArgs {
   int64_t zs[3];
   const void* weight;
   float eps;
+  int* counters;
+  size_t counter_bytes;
 };
 
 template <bool kConv>
@@ -335,8 +333,12 @@ void (*gdn_kernel_for(int dtype, bool norm))(GdnParams) {
   }
 }
 
-int check_norm(const NormArgs* norm, const char* what) {
+int check_norm(const NormArgs* norm, int64_t batch, int64_t num_heads, const char* what) {
   if (norm && (!norm->z || !norm->weight)) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: null gate or norm weight", what);
+  if (norm && (!norm->counters || norm->counter_bytes < size_t(batch * num_heads) * sizeof(int))) {
+    return fail(OQ_ERR_WORKSPACE, "%s: norm workspace of %zu bytes needed", what,
+                size_t(batch * num_heads) * sizeof(int));
+  }
   if (norm && !(norm->eps >= 0.0f)) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: norm eps must be >= 0", what);
   return OQ_OK;
 }
@@ -348,6 +350,7 @@ void set_norm(GdnParams& p, const NormArgs* norm) {
   p.zs[2] = norm ? norm->zs[2] : 0;
   p.norm_w = norm ? norm->weight : nullptr;
   p.norm_eps = norm ? norm->eps : 0.0f;
+  p.norm_counters = norm ? norm->counters : nullptr;
 }
 
 int gdn_recurrent_impl(
@@ -359,7 +362,7 @@ int gdn_recurrent_impl(
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, const NormArgs* norm, int flags, void* stream) {
-  if (int st = check_norm(norm, "gdn_recurrent"); st != OQ_OK) return st;
+  if (int st = check_norm(norm, batch, num_heads, "gdn_recurrent"); st != OQ_OK) return st;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
   }
@@ -396,11 +399,7 @@ int gdn_recurrent_impl(
   set_norm(p, norm);
   dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (norm) {
-    launch_gdn_cluster(gdn_kernel_for<false>(qkv_dtype, true), grid, s, p);
-  } else {
-    launch_gdn(gdn_kernel_for<false>(qkv_dtype, false), grid, s, p);
-  }
+  launch_gdn(gdn_kernel_for<false>(qkv_dtype, norm != nullptr), grid, s, p);
   return check_launch("gdn_recurrent");
 }
 
@@ -412,7 +411,7 @@ int gdn_conv_step_impl(
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, const NormArgs* norm, int flags, void* stream) {
-  if (int st = check_norm(norm, "gdn_conv_step"); st != OQ_OK) return st;
+  if (int st = check_norm(norm, batch, num_heads, "gdn_conv_step"); st != OQ_OK) return st;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype) || !valid_dtype(conv_w_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_conv_step: unknown dtype");
   }
@@ -485,8 +484,10 @@ extern "C" int oq_gdn_recurrent_norm(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm,
     const void* z, int64_t z_stride_b, int64_t z_stride_t, int64_t z_stride_h,
-    const void* norm_weight, float norm_eps, int flags, void* stream) {
-  const oq::NormArgs norm = {z, {z_stride_b, z_stride_t, z_stride_h}, norm_weight, norm_eps};
+    const void* norm_weight, float norm_eps, void* norm_workspace, size_t norm_workspace_bytes,
+    int flags, void* stream) {
+  const oq::NormArgs norm = {z, {z_stride_b, z_stride_t, z_stride_h}, norm_weight, norm_eps,
+                             static_cast<int*>(norm_workspace), norm_workspace_bytes};
   return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
                                 k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
                                 initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
@@ -516,10 +517,16 @@ extern "C" int oq_gdn_conv_step_norm(
     int64_t batch, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm,
     const void* z, int64_t z_stride_b, int64_t z_stride_h, const void* norm_weight, float norm_eps,
-    int flags, void* stream) {
-  const oq::NormArgs norm = {z, {z_stride_b, 0, z_stride_h}, norm_weight, norm_eps};
+    void* norm_workspace, size_t norm_workspace_bytes, int flags, void* stream) {
+  const oq::NormArgs norm = {z, {z_stride_b, 0, z_stride_h}, norm_weight, norm_eps,
+                             static_cast<int*>(norm_workspace), norm_workspace_bytes};
   return oq::gdn_conv_step_impl(qkv, qkv_dtype, qkv_stride_b, conv_state, conv_weight, conv_bias, conv_w_dtype,
                                 conv_width, conv_kernel_size, g, g_dtype, beta, beta_dtype, initial_state,
                                 final_state, out, batch, num_heads, k_dim, v_dim, scale, use_qk_l2norm, &norm, flags,
                                 stream);
+}
+
+extern "C" size_t oq_gdn_norm_workspace_bytes(int64_t batch, int64_t num_heads) {
+  if (batch <= 0 || num_heads <= 0) return 0;
+  return size_t((batch * num_heads * int64_t(sizeof(int)) + 255) / 256 * 256);
 }

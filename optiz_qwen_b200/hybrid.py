@@ -60,6 +60,7 @@ class _AttnLayer:
     q: torch.Tensor = None
     k: torch.Tensor = None
     v: torch.Tensor = None
+    gate: torch.Tensor = None    # [B, Hq, D] output gate (with epilogues)
     out: torch.Tensor = None
 
 
@@ -75,6 +76,8 @@ class _GdnLayer:
     v: torch.Tensor = None
     g: torch.Tensor = None
     beta: torch.Tensor = None
+    z: torch.Tensor = None           # [B, 1, H, Dv] gate of the output norm (with epilogues)
+    norm_w: torch.Tensor = None      # [Dv] weight of the output norm
     out: torch.Tensor = None
 
 
@@ -102,6 +105,12 @@ class HybridDecodeStack:
     ``"fused"`` the single-launch ``oq_gdn_conv_step`` (slower on B200, measured: the four
     column-slice CTAs of a head each convolve q/k and synchronise as a cluster).  With
     ``conv=None`` q/k/v are given post-conv.
+    ``epilogues=True`` adds the layers' output epilogues: the attention output gate
+    ``* sigmoid(gate)`` (q_proj's second half), fused into the attention kernel's store, and
+    the GDN output norm ``Qwen3_5RMSNormGated(o, z)`` (z = the z projection) as the
+    ``oq_rmsnorm_gated`` kernel right after the GDN step, in place.  The norm fused into the
+    GDN kernel (``oq_gdn_recurrent_norm``) measured slower on B200 in this step: its
+    end-of-CTA hand-off lengthens every CTA of the ~5.5-wave launch.
     """
 
     CONV_KERNEL = 4
@@ -110,11 +119,12 @@ class HybridDecodeStack:
 
     def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
                  hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16,
-                 conv: str | None = None):
+                 conv: str | None = None, epilogues: bool = False):
         if conv not in (None, "separate", "fused"):
             raise ValueError("conv must be None, 'separate' or 'fused'")
         self.shape = shape
         self.conv = conv
+        self.epilogues = epilogues
         self.device = torch.device(device)
         self.dtype = dtype
         self.hold_context = hold_context
@@ -134,6 +144,9 @@ class HybridDecodeStack:
                 state = torch.randn((b, shape.gdn_heads, shape.gdn_dim, shape.gdn_dim), generator=self.gen,
                                     device=self.device, dtype=torch.float32).mul_(0.02)
                 layer = _GdnLayer(state=state)
+                if epilogues:
+                    layer.norm_w = (1.0 + 0.1 * torch.randn(shape.gdn_dim, generator=self.gen,
+                                                            device=self.device)).to(dtype)
                 if conv:
                     ch = self.conv_channels
                     rnd = lambda *shp: torch.randn(shp, generator=self.gen, device=self.device)  # noqa: E731
@@ -195,6 +208,8 @@ class HybridDecodeStack:
                 in_specs += [(("attn", i, "q"), (b, s.num_heads, s.head_dim)),
                              (("attn", i, "k"), (b, s.num_kv_heads, 1, s.head_dim)),
                              (("attn", i, "v"), (b, s.num_kv_heads, 1, s.head_dim))]
+                if self.epilogues:
+                    in_specs += [(("attn", i, "gate"), (b, s.num_heads, s.head_dim))]
                 out_specs += [(("attn", i, "out"), (b, s.num_heads, s.head_dim))]
             else:
                 shp = (b, 1, s.gdn_heads, s.gdn_dim)
@@ -206,6 +221,8 @@ class HybridDecodeStack:
                 else:
                     in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp)]
                 in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
+                if self.epilogues:
+                    in_specs += [(("gdn", i, "z"), shp)]
                 out_specs += [(("gdn", i, "out"), shp)]
         n_in = sum(math.prod(shp) for _, shp in in_specs)
         n_out = sum(math.prod(shp) for _, shp in out_specs)
@@ -257,13 +274,15 @@ class HybridDecodeStack:
                     prev = ("append", i)
                 if "attn" in kinds:
                     cabi.decode_attention_int4(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
-                                               out=layer.out, workspace=layer.workspace)
+                                               out=layer.out, workspace=layer.workspace, gate=layer.gate)
                     prev = ("attn", i)
             elif "gdn" in kinds:
                 layer = self.gdn[i]
                 # A layer's state is written only by its own launch one step earlier, so when the
                 # launch right before this one is another layer's GDN step, this one may start
                 # early and load its state during that step's tail.
+                # (the launch right before may also be the previous GDN layer's output norm, which
+                # writes that layer's output, not this layer's state)
                 chained = prev is not None and prev[0] == "gdn" and prev[1] != i
                 if self.conv == "fused":
                     cabi.gdn_conv_step(layer.qkv, layer.conv_state, layer.conv_w, layer.conv_b, layer.g, layer.beta,
@@ -281,6 +300,8 @@ class HybridDecodeStack:
                     cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
                                        final_state=layer.state, out=layer.out, use_qk_l2norm=True,
                                        prefetch_state=chained)
+                if layer.z is not None:
+                    cabi.rmsnorm_gated(layer.out, layer.z, layer.norm_w, 1e-6, out=layer.out)
                 prev = ("gdn", i)
 
     def capture(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
@@ -316,11 +337,15 @@ class HybridDecodeStack:
             esz = torch.tensor([], dtype=self.dtype).element_size()
             gdn_bytes_layer += (2 * s.batch * self.conv_channels * self.CONV_KERNEL
                                 + self.conv_channels * (self.CONV_KERNEL + 1)) * esz
+        if self.epilogues:  # gate / z reads and the norm weight (model dtype)
+            esz = torch.tensor([], dtype=self.dtype).element_size()
+            attn_bytes_layer += s.batch * s.num_heads * s.head_dim * esz
+            gdn_bytes_layer += (s.batch * s.gdn_heads + 1) * s.gdn_dim * esz
         append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.KV_BYTES_PER_TOKEN_HEAD)
         n_attn, n_gdn = len(self.attn), len(self.gdn)
         esize = self.in_dev.element_size()
         return StepCounts(
-            launches=2 * n_attn + n_gdn * (2 if self.conv == "separate" else 1),
+            launches=2 * n_attn + n_gdn * ((2 if self.conv == "separate" else 1) + (1 if self.epilogues else 0)),
             attn_bytes=attn_bytes_layer * n_attn,
             gdn_bytes=gdn_bytes_layer * n_gdn,
             append_bytes=append_bytes_layer * n_attn,

@@ -107,8 +107,9 @@ def test_gdn_recurrent_with_gated_norm(b, t, h):
     ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, g, beta, s0, True, True)
     assert_gdn_close(s_norm.cpu().numpy(), rs)
     ref = ep.rmsnorm_gated(kq.round_bf16(ro), z, w, 1e-6, rnd=kq.round_bf16)
-    # o agrees with the fp32 oracle to ~1e-4, i.e. up to one bf16 rounding step before the norm
-    _ulp_close(got, ref, ulps=3)
+    # o agrees with the fp32 oracle to 1e-4 of its largest element, which the norm carries to the output
+    # scale: bf16 rounding plus that error
+    assert np.all(np.abs(got - ref) <= 3 * 2.0 ** -7 * np.abs(ref) + 2e-3 * np.abs(ref).max())
 
 
 def test_gdn_conv_step_with_gated_norm():

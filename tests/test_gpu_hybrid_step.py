@@ -91,3 +91,51 @@ def test_graph_step_with_conv_matches_conv_then_recurrence(conv):
         assert_gdn_close(layer.state.cpu().numpy(), rs)
         got = f(layer.out)
         assert np.all(np.abs(got - ro) <= 2.0 ** -8 * np.abs(ro) + 1e-4 * np.abs(ro).max())
+
+
+@pytest.mark.parametrize("conv", [None, "fused"])
+def test_graph_step_with_epilogues(conv):
+    """The step with the output epilogues fused in: attention outputs are the oracle attention
+    times sigmoid(gate), GDN outputs the oracle recurrence through Qwen3_5RMSNormGated(o, z)."""
+    from oracle import epilogue as ep
+    from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
+
+    shape = HybridShape(batch=2, context=[40, 131], num_layers=4)
+    stack = HybridDecodeStack(shape, device="cuda", seed=9, conv=conv, epilogues=True)
+    stack.fill_inputs()
+    states0 = [layer.state.cpu().numpy().copy() for layer in stack.gdn]
+    conv0 = [layer.conv_state.float().cpu().numpy().copy() for layer in stack.gdn] if conv else None
+    graph = stack.capture()
+    for j, (layer, s0) in enumerate(zip(stack.gdn, states0)):
+        layer.state.copy_(torch.from_numpy(s0))
+        if conv:
+            layer.conv_state.copy_(torch.from_numpy(conv0[j]).to(layer.conv_state.dtype))
+    graph.replay()
+    torch.cuda.synchronize()
+
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    h, d = shape.gdn_heads, shape.gdn_dim
+    for j, (layer, s0) in enumerate(zip(stack.gdn, states0)):
+        if conv:
+            cst = conv0[j].copy()
+            y = kq.round_bf16(ogdn.causal_conv1d_update(f(layer.qkv)[:, :, None], cst, f(layer.conv_w),
+                                                        f(layer.conv_b), silu=True)[:, :, 0])
+            b = y.shape[0]
+            q, k, v = (y[:, i * h * d:(i + 1) * h * d].reshape(b, 1, h, d) for i in range(3))
+        else:
+            q, k, v = f(layer.q), f(layer.k), f(layer.v)
+        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, f(layer.g), f(layer.beta), s0, True, True)
+        assert_gdn_close(layer.state.cpu().numpy(), rs)
+        ref = ep.rmsnorm_gated(kq.round_bf16(ro), f(layer.z), f(layer.norm_w), 1e-6, rnd=kq.round_bf16)
+        got = f(layer.out)
+        # o carries the recurrence's 1e-4-of-max error into the norm: bf16 rounding plus that, at output scale
+        assert np.all(np.abs(got - ref) <= 3 * 2.0 ** -7 * np.abs(ref) + 2e-3 * np.abs(ref).max())
+
+    for layer in stack.attn:
+        p = layer.paged
+        cache = kq.PagedKvOracle(p.pool.kv_codes.shape[0], shape.num_kv_heads, shape.head_dim, shape.page_size,
+                                 p.block_table.cpu().numpy(), layer.attend_lens.cpu().numpy())
+        cache.kv_codes[...] = p.pool.kv_codes.cpu().numpy()
+        cache.kv_meta[...] = p.pool.kv_meta.cpu().numpy()
+        ref, _ = oracle_attention(cache, f(layer.q), shape.head_dim ** -0.5)
+        assert_attn_close(f(layer.out), ep.sigmoid_gate(ref, f(layer.gate), rnd=kq.round_bf16))
