@@ -12,6 +12,8 @@
  *   kv_codes  uint8   [num_pages, num_kv_heads, 2, page_size, head_dim/2]
  *             index 2: 0 = keys, 1 = values; byte j of a token row holds
  *             dimension 2j in its low nibble and 2j+1 in its high nibble.
+ *             The 8-bit cache (the *_int8 entry points) has rows of head_dim
+ *             bytes, one code per dimension, and the same meta.
  *   kv_meta   fp16    [num_pages, num_kv_heads, 4, page_size]
  *             index 4: 0 = key scale, 1 = key min, 2 = value scale, 3 = value min.
  *   block_table int32 [batch, block_table_stride]  physical page of each logical page.
@@ -90,6 +92,20 @@ int oq_append_quant_int4(
     int32_t* seq_lens, int advance_seq_lens,
     int32_t* device_status, void* stream);
 
+/* The 8-bit cache format (the reference's k_bits = v_bits = 8 path, _quantize_groupwise with
+ * bits = 8): codes [num_pages, num_kv_heads, 2, page_size, head_dim] one byte per element,
+ * 255 levels (round-half-even of (x - min) / scale clamped to [0, 255], scale = (max - min) / 255),
+ * same fp16 scale/min, same arguments and contract as oq_append_quant_int4. */
+int oq_append_quant_int8(
+    const void* key, const void* value, int dtype,
+    int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
+    int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
+    int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    int32_t* seq_lens, int advance_seq_lens,
+    int32_t* device_status, void* stream);
+
 /* seq_lens[b] += delta for b < batch (cache bookkeeping between steps). */
 int oq_advance_seq_lens(int32_t* seq_lens, int64_t batch, int32_t delta, void* stream);
 
@@ -131,6 +147,22 @@ int oq_decode_attn_int4_paged(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream);
 
+/* The same attention over the 8-bit cache of oq_append_quant_int8 (codes
+ * [num_pages, num_kv_heads, 2, page_size, head_dim], one byte per element): replaces
+ * qserve_int8_decode_attention and its Triton kernel (qserve_int4_attention.py:18-109,
+ * 548-573).  Same arguments and contract as oq_decode_attn_int4_paged. */
+int oq_decode_attn_int8_paged(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream);
+
 /* Same attention with the decode forward's output gate fused into the store:
  * out = rnd(rnd(o) * rnd(sigmoid(gate))) in the query dtype (rnd = rounding to it),
  * replacing ``attn_output * torch.sigmoid(gate)`` after the kernel
@@ -139,6 +171,20 @@ int oq_decode_attn_int4_paged(
  * not the query.  out is required; no fp32 / lse outputs (they feed merges, which
  * must see the ungated values). */
 int oq_decode_attn_int4_paged_gated(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream);
+
+/* The gated attention over the 8-bit cache; same arguments and contract as
+ * oq_decode_attn_int4_paged_gated. */
+int oq_decode_attn_int8_paged_gated(
     const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
     const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
@@ -194,6 +240,15 @@ int oq_lse_merge(const float* part_out, const float* part_lse,
  * Rows at or beyond a sequence's length are left untouched.
  */
 int oq_gather_dequant_int4(
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,
+    int64_t max_len, void* keys, void* values, int dtype,
+    int32_t* device_status, void* stream);
+
+/* The same gather over the 8-bit cache of oq_append_quant_int8 (the reference's
+ * _dequantize_groupwise with bits = 8, qserve_kv_cache.py:337-353, 126-135). */
+int oq_gather_dequant_int8(
     const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
     const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
     const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,

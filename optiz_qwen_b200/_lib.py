@@ -35,17 +35,25 @@ SIGNATURES = {
     "oq_abi_version": (i32, []),
     "oq_append_quant_int4": (i32, [p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                    p, p, i64, i64, p, i64, i64, p, i32, p, p]),
+    "oq_append_quant_int8": (i32, [p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                   p, p, i64, i64, p, i64, i64, p, i32, p, p]),
     "oq_advance_seq_lens": (i32, [p, i64, C.c_int32, p]),
     "oq_decode_attn_workspace_bytes": (sz, [i64, i64, i64, i64, i64]),
     "oq_decode_attn_int4_paged": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
+                                        i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, p]),
+    "oq_decode_attn_int8_paged": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                         i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, p]),
     "oq_decode_attn_int4_paged_noalloc": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                                 i64, i64, i64, i64, f32, p, i64, i64, p, p, i32, p, p]),
     "oq_decode_attn_int4_paged_gated": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                               i64, i64, i64, i64, f32, p, i64, i64, p, i64, i64, p, sz, i32, p,
                                               p]),
+    "oq_decode_attn_int8_paged_gated": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
+                                              i64, i64, i64, i64, f32, p, i64, i64, p, i64, i64, p, sz, i32, p,
+                                              p]),
     "oq_lse_merge": (i32, [p, p, i64, i64, i64, p, i32, p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
+    "oq_gather_dequant_int8": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p]),
     "oq_gdn_recurrent_norm": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,

@@ -21,24 +21,28 @@ PAGE_SIZE = 64
 
 
 class PagedKvPool:
-    """Device storage of one layer's paged INT4 KV cache.
+    """Device storage of one layer's paged INT4 (or INT8) KV cache.
 
-    ``kv_codes`` uint8 ``[num_pages, Hkv, 2, page_size, D/2]`` (0 = K, 1 = V) and
+    ``kv_codes`` uint8 ``[num_pages, Hkv, 2, page_size, D * bits / 8]`` (0 = K, 1 = V) and
     ``kv_meta`` fp16 ``[num_pages, Hkv, 4, page_size]`` (k_scale, k_min, v_scale, v_min).
-    Pages are zero-filled on creation.
+    Pages are zero-filled on creation.  The append, attention and gather wrappers below
+    pick the 4- or 8-bit entry point from ``bits``.
     """
 
     def __init__(self, num_pages: int, num_kv_heads: int, head_dim: int, page_size: int = PAGE_SIZE,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", bits: int = 4):
         if head_dim % 2:
             raise ValueError("head_dim must be even")
+        if bits not in (4, 8):
+            raise ValueError(f"bits must be 4 or 8, got {bits}")
         self.num_pages = int(num_pages)
         self.num_kv_heads = int(num_kv_heads)
         self.head_dim = int(head_dim)
         self.page_size = int(page_size)
+        self.bits = int(bits)
         self.device = torch.device(device)
-        self.kv_codes = torch.zeros((num_pages, num_kv_heads, 2, page_size, head_dim // 2), dtype=torch.uint8,
-                                    device=self.device)
+        self.kv_codes = torch.zeros((num_pages, num_kv_heads, 2, page_size, head_dim * bits // 8),
+                                    dtype=torch.uint8, device=self.device)
         self.kv_meta = torch.zeros((num_pages, num_kv_heads, 4, page_size), dtype=torch.float16, device=self.device)
 
     @property
@@ -65,11 +69,20 @@ def _check_table(block_table: torch.Tensor, seq_lens: torch.Tensor, batch: int) 
         raise ValueError("block_table / seq_lens have fewer rows than the batch")
 
 
-def append_quant_int4(key: torch.Tensor, value: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
-                      seq_lens: torch.Tensor, *, advance: bool = True,
-                      device_status: torch.Tensor | None = None) -> None:
-    """Quantise ``key``/``value`` ``[B, Hkv, n, D]`` into ``pool`` at positions ``seq_lens[b] + t``."""
+def _bits_entry(base: str, pool: PagedKvPool, bits: int | None) -> str:
+    """The entry point ``oq_<base>_int<bits>`` for ``pool``; ``bits`` (when given) must match it."""
+    if bits is not None and bits != pool.bits:
+        raise ValueError(f"this is the {bits}-bit entry point but the pool holds {pool.bits}-bit codes")
+    return f"oq_{base}_int{pool.bits}"
+
+
+def append_quant(key: torch.Tensor, value: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
+                 seq_lens: torch.Tensor, *, advance: bool = True, device_status: torch.Tensor | None = None,
+                 _bits: int | None = None) -> None:
+    """Quantise ``key``/``value`` ``[B, Hkv, n, D]`` into ``pool`` at positions ``seq_lens[b] + t``
+    (4- or 8-bit codes, as the pool holds)."""
     require_cuda(key, value, block_table, seq_lens)
+    entry = _bits_entry("append_quant", pool, _bits)
     if key.shape != value.shape or key.dim() != 4:
         raise ValueError("key and value must both be [batch, num_kv_heads, num_new, head_dim]")
     if key.dtype != value.dtype:
@@ -81,11 +94,21 @@ def append_quant_int4(key: torch.Tensor, value: torch.Tensor, pool: PagedKvPool,
     if key.stride(3) != 1 or value.stride(3) != 1:
         key, value = key.contiguous(), value.contiguous()
     _check_table(block_table, seq_lens, b)
-    call("oq_append_quant_int4", ptr(key), ptr(value), dtype_code(key.dtype), b, h, n, d,
+    call(entry, ptr(key), ptr(value), dtype_code(key.dtype), b, h, n, d,
          key.stride(0), key.stride(1), key.stride(2), value.stride(0), value.stride(1), value.stride(2),
          ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
          ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens), int(advance),
          ptr(device_status), stream_ptr(key.device))
+
+
+def append_quant_int4(key, value, pool, block_table, seq_lens, **kw) -> None:
+    """:func:`append_quant` into a 4-bit pool (``oq_append_quant_int4``)."""
+    append_quant(key, value, pool, block_table, seq_lens, _bits=4, **kw)
+
+
+def append_quant_int8(key, value, pool, block_table, seq_lens, **kw) -> None:
+    """:func:`append_quant` into an 8-bit pool (``oq_append_quant_int8``)."""
+    append_quant(key, value, pool, block_table, seq_lens, _bits=8, **kw)
 
 
 def advance_seq_lens(seq_lens: torch.Tensor, delta: int = 1) -> None:
@@ -114,20 +137,22 @@ def new_decode_workspace(batch: int, num_heads: int, num_kv_heads: int, max_page
     return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
 
 
-def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
-                          seq_lens: torch.Tensor, scaling: float, *, out: torch.Tensor | None = None,
-                          out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
-                          workspace: torch.Tensor | None = None, num_splits: int = 0,
-                          device_status: torch.Tensor | None = None, want_out: bool = True,
-                          gate: torch.Tensor | None = None):
-    """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache.
+def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.Tensor,
+                     seq_lens: torch.Tensor, scaling: float, *, out: torch.Tensor | None = None,
+                     out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None, num_splits: int = 0,
+                     device_status: torch.Tensor | None = None, want_out: bool = True,
+                     gate: torch.Tensor | None = None, _bits: int | None = None):
+    """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache (4- or 8-bit codes,
+    as the pool holds: ``oq_decode_attn_int{4,8}_paged``).
 
     Returns ``out`` (query dtype, ``[B, Hq, D]``) unless ``want_out`` is False.  With
     ``gate`` ``[B, Hq, D]`` (query dtype, unit stride along D) the output is gated in the
-    kernel: ``out = attn * sigmoid(gate)`` (``oq_decode_attn_int4_paged_gated``); fp32 /
+    kernel: ``out = attn * sigmoid(gate)`` (``oq_decode_attn_int{4,8}_paged_gated``); fp32 /
     lse outputs are not available then.
     """
     require_cuda(query, block_table, seq_lens)
+    entry = _bits_entry("decode_attn", pool, _bits) + "_paged"
     if query.dim() != 3:
         raise ValueError("query must be [batch, num_heads, head_dim]")
     if query.dtype not in (torch.bfloat16, torch.float16):
@@ -151,14 +176,14 @@ def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: t
             raise ValueError("gate must be [B, Hq, D] in the query dtype with unit stride along D")
         if out is None or out_f32 is not None or out_lse is not None:
             raise ValueError("a gated call writes the query-dtype output only")
-        call("oq_decode_attn_int4_paged_gated", ptr(query), dtype_code(query.dtype), query.stride(0),
+        call(entry + "_gated", ptr(query), dtype_code(query.dtype), query.stride(0),
              query.stride(1), ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
              ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
              b, hq, pool.num_kv_heads, d, float(scaling), ptr(gate), gate.stride(0), gate.stride(1),
              ptr(out), out.stride(0), out.stride(1), ptr(workspace), workspace.numel(), int(num_splits),
              ptr(device_status), stream_ptr(query.device))
         return out
-    call("oq_decode_attn_int4_paged", ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
+    call(entry, ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
          ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
          ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
          b, hq, pool.num_kv_heads, d, float(scaling),
@@ -166,6 +191,16 @@ def decode_attention_int4(query: torch.Tensor, pool: PagedKvPool, block_table: t
          ptr(out_f32), ptr(out_lse), ptr(workspace), workspace.numel(), int(num_splits),
          ptr(device_status), stream_ptr(query.device))
     return out
+
+
+def decode_attention_int4(query, pool, block_table, seq_lens, scaling, **kw):
+    """:func:`decode_attention` over a 4-bit pool."""
+    return decode_attention(query, pool, block_table, seq_lens, scaling, _bits=4, **kw)
+
+
+def decode_attention_int8(query, pool, block_table, seq_lens, scaling, **kw):
+    """:func:`decode_attention` over an 8-bit pool."""
+    return decode_attention(query, pool, block_table, seq_lens, scaling, _bits=8, **kw)
 
 
 def lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, dtype: torch.dtype = torch.bfloat16,
@@ -185,20 +220,31 @@ def lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, dtype: torch.dtype
     return out
 
 
-def gather_dequant_int4(pool: PagedKvPool, block_table: torch.Tensor, seq_lens: torch.Tensor, max_len: int,
-                        dtype: torch.dtype, *, device_status: torch.Tensor | None = None):
+def gather_dequant(pool: PagedKvPool, block_table: torch.Tensor, seq_lens: torch.Tensor, max_len: int,
+                   dtype: torch.dtype, *, device_status: torch.Tensor | None = None, _bits: int | None = None):
     """Dequantised ``(keys, values)`` ``[B, Hkv, max_len, D]`` (rows past a sequence's length are 0)."""
     require_cuda(block_table, seq_lens)
+    entry = _bits_entry("gather_dequant", pool, _bits)
     b = block_table.shape[0]
     _check_table(block_table, seq_lens, b)
     shape = (b, pool.num_kv_heads, int(max_len), pool.head_dim)
     keys = torch.zeros(shape, dtype=dtype, device=pool.device)
     values = torch.zeros(shape, dtype=dtype, device=pool.device)
-    call("oq_gather_dequant_int4", ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+    call(entry, ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
          ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens), b, pool.num_kv_heads,
          pool.head_dim, int(max_len), ptr(keys), ptr(values), dtype_code(dtype), ptr(device_status),
          stream_ptr(pool.device))
     return keys, values
+
+
+def gather_dequant_int4(pool, block_table, seq_lens, max_len, dtype, **kw):
+    """:func:`gather_dequant` of a 4-bit pool."""
+    return gather_dequant(pool, block_table, seq_lens, max_len, dtype, _bits=4, **kw)
+
+
+def gather_dequant_int8(pool, block_table, seq_lens, max_len, dtype, **kw):
+    """:func:`gather_dequant` of an 8-bit pool."""
+    return gather_dequant(pool, block_table, seq_lens, max_len, dtype, _bits=8, **kw)
 
 
 def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,

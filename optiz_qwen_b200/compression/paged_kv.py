@@ -105,8 +105,8 @@ class PagedKvState:
         """Quantise ``[batch, Hkv, n, D]`` tokens onto the end of every row."""
         n = int(key.shape[-2])
         self.reserve([length + n for length in self.host_lens])
-        cabi.append_quant_int4(key, value, self.pool, self.block_table, self.seq_lens, advance=True,
-                               device_status=device_status)
+        cabi.append_quant(key, value, self.pool, self.block_table, self.seq_lens, advance=True,
+                          device_status=device_status)
         self.host_lens = [length + n for length in self.host_lens]
 
     def set_lengths(self, lengths) -> None:

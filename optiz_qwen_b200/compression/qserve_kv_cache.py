@@ -1,4 +1,4 @@
-"""Drop-in QServe packed-KV cache for Qwen3.5, stored as paged INT4 on the GPU.
+"""Drop-in QServe packed-KV cache for Qwen3.5, stored as paged INT4 (or INT8) on the GPU.
 
 Same public surface as optiz_qwen/compression/qserve_kv_cache.py (config,
 layer and cache classes, builder, report, counters), with a different storage
@@ -104,7 +104,8 @@ class QServeKvCacheReport:
 
 
 class QServeAttentionLayer(CacheLayerMixin):
-    """Full-attention layer cache backed by a paged INT4 pool (qserve_kv_cache.py:71-377)."""
+    """Full-attention layer cache backed by a paged INT4 (or INT8, ``k_bits = 8``) pool
+    (qserve_kv_cache.py:71-377)."""
 
     is_compileable = False
     supports_early_init = True
@@ -113,8 +114,6 @@ class QServeAttentionLayer(CacheLayerMixin):
     def __init__(self, config: QServeKvConfig) -> None:
         super().__init__()
         config.validate()
-        if config.k_bits != 4:
-            raise ValueError("8-bit paged KV is not implemented on this build; use k_bits=v_bits=4.")
         self.config = config
         self.keys = None
         self.values = None
@@ -150,8 +149,8 @@ class QServeAttentionLayer(CacheLayerMixin):
     def materialize(self) -> tuple[torch.Tensor, torch.Tensor]:
         if not self.is_initialized or self._seq_length == 0 or self.paged is None:
             raise ValueError("qserve_kv cache layer is empty and cannot be materialized.")
-        keys, values = cabi.gather_dequant_int4(self.paged.pool, self.paged.block_table, self.paged.seq_lens,
-                                                self._seq_length, self.dtype)
+        keys, values = cabi.gather_dequant(self.paged.pool, self.paged.block_table, self.paged.seq_lens,
+                                           self._seq_length, self.dtype)
         self.keys, self.values = keys, values
         return keys, values
 
@@ -201,7 +200,7 @@ class QServeAttentionLayer(CacheLayerMixin):
     def _rebuild_from_full(self, keys: torch.Tensor, values: torch.Tensor) -> None:
         if keys.shape[-1] != self.config.group_size:
             raise ValueError(
-                f"qserve_kv paged INT4 cache keeps one group per token: group_size ({self.config.group_size}) "
+                f"qserve_kv paged cache keeps one group per token: group_size ({self.config.group_size}) "
                 f"must equal head_dim ({keys.shape[-1]}).")
         self.dtype = keys.dtype
         self.device = keys.device
@@ -211,7 +210,7 @@ class QServeAttentionLayer(CacheLayerMixin):
             self.paged.release()
         if self.paged is None or self.paged.batch != batch or self.paged.pool.num_kv_heads != heads:
             pages = max(4, 2 * batch * cabi.pages_for(seq + 1, self.config.page_size))
-            pool = cabi.PagedKvPool(pages, heads, dim, self.config.page_size, keys.device)
+            pool = cabi.PagedKvPool(pages, heads, dim, self.config.page_size, keys.device, bits=self.config.k_bits)
             self.paged = PagedKvState(pool, batch, max_pages=cabi.pages_for(seq + 1, self.config.page_size),
                                       allocator=PageAllocator(pages, self.config.page_seed))
         self._seq_length = 0

@@ -1,4 +1,4 @@
-// Fused append-quantize into the paged INT4 KV cache.
+// Fused append-quantize into the paged INT4 (or INT8) KV cache.
 //
 // Replaces the reference's per-token torch.cat into a dense residual window and
 // its periodic groupwise quantise + torch.cat of the whole code tensor
@@ -6,7 +6,8 @@
 // Here every appended token is quantised at once into its page slot: one warp
 // per (token, KV head, K-or-V) row of head_dim values, min/max by warp shuffles,
 // codes from the fp32 scale/min with IEEE division and round-half-even exactly
-// as the reference computes them, then one 4-byte store per lane.
+// as the reference computes them, then one 4-byte store per lane.  The 8-bit variant
+// (the reference's bits=8 path: 255 levels, one code per byte) shares the kernel.
 #include <algorithm>
 
 #include "common.cuh"
@@ -50,8 +51,8 @@ __device__ __forceinline__ void load_row(const T* row, int lane, float (&x)[EPL]
   }
 }
 
-// One (token, head, K|V) row per warp; head_dim = 32 * EPL.
-template <typename T, int EPL, bool VEC>
+// One (token, head, K|V) row per warp; head_dim = 32 * EPL; codes of kBits bits.
+template <typename T, int EPL, bool VEC, int kBits>
 __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams p) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -61,7 +62,9 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
   const int32_t start = p.seq_lens[b];
   const int64_t jobs = p.num_kv_heads * p.num_new * 2;
   constexpr int kHeadDim = EPL * 32;
-  constexpr int kRowBytes = kHeadDim / 2;
+  constexpr int kRowBytes = kHeadDim * kBits / 8;
+  constexpr float kLevels = float((1 << kBits) - 1);
+  constexpr int kLaneBytes = EPL * kBits / 8;
 
   for (int64_t job = int64_t(blockIdx.x) * kWarps + warp; job < jobs; job += int64_t(gridDim.x) * kWarps) {
     const int kv = int(job & 1);
@@ -97,33 +100,29 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
       mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    // scale = (max - min) / 15 in fp32; 1 where it is not positive (qserve_kv_cache.py:326-328)
-    float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    // scale = (max - min) / levels in fp32; 1 where it is not positive (qserve_kv_cache.py:326-328)
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), kLevels);
     if (!(scale > 0.0f)) scale = 1.0f;
 
-    uint32_t packed[EPL / 8 > 0 ? EPL / 8 : 1] = {};
-    uint32_t small = 0;  // EPL < 8: fewer than 4 bytes per lane
+    constexpr int kWords = kLaneBytes / 4 > 0 ? kLaneBytes / 4 : 1;
+    constexpr int kPerWord = 32 / kBits;
+    uint32_t packed[kWords] = {};
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
       float c = rintf(__fdiv_rn(__fsub_rn(x[i], mn), scale));
-      c = fminf(fmaxf(c, 0.0f), 15.0f);
-      const uint32_t code = static_cast<uint32_t>(c);
-      if constexpr (EPL >= 8) {
-        packed[i / 8] |= code << (4 * (i % 8));
-      } else {
-        small |= code << (4 * i);
-      }
+      c = fminf(fmaxf(c, 0.0f), kLevels);
+      packed[i / kPerWord] |= static_cast<uint32_t>(c) << (kBits * (i % kPerWord));
     }
 
     const int64_t block = (page * p.num_kv_heads + h) * 2 + kv;
-    uint8_t* row = p.kv_codes + (block * p.page_size + slot) * kRowBytes + lane * (EPL / 2);
-    if constexpr (EPL >= 8) {
+    uint8_t* row = p.kv_codes + (block * p.page_size + slot) * kRowBytes + lane * kLaneBytes;
+    if constexpr (kLaneBytes >= 4) {
 #pragma unroll
-      for (int w = 0; w < EPL / 8; ++w) reinterpret_cast<uint32_t*>(row)[w] = packed[w];
-    } else if constexpr (EPL == 4) {
-      *reinterpret_cast<uint16_t*>(row) = static_cast<uint16_t>(small);
+      for (int w = 0; w < kLaneBytes / 4; ++w) reinterpret_cast<uint32_t*>(row)[w] = packed[w];
+    } else if constexpr (kLaneBytes == 2) {
+      *reinterpret_cast<uint16_t*>(row) = static_cast<uint16_t>(packed[0]);
     } else {
-      *row = static_cast<uint8_t>(small);
+      *row = static_cast<uint8_t>(packed[0]);
     }
     if (lane == 0) {
       uint16_t* meta = p.kv_meta + ((page * p.num_kv_heads + h) * 4 + kv * 2) * p.page_size + slot;
@@ -144,22 +143,22 @@ __global__ void advance_kernel(int32_t* seq_lens, int64_t batch, int32_t delta) 
   if (i < batch) seq_lens[i] += delta;
 }
 
-template <typename T, int EPL>
+template <typename T, int EPL, int kBits>
 void launch_append(const AppendParams& p, bool vec, dim3 grid, cudaStream_t s) {
   if (vec) {
-    launch_plain(append_quant_kernel<T, EPL, true>, grid, dim3(kWarps * 32), 0, s, p);
+    launch_plain(append_quant_kernel<T, EPL, true, kBits>, grid, dim3(kWarps * 32), 0, s, p);
   } else {
-    launch_plain(append_quant_kernel<T, EPL, false>, grid, dim3(kWarps * 32), 0, s, p);
+    launch_plain(append_quant_kernel<T, EPL, false, kBits>, grid, dim3(kWarps * 32), 0, s, p);
   }
 }
 
-template <typename T>
+template <typename T, int kBits>
 void launch_dim(const AppendParams& p, int64_t head_dim, bool vec, dim3 grid, cudaStream_t s) {
   switch (head_dim) {
-    case 64: launch_append<T, 2>(p, vec, grid, s); break;
-    case 128: launch_append<T, 4>(p, vec, grid, s); break;
-    case 256: launch_append<T, 8>(p, vec, grid, s); break;
-    default: launch_append<T, 16>(p, vec, grid, s); break;  // 512
+    case 64: launch_append<T, 2, kBits>(p, vec, grid, s); break;
+    case 128: launch_append<T, 4, kBits>(p, vec, grid, s); break;
+    case 256: launch_append<T, 8, kBits>(p, vec, grid, s); break;
+    default: launch_append<T, 16, kBits>(p, vec, grid, s); break;  // 512
   }
 }
 
@@ -176,8 +175,11 @@ extern "C" int oq_advance_seq_lens(int32_t* seq_lens, int64_t batch, int32_t del
   return check_launch("advance_seq_lens");
 }
 
-extern "C" int oq_append_quant_int4(
-    const void* key, const void* value, int dtype,
+namespace oq {
+namespace {
+
+int append_quant_impl(
+    int bits, const void* key, const void* value, int dtype,
     int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
     int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
     int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
@@ -185,26 +187,25 @@ extern "C" int oq_append_quant_int4(
     const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
     int32_t* seq_lens, int advance_seq_lens,
     int32_t* device_status, void* stream) {
-  using namespace oq;
-  if (!valid_dtype(dtype)) return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: unknown dtype %d", dtype);
+  if (!valid_dtype(dtype)) return fail(OQ_ERR_UNSUPPORTED, "append_quant: unknown dtype %d", dtype);
   if (batch < 0 || num_kv_heads <= 0 || num_new < 0 || num_pages <= 0 || page_size <= 0 ||
       max_pages_per_seq <= 0 || block_table_stride < max_pages_per_seq) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: bad sizes");
+    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant: bad sizes");
   }
   if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512) {
-    return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: head_dim %lld not in {64,128,256,512}",
+    return fail(OQ_ERR_UNSUPPORTED, "append_quant: head_dim %lld not in {64,128,256,512}",
                 (long long)head_dim);
   }
   if (batch == 0 || num_new == 0) return ok();
   if (!key || !value || !kv_codes || !kv_meta || !block_table || !seq_lens) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: null pointer");
+    return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant: null pointer");
   }
   const int64_t esize = dtype == OQ_F32 ? 4 : 2;
   const int64_t strides[6] = {key_stride_b, key_stride_h, key_stride_t, value_stride_b, value_stride_h, value_stride_t};
   bool vec = (reinterpret_cast<uintptr_t>(key) % 16 == 0) && (reinterpret_cast<uintptr_t>(value) % 16 == 0) &&
              ((head_dim / 32) * esize % 16 == 0);
   for (int64_t s : strides) {
-    if (s < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant_int4: negative stride");
+    if (s < 0) return fail(OQ_ERR_INVALID_ARGUMENT, "append_quant: negative stride");
     vec = vec && ((s * esize) % 16 == 0);
   }
 
@@ -234,18 +235,59 @@ extern "C" int oq_append_quant_int4(
   const int64_t blocks_x = std::min<int64_t>((jobs + kWarps - 1) / kWarps, 1024);
   const bool fused_advance = blocks_x == 1;
   p.advance = (advance_seq_lens && fused_advance) ? 1 : 0;
-  if (batch > 65535) return fail(OQ_ERR_UNSUPPORTED, "append_quant_int4: batch > 65535");
+  if (batch > 65535) return fail(OQ_ERR_UNSUPPORTED, "append_quant: batch > 65535");
   dim3 grid((unsigned)blocks_x, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (dtype) {
-    case OQ_F32: launch_dim<float>(p, head_dim, vec, grid, s); break;
-    case OQ_F16: launch_dim<__half>(p, head_dim, vec, grid, s); break;
-    default: launch_dim<__nv_bfloat16>(p, head_dim, vec, grid, s); break;
+  if (bits == 8) {
+    switch (dtype) {
+      case OQ_F32: launch_dim<float, 8>(p, head_dim, vec, grid, s); break;
+      case OQ_F16: launch_dim<__half, 8>(p, head_dim, vec, grid, s); break;
+      default: launch_dim<__nv_bfloat16, 8>(p, head_dim, vec, grid, s); break;
+    }
+  } else {
+    switch (dtype) {
+      case OQ_F32: launch_dim<float, 4>(p, head_dim, vec, grid, s); break;
+      case OQ_F16: launch_dim<__half, 4>(p, head_dim, vec, grid, s); break;
+      default: launch_dim<__nv_bfloat16, 4>(p, head_dim, vec, grid, s); break;
+    }
   }
-  int st = check_launch("append_quant_int4");
+  int st = check_launch(bits == 8 ? "append_quant_int8" : "append_quant_int4");
   if (st != OQ_OK) return st;
   if (advance_seq_lens && !fused_advance) {
     return oq_advance_seq_lens(seq_lens, batch, int32_t(num_new), stream);
   }
   return ok();
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" int oq_append_quant_int4(
+    const void* key, const void* value, int dtype,
+    int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
+    int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
+    int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    int32_t* seq_lens, int advance_seq_lens,
+    int32_t* device_status, void* stream) {
+  return oq::append_quant_impl(4, key, value, dtype, batch, num_kv_heads, num_new, head_dim, key_stride_b,
+                               key_stride_h, key_stride_t, value_stride_b, value_stride_h, value_stride_t, kv_codes,
+                               kv_meta, num_pages, page_size, block_table, block_table_stride, max_pages_per_seq,
+                               seq_lens, advance_seq_lens, device_status, stream);
+}
+
+extern "C" int oq_append_quant_int8(
+    const void* key, const void* value, int dtype,
+    int64_t batch, int64_t num_kv_heads, int64_t num_new, int64_t head_dim,
+    int64_t key_stride_b, int64_t key_stride_h, int64_t key_stride_t,
+    int64_t value_stride_b, int64_t value_stride_h, int64_t value_stride_t,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    int32_t* seq_lens, int advance_seq_lens,
+    int32_t* device_status, void* stream) {
+  return oq::append_quant_impl(8, key, value, dtype, batch, num_kv_heads, num_new, head_dim, key_stride_b,
+                               key_stride_h, key_stride_t, value_stride_b, value_stride_h, value_stride_t, kv_codes,
+                               kv_meta, num_pages, page_size, block_table, block_table_stride, max_pages_per_seq,
+                               seq_lens, advance_seq_lens, device_status, stream);
 }

@@ -54,8 +54,14 @@ struct __align__(16) SmemTail {
   int is_last;
 };
 
-constexpr size_t kSmemBytes =
-    1024 /*alignment slack*/ + kStages * (kStageCodeBytes + kStageMetaBytes) + sizeof(SmemTail);
+// Page formats: INT4 (two codes per byte, 16 KB of codes per page and KV head, 4 stages)
+// and INT8 (one code per byte, 32 KB, 3 stages so that two CTAs still share an SM).
+template <int kBits>
+struct PageFormat {
+  static constexpr int kCodeBytes = 2 * kPage * kHeadDim * kBits / 8;
+  static constexpr int kStagesN = kBits == 8 ? 3 : kStages;
+  static constexpr size_t kSmem = 1024 /*alignment slack*/ + kStagesN * (kCodeBytes + kStageMetaBytes) + sizeof(SmemTail);
+};
 
 // ---- q.k on integer tensor cores.
 // Each query head is turned into 15-bit fixed point, q ~ q_int * 2^-e_h with
@@ -98,20 +104,29 @@ __device__ __forceinline__ int red_index(int w, int h, int d) { return (w * kMax
 __device__ __forceinline__ const uint4* swz(const uint8_t* base, int row, int chunk) {
   return reinterpret_cast<const uint4*>(base + row * kRowBytes + ((chunk ^ (row & 7)) << 4));
 }
+// INT8 stage: each 256-byte row is two 128-byte lines (line = 2 row + chunk / 8), swizzled per line.
+__device__ __forceinline__ const uint4* swz8(const uint8_t* base, int row, int chunk) {
+  const int line = 2 * row + (chunk >> 3);
+  return reinterpret_cast<const uint4*>(base + line * 128 + (((chunk & 7) ^ (line & 7)) << 4));
+}
+// fp16 pair (1024 + byte p of a, 1024 + byte p of b) for the INT8 p.v operand
+constexpr uint32_t kFp16Hi = 0x64646464u;
 
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
          ((uint32_t(d) & 0xFFu) << 24);
 }
 
-template <typename T, bool kDual>
+template <typename T, bool kDual, int kBits>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                AttnParams p) {
+  constexpr int kSt = PageFormat<kBits>::kStagesN;
+  constexpr int kCB = PageFormat<kBits>::kCodeBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* codes = smem;                                       // kStages x 16 KB, 1024-aligned
-  uint8_t* metas = smem + kStages * kStageCodeBytes;           // kStages x 512 B
-  SmemTail* tail = reinterpret_cast<SmemTail*>(metas + kStages * kStageMetaBytes);
+  uint8_t* codes = smem;                                       // kSt x kCB bytes, 1024-aligned
+  uint8_t* metas = smem + kSt * kCB;                           // kSt x 512 B
+  SmemTail* tail = reinterpret_cast<SmemTail*>(metas + kSt * kStageMetaBytes);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -137,17 +152,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int n = max(0, min(npages_b, page_begin + p.pages_per_split) - page_begin);
 
   // ---- every independent global load of the prologue is issued first, so their
-  // latencies overlap: the first kStages page ids (one lane each), this thread's
+  // latencies overlap: the first kSt page ids (one lane each), this thread's
   // share of the remaining page ids, and the query elements this thread needs.
   constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
   constexpr int kPidRegs = kPageIdSlots / kThreads;
   const int32_t* bt_row = p.block_table + b * p.bt_stride;
   const int n_smem = min(n, kPageIdSlots);
-  const int first_page = (warp == 0 && lane < min(n, kStages)) ? bt_row[page_begin + lane] : -1;
+  const int first_page = (warp == 0 && lane < min(n, kSt)) ? bt_row[page_begin + lane] : -1;
   int pid_reg[kPidRegs];
 #pragma unroll
   for (int j = 0; j < kPidRegs; ++j) {
-    const int idx = kStages + tid + j * kThreads;
+    const int idx = kSt + tid + j * kThreads;
     pid_reg[j] = idx < n_smem ? bt_row[page_begin + idx] : 0;
   }
   // warp 0: a quarter of one head per lane (head lane/4, dims 64*(lane%4) ..) for the exponents
@@ -173,7 +188,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&tail->full[s], 1);
+    for (int s = 0; s < kSt; ++s) mbar_init(&tail->full[s], 1);
     fence_mbar_init();
   }
   // warp 0: per-head fixed-point exponent and sum(q)
@@ -206,7 +221,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();  // barriers initialised, exponents known
 
-  // page id of range page i: the first kStages were fetched by warp 0's lanes,
+  // page id of range page i: the first kSt were fetched by warp 0's lanes,
   // later ones come from the shared-memory copy made after the prologue
   auto issue = [&](int i, int s, int64_t page) {
     if (page < 0 || page >= p.num_pages) {
@@ -217,25 +232,31 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
     tail->stage_ok[s] = 1;
     const int64_t blk = page * p.num_kv_heads + kvh;
-    mbar_arrive_expect_tx(&tail->full[s], kStageCodeBytes + kStageMetaBytes);
-    tma_load_2d(codes + s * kStageCodeBytes, &tmap, 0, int32_t(blk * 2 * kPage), &tail->full[s]);
+    mbar_arrive_expect_tx(&tail->full[s], kCB + kStageMetaBytes);
+    if constexpr (kBits == 8) {  // box {128 B, 2 halves, 128 rows}
+      tma_load_3d(codes + s * kCB, &tmap, 0, 0, int32_t(blk * 2 * kPage), &tail->full[s]);
+    } else {
+      tma_load_2d(codes + s * kCB, &tmap, 0, int32_t(blk * 2 * kPage), &tail->full[s]);
+    }
     bulk_load(metas + s * kStageMetaBytes, p.kv_meta + blk * 4 * kPage, kStageMetaBytes, &tail->full[s]);
   };
   int issued = 0;
   if (warp == 0) {
 #pragma unroll
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kSt; ++i) {
       const int page = __shfl_sync(0xffffffffu, first_page, i);
       if (lane == 0 && i < n) issue(i, i, page);
     }
-    issued = min(n, kStages);
+    issued = min(n, kSt);
   }
 
   // ---- query digits (B operand of q.k).  This lane feeds MMA column r: head
   // (packed) r & 3, digit hi for r < 4 and lo for r >= 4; (dual) head r, both
   // digits.  Lane c supplies dims 64c .. 64c+63; k-step s covers dims
   // 64c + 16s + {0..15}: the even dims in the "low nibble" MMA, the odd dims in
-  // the "high nibble" MMA.  Warp w builds k-step w for all 32 lanes.
+  // the "high nibble" MMA.  Warp w builds k-step w for all 32 lanes.  INT8: the
+  // same 16 dims feed two MMAs, 2w (dims 64c + 16w + 0..7) and 2w + 1 (+ 8..15),
+  // each taking 4 dims per word: words (b0, b1) of MMA 2w, then of MMA 2w + 1.
   {
     const float up = f_has ? ldexpf(1.0f, tail->q_exp[f_head]) : 0.0f;
     uint32_t frag[8];
@@ -252,10 +273,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         hi_o[j] = q_o >> 7;
         lo_o[j] = q_o - 128 * hi_o[j];
       }
-      const uint32_t he = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
-      const uint32_t le = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
-      const uint32_t ho = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
-      const uint32_t lo = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+      uint32_t he, le, ho, lo;
+      if constexpr (kBits == 8) {  // he / le: dims +0..3 (b0), ho / lo: dims +4..7 (b1) of MMA 2w + half
+        he = pack_s8x4(hi_e[0], hi_o[0], hi_e[1], hi_o[1]);
+        le = pack_s8x4(lo_e[0], lo_o[0], lo_e[1], lo_o[1]);
+        ho = pack_s8x4(hi_e[2], hi_o[2], hi_e[3], hi_o[3]);
+        lo = pack_s8x4(lo_e[2], lo_o[2], lo_e[3], lo_o[3]);
+      } else {
+        he = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
+        le = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
+        ho = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
+        lo = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+      }
       if (kDual) {
         frag[half] = he;          // set 0 (hi digits): low-nibble MMA
         frag[2 + half] = ho;      //                     high-nibble MMA
@@ -289,7 +318,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   __syncthreads();  // every warp holds its fragments: the union now takes the page ids
 #pragma unroll
   for (int j = 0; j < kPidRegs; ++j) {
-    const int idx = kStages + tid + j * kThreads;
+    const int idx = kSt + tid + j * kThreads;
     if (idx < n_smem) tail->u.page_ids[idx] = pid_reg[j];
   }
   __syncthreads();
@@ -312,23 +341,65 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   bool aborted = false;
 
   for (int i = 0; i < n; ++i) {
-    const int s = i % kStages;
-    const uint32_t parity = (i / kStages) & 1;
+    const int s = i % kSt;
+    const uint32_t parity = (i / kSt) & 1;
     bool ready = wait_stage(&tail->full[s], parity);
     ready = __all_sync(0xffffffffu, ready);
     const int page_tokens = min(kPage, len - (page_begin + i) * kPage);
     if (ready && tail->stage_ok[s] && warp * 16 < page_tokens) {
-      const uint8_t* st = codes + s * kStageCodeBytes;
+      const uint8_t* st = codes + s * kCB;
       const __half* meta = reinterpret_cast<const __half*>(metas + s * kStageMetaBytes);
       const int tb = warp * 16 + kPage;  // V rows follow the 64 K rows
-      const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
-      const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
-      const uint4 va = *swz(st, tb + 2 * c, r), vb = *swz(st, tb + 2 * c + 1, r);
-      const uint4 vc = *swz(st, tb + 2 * c + 8, r), vd = *swz(st, tb + 2 * c + 9, r);
 
       // ---------------- integer q.k: A = K codes (16 tokens x 32 dims, u8), B = q digits (s8)
       int dot_a0, dot_b0, dot_a1, dot_b1;  // (token r, head 2c), (r, 2c+1), (r+8, 2c), (r+8, 2c+1)
-      {
+      uint4 va, vb, vc, vd;
+      if constexpr (kBits == 8) {
+        // lane c holds dims 64c .. 64c + 63 of both token rows (16 words each); MMA "lo" of
+        // step s takes words 4s (b0 dims) and 4s + 2, MMA "hi" words 4s + 1 and 4s + 3,
+        // both into one accumulator (codes are whole bytes)
+        uint32_t w0[16], w1[16];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint4 x0 = *swz8(st, tok0, 4 * c + q4), x1 = *swz8(st, tok1, 4 * c + q4);
+          w0[4 * q4] = x0.x; w0[4 * q4 + 1] = x0.y; w0[4 * q4 + 2] = x0.z; w0[4 * q4 + 3] = x0.w;
+          w1[4 * q4] = x1.x; w1[4 * q4 + 1] = x1.y; w1[4 * q4 + 2] = x1.z; w1[4 * q4 + 3] = x1.w;
+        }
+        int tot[kSets][4];
+#pragma unroll
+        for (int k = 0; k < kSets; ++k) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tot[k][j] = 0;
+        }
+#pragma unroll
+        for (int st4 = 0; st4 < 4; ++st4) {
+          const uint32_t al[4] = {w0[4 * st4], w1[4 * st4], w0[4 * st4 + 2], w1[4 * st4 + 2]};
+          const uint32_t ah[4] = {w0[4 * st4 + 1], w1[4 * st4 + 1], w0[4 * st4 + 3], w1[4 * st4 + 3]};
+#pragma unroll
+          for (int k = 0; k < kSets; ++k) {
+            imma_u8s8_16832(tot[k], al, bq_lo[k][st4][0], bq_lo[k][st4][1]);
+            imma_u8s8_16832(tot[k], ah, bq_hi[k][st4][0], bq_hi[k][st4][1]);
+          }
+        }
+        int dot[4];
+        if (kDual) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + tot[kSets - 1][j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
+        }
+        dot_a0 = dot[0];
+        dot_b0 = dot[1];
+        dot_a1 = dot[2];
+        dot_b1 = dot[3];
+      } else {
+        const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
+        const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
+        va = *swz(st, tb + 2 * c, r);
+        vb = *swz(st, tb + 2 * c + 1, r);
+        vc = *swz(st, tb + 2 * c + 8, r);
+        vd = *swz(st, tb + 2 * c + 9, r);
         const uint32_t w0[8] = {k00.x, k00.y, k00.z, k00.w, k01.x, k01.y, k01.z, k01.w};
         const uint32_t w1[8] = {k10.x, k10.y, k10.z, k10.w, k11.x, k11.y, k11.z, k11.w};
         int lo[kSets][4], hi[kSets][4];
@@ -429,7 +500,30 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       const uint32_t pb1 = movmatrix_trans(blk1);
 
       // ---------------- values: A = V^T codes (16 dims x 16 tokens), B = P' (16 tokens x 8 heads)
-      {
+      if constexpr (kBits == 8) {
+        // half hf, lane r: 16-byte chunk 8 hf + r of the four token rows; MMA 8 hf + k has
+        // row r = dim 128 hf + 16 r + 2k, row r + 8 = that dim + 1, each code as fp16 1024 + c
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint4 xa = *swz8(st, tb + 2 * c, 8 * hf + r), xb = *swz8(st, tb + 2 * c + 1, 8 * hf + r);
+          const uint4 xc = *swz8(st, tb + 2 * c + 8, 8 * hf + r), xd = *swz8(st, tb + 2 * c + 9, 8 * hf + r);
+          const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w}, wb[4] = {xb.x, xb.y, xb.z, xb.w};
+          const uint32_t wc[4] = {xc.x, xc.y, xc.z, xc.w}, wd[4] = {xd.x, xd.y, xd.z, xd.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t pb = 2u * uint32_t(k & 1);  // bytes pb, pb + 1 of word k / 2
+            const uint32_t sel = pb | ((4u + pb) << 4) | ((pb + 1u) << 8) | ((5u + pb) << 12);
+            const uint32_t x = prmt(wa[k >> 1], wb[k >> 1], sel);  // tokens 2c, 2c+1: dims 2k, 2k+1 of the chunk
+            const uint32_t y = prmt(wc[k >> 1], wd[k >> 1], sel);  // tokens 2c+8, 2c+9
+            uint32_t a[4];
+            a[0] = prmt(x, kFp16Hi, 0x4140u);  // row r: dim 2k, 1024 + c
+            a[1] = prmt(x, kFp16Hi, 0x4342u);  // row r+8: dim 2k + 1
+            a[2] = prmt(y, kFp16Hi, 0x4140u);
+            a[3] = prmt(y, kFp16Hi, 0x4342u);
+            mma_f16_16816(acc[8 * hf + k], a, pb0, pb1);
+          }
+        }
+      } else {
         const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
         const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w}, wd[4] = {vd.x, vd.y, vd.z, vd.w};
 #pragma unroll
@@ -453,8 +547,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       aborted = true;
       break;
     }
-    if (tid == 0 && i + kStages < n) {
-      const int nxt = i + kStages;
+    if (tid == 0 && i + kSt < n) {
+      const int nxt = i + kSt;
       issue(nxt, s, nxt < kPageIdSlots ? tail->u.page_ids[nxt] : bt_row[page_begin + nxt]);
       ++issued;
     }
@@ -465,8 +559,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     // Leave no copy in flight before the CTA exits: wait (bounded) for every issued stage.
     if (tid == 0) {
       report(p.status, OQ_DEV_TIMEOUT);
-      for (int i = max(0, issued - kStages); i < issued; ++i) {
-        wait_stage(&tail->full[i % kStages], (i / kStages) & 1);
+      for (int i = max(0, issued - kSt); i < issued; ++i) {
+        wait_stage(&tail->full[i % kSt], (i / kSt) & 1);
       }
     }
     return;
@@ -512,16 +606,19 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     const float fa = ha < G ? tail->warp_f[warp][ha] : 0.0f;
     const float fb = hb < G ? tail->warp_f[warp][hb] : 0.0f;
     const float off_a = -kVBias * sp_a, off_b = -kVBias * sp_b;
+    // INT4: row r = even dim 32r + 2j (weight 1), row r + 8 = odd dim (codes x 16);
+    // INT8: MMA j = 8 hf + k, row r = dim 128 hf + 16r + 2k, row r + 8 = the next dim (weight 1)
+    constexpr float kOddUnscale = kBits == 8 ? kPUnscale : kPUnscale / 16.0f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const int d0 = 32 * r + 2 * j;  // row r: even dim d0 (weight 1); row r+8: odd dim d0+1 (weight 16)
+      const int d0 = kBits == 8 ? 128 * (j >> 3) + 16 * r + 2 * (j & 7) : 32 * r + 2 * j;
       if (ha < G) {
         red[red_index(warp, ha, d0)] = fmaf(acc[j][0] + off_a, kPUnscale, mp_a) * fa;
-        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2] + off_a, kPUnscale / 16.0f, mp_a) * fa;
+        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2] + off_a, kOddUnscale, mp_a) * fa;
       }
       if (hb < G) {
         red[red_index(warp, hb, d0)] = fmaf(acc[j][1] + off_b, kPUnscale, mp_b) * fb;
-        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3] + off_b, kPUnscale / 16.0f, mp_b) * fb;
+        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3] + off_b, kOddUnscale, mp_b) * fb;
       }
     }
   }
@@ -650,16 +747,30 @@ int64_t resident_slots(const void* kernel, int threads, size_t smem) {
 
 }  // namespace
 
-int encode_codes_map(CUtensorMap* map, const uint8_t* kv_codes, int64_t num_pages, int64_t num_kv_heads) {
+// INT4: rows of 128 B, one box = the 128 K + V rows of a (page, KV head).  INT8: rows of
+// 256 B seen as {128 B, 2 halves, rows} (the 128-byte swizzle caps a box line at 128 B).
+int encode_codes_map(CUtensorMap* map, const uint8_t* kv_codes, int64_t num_pages, int64_t num_kv_heads, int bits) {
   auto fn = tensor_map_encoder();
   if (fn == nullptr) return fail(OQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {cuuint64_t(kRowBytes), cuuint64_t(num_pages * num_kv_heads * 2 * kPage)};
-  const cuuint64_t strides[1] = {cuuint64_t(kRowBytes)};
-  const cuuint32_t box[2] = {cuuint32_t(kRowBytes), cuuint32_t(2 * kPage)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(kv_codes), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint64_t rows = cuuint64_t(num_pages * num_kv_heads * 2 * kPage);
+  CUresult res;
+  if (bits == 8) {
+    const cuuint64_t dims[3] = {128, 2, rows};
+    const cuuint64_t strides[2] = {128, 256};
+    const cuuint32_t box[3] = {128, 2, cuuint32_t(2 * kPage)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    res = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(kv_codes), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    const cuuint64_t dims[2] = {cuuint64_t(kRowBytes), rows};
+    const cuuint64_t strides[1] = {cuuint64_t(kRowBytes)};
+    const cuuint32_t box[2] = {cuuint32_t(kRowBytes), cuuint32_t(2 * kPage)};
+    const cuuint32_t estr[2] = {1, 1};
+    res = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(kv_codes), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (res != CUDA_SUCCESS) return fail(OQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(res));
   return OQ_OK;
 }
@@ -678,7 +789,7 @@ namespace oq {
 namespace {
 
 int decode_attn_impl(
-    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
     const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
     const int32_t* seq_lens,
@@ -689,44 +800,52 @@ int decode_attn_impl(
     void* workspace, size_t workspace_bytes, int num_splits,
     const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
     int32_t* device_status, void* stream) {
-  if (gate && !out) return fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged: a gate needs the model-dtype output");
+  const char* name = bits == 8 ? "decode_attn_int8_paged" : "decode_attn_int4_paged";
+  if (gate && !out) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: a gate needs the model-dtype output", name);
   if (dtype != OQ_BF16 && dtype != OQ_F16) {
-    return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: query dtype must be bf16 or fp16");
+    return fail(OQ_ERR_UNSUPPORTED, "%s: query dtype must be bf16 or fp16", name);
   }
-  if (head_dim != kHeadDim) return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: head_dim must be 256");
-  if (page_size != kPage) return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: page_size must be 64");
+  if (head_dim != kHeadDim) return fail(OQ_ERR_UNSUPPORTED, "%s: head_dim must be 256", name);
+  if (page_size != kPage) return fail(OQ_ERR_UNSUPPORTED, "%s: page_size must be 64", name);
   if (batch < 0 || num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads != 0 || num_pages <= 0 ||
       max_pages_per_seq <= 0 || block_table_stride < max_pages_per_seq) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged: bad sizes");
+    return fail(OQ_ERR_INVALID_ARGUMENT, "%s: bad sizes", name);
   }
   const int64_t group = num_heads / num_kv_heads;
-  if (group > kMaxGroup) return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: more than 8 query heads per KV head");
+  if (group > kMaxGroup) return fail(OQ_ERR_UNSUPPORTED, "%s: more than 8 query heads per KV head", name);
   if (batch == 0) return ok();
-  if (batch > 65535 || num_kv_heads > 65535) return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: grid too large");
+  if (batch > 65535 || num_kv_heads > 65535) return fail(OQ_ERR_UNSUPPORTED, "%s: grid too large", name);
   if (!query || !kv_codes || !kv_meta || !block_table || !seq_lens || (!out && !out_f32 && !out_lse)) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged: null pointer");
+    return fail(OQ_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   }
   if (reinterpret_cast<uintptr_t>(query) % 16 || (query_stride_b * 2) % 16 || (query_stride_h * 2) % 16 ||
       reinterpret_cast<uintptr_t>(kv_codes) % 128 || reinterpret_cast<uintptr_t>(kv_meta) % 16) {
-    return fail(OQ_ERR_MISALIGNED,
-                "decode_attn_int4_paged: query rows need 16-byte alignment, kv_codes 128 bytes, kv_meta 16 bytes");
+    return fail(OQ_ERR_MISALIGNED, "%s: query rows need 16-byte alignment, kv_codes 128 bytes, kv_meta 16 bytes", name);
   }
   if (num_pages * num_kv_heads * 2 * kPage >= (int64_t(1) << 31)) {
-    return fail(OQ_ERR_UNSUPPORTED, "decode_attn_int4_paged: page pool too large for 32-bit TMA rows");
+    return fail(OQ_ERR_UNSUPPORTED, "%s: page pool too large for 32-bit TMA rows", name);
   }
 
   using Kernel = void (*)(const CUtensorMap, AttnParams);
-  Kernel kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true>
-                                                : decode_attn_kernel<__nv_bfloat16, false>)
-                                   : (group > 4 ? decode_attn_kernel<__half, true> : decode_attn_kernel<__half, false>);
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  Kernel kernel;
+  if (bits == 8) {
+    kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 8>
+                                           : decode_attn_kernel<__nv_bfloat16, false, 8>)
+                              : (group > 4 ? decode_attn_kernel<__half, true, 8> : decode_attn_kernel<__half, false, 8>);
+  } else {
+    kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 4>
+                                           : decode_attn_kernel<__nv_bfloat16, false, 4>)
+                              : (group > 4 ? decode_attn_kernel<__half, true, 4> : decode_attn_kernel<__half, false, 4>);
+  }
+  const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
 
   // Split heuristic: as many KV ranges per (sequence, KV head) as fill one wave of
   // resident CTAs (SMs x CTAs per SM), so no SM idles behind a short last wave.
   const int64_t units = batch * num_kv_heads;
   int splits = num_splits;
   if (splits <= 0) {
-    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), kThreads, kSmemBytes);
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), kThreads, smem_bytes);
     // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
     splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
                                    std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
@@ -739,7 +858,7 @@ int decode_attn_impl(
   if (splits > 1 || workspace) {
     const size_t need = oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, splits);
     if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
-      return fail(OQ_ERR_WORKSPACE, "decode_attn_int4_paged: workspace of %zu bytes needed for %d splits", need,
+      return fail(OQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed for %d splits", name, need,
                   splits);
     }
   }
@@ -749,7 +868,7 @@ int decode_attn_impl(
                 : 1;
 
   CUtensorMap tmap;
-  int st = encode_codes_map(&tmap, kv_codes, num_pages, num_kv_heads);
+  int st = encode_codes_map(&tmap, kv_codes, num_pages, num_kv_heads, bits);
   if (st != OQ_OK) return st;
 
   AttnParams p;
@@ -783,7 +902,7 @@ int decode_attn_impl(
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  launch_plain(kernel, grid, dim3(kThreads), kSmemBytes, s, tmap, p);
+  launch_plain(kernel, grid, dim3(kThreads), smem_bytes, s, tmap, p);
   if (p.defer_merge) {
     const dim3 mgrid((unsigned)units, (unsigned)group);
     if (dtype == OQ_BF16) {
@@ -792,7 +911,7 @@ int decode_attn_impl(
       launch_plain(split_merge_kernel<__half>, mgrid, dim3(kMergeThreads), 0, s, p);
     }
   }
-  return check_launch("decode_attn_int4_paged");
+  return check_launch(name);
 }
 
 }  // namespace
@@ -809,10 +928,27 @@ extern "C" int oq_decode_attn_int4_paged(
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream) {
-  return oq::decode_attn_impl(query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages, page_size,
-                              block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_heads,
-                              num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32, out_lse,
-                              workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream);
+  return oq::decode_attn_impl(4, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32,
+                              out_lse, workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream);
+}
+
+extern "C" int oq_decode_attn_int8_paged(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream) {
+  return oq::decode_attn_impl(8, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32,
+                              out_lse, workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream);
 }
 
 extern "C" int oq_decode_attn_int4_paged_gated(
@@ -827,9 +963,29 @@ extern "C" int oq_decode_attn_int4_paged_gated(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream) {
   if (gate == nullptr) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int4_paged_gated: null gate");
-  return oq::decode_attn_impl(query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages, page_size,
-                              block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_heads,
-                              num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, nullptr, nullptr,
+  return oq::decode_attn_impl(4, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, nullptr,
+                              nullptr,
                               workspace, workspace_bytes, num_splits, gate, gate_stride_b, gate_stride_h,
+                              device_status, stream);
+}
+
+extern "C" int oq_decode_attn_int8_paged_gated(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    int32_t* device_status, void* stream) {
+  if (gate == nullptr) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_int8_paged_gated: null gate");
+  return oq::decode_attn_impl(8, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, nullptr,
+                              nullptr, workspace, workspace_bytes, num_splits, gate, gate_stride_b, gate_stride_h,
                               device_status, stream);
 }

@@ -37,8 +37,9 @@ __global__ void lse_merge_kernel(const float* __restrict__ part_out, const float
   if (out_lse != nullptr && lane == 0) out_lse[row] = denom > 0.0f ? m + logf(denom) : -INFINITY;
 }
 
-// One warp per (token, KV head, K|V) row: 32 lanes x head_dim/32 values.
-template <typename T>
+// One warp per (token, KV head, K|V) row: 32 lanes x head_dim/32 values.  kBits = 4: two
+// codes per byte, low nibble first; kBits = 8: one code per byte.
+template <typename T, int kBits>
 __global__ void gather_dequant_kernel(const uint8_t* __restrict__ kv_codes, const uint16_t* __restrict__ kv_meta,
                                       int64_t num_pages, int64_t page_size, const int32_t* __restrict__ block_table,
                                       int64_t bt_stride, int64_t max_pages, const int32_t* __restrict__ seq_lens,
@@ -70,16 +71,54 @@ __global__ void gather_dequant_kernel(const uint8_t* __restrict__ kv_codes, cons
   }
   const int64_t slot = t - lp * page_size;
   const int64_t blk = page * num_kv_heads + h;
-  const uint8_t* src = kv_codes + ((blk * 2 + kv) * page_size + slot) * (head_dim / 2);
+  const int64_t row_bytes = head_dim * kBits / 8;
+  const uint8_t* src = kv_codes + ((blk * 2 + kv) * page_size + slot) * row_bytes;
   const uint16_t* meta = kv_meta + (blk * 4 + 2 * kv) * page_size + slot;
   const float scale = __half2float(__ushort_as_half(meta[0]));
   const float mn = __half2float(__ushort_as_half(meta[page_size]));
   T* dst = (kv ? values : keys) + ((b * num_kv_heads + h) * max_len + t) * head_dim;
-  for (int64_t j = lane; j < head_dim / 2; j += 32) {
+  for (int64_t j = lane; j < row_bytes; j += 32) {
     const uint8_t byte = src[j];
-    dst[2 * j] = from_float<T>(__fadd_rn(mn, __fmul_rn(float(byte & 15), scale)));
-    dst[2 * j + 1] = from_float<T>(__fadd_rn(mn, __fmul_rn(float(byte >> 4), scale)));
+    if constexpr (kBits == 8) {
+      dst[j] = from_float<T>(__fadd_rn(mn, __fmul_rn(float(byte), scale)));
+    } else {
+      dst[2 * j] = from_float<T>(__fadd_rn(mn, __fmul_rn(float(byte & 15), scale)));
+      dst[2 * j + 1] = from_float<T>(__fadd_rn(mn, __fmul_rn(float(byte >> 4), scale)));
+    }
   }
+}
+
+template <int kBits>
+int gather_dequant_impl(const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+                        const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+                        const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,
+                        int64_t max_len, void* keys, void* values, int dtype, int32_t* device_status, void* stream) {
+  const char* name = kBits == 8 ? "gather_dequant_int8" : "gather_dequant_int4";
+  if (!valid_dtype(dtype)) return fail(OQ_ERR_UNSUPPORTED, "%s: unknown dtype %d", name, dtype);
+  if (batch < 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 || max_len < 0 || num_pages <= 0 ||
+      page_size <= 0 || max_pages_per_seq <= 0 || block_table_stride < max_pages_per_seq) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "%s: bad sizes", name);
+  }
+  if (batch == 0 || max_len == 0) return ok();
+  if (!kv_codes || !kv_meta || !block_table || !seq_lens || !keys || !values) {
+    return fail(OQ_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  }
+  const int64_t rows = batch * num_kv_heads * max_len * 2;
+  const int warps = 8;
+  const int64_t blocks = (rows + warps - 1) / warps;
+  if (blocks > 0x7fffffff) return fail(OQ_ERR_UNSUPPORTED, "%s: too many rows", name);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define OQ_GATHER(T)                                                                                              \
+  launch_plain(gather_dequant_kernel<T, kBits>, dim3(unsigned(blocks)), dim3(warps * 32), 0, s, kv_codes, kv_meta, \
+               num_pages, page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,         \
+               num_kv_heads, head_dim, max_len, static_cast<T*>(keys), static_cast<T*>(values), device_status)
+  switch (dtype) {
+    case OQ_F32: OQ_GATHER(float); break;
+    case OQ_F16: OQ_GATHER(__half); break;
+    default: OQ_GATHER(__nv_bfloat16); break;
+  }
+#undef OQ_GATHER
+  return check_launch(name);
 }
 
 }  // namespace
@@ -117,30 +156,18 @@ extern "C" int oq_gather_dequant_int4(
     const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,
     int64_t max_len, void* keys, void* values, int dtype,
     int32_t* device_status, void* stream) {
-  using namespace oq;
-  if (!valid_dtype(dtype)) return fail(OQ_ERR_UNSUPPORTED, "gather_dequant_int4: unknown dtype %d", dtype);
-  if (batch < 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 || max_len < 0 || num_pages <= 0 ||
-      page_size <= 0 || max_pages_per_seq <= 0 || block_table_stride < max_pages_per_seq) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "gather_dequant_int4: bad sizes");
-  }
-  if (batch == 0 || max_len == 0) return ok();
-  if (!kv_codes || !kv_meta || !block_table || !seq_lens || !keys || !values) {
-    return fail(OQ_ERR_INVALID_ARGUMENT, "gather_dequant_int4: null pointer");
-  }
-  const int64_t rows = batch * num_kv_heads * max_len * 2;
-  const int warps = 8;
-  const int64_t blocks = (rows + warps - 1) / warps;
-  if (blocks > 0x7fffffff) return fail(OQ_ERR_UNSUPPORTED, "gather_dequant_int4: too many rows");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define OQ_GATHER(T)                                                                                             \
-  launch_plain(gather_dequant_kernel<T>, dim3(unsigned(blocks)), dim3(warps * 32), 0, s, kv_codes, kv_meta, num_pages, \
-             page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch, num_kv_heads, head_dim,  \
-             max_len, static_cast<T*>(keys), static_cast<T*>(values), device_status)
-  switch (dtype) {
-    case OQ_F32: OQ_GATHER(float); break;
-    case OQ_F16: OQ_GATHER(__half); break;
-    default: OQ_GATHER(__nv_bfloat16); break;
-  }
-#undef OQ_GATHER
-  return check_launch("gather_dequant_int4");
+  return oq::gather_dequant_impl<4>(kv_codes, kv_meta, num_pages, page_size, block_table, block_table_stride,
+                                    max_pages_per_seq, seq_lens, batch, num_kv_heads, head_dim, max_len, keys, values,
+                                    dtype, device_status, stream);
+}
+
+extern "C" int oq_gather_dequant_int8(
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens, int64_t batch, int64_t num_kv_heads, int64_t head_dim,
+    int64_t max_len, void* keys, void* values, int dtype,
+    int32_t* device_status, void* stream) {
+  return oq::gather_dequant_impl<8>(kv_codes, kv_meta, num_pages, page_size, block_table, block_table_stride,
+                                    max_pages_per_seq, seq_lens, batch, num_kv_heads, head_dim, max_len, keys, values,
+                                    dtype, device_status, stream);
 }

@@ -1,13 +1,14 @@
-"""INT4 paged-KV decode attention launchers (drop-in for optiz_qwen/kernels/qserve_int4_attention.py).
+"""INT4 / INT8 paged-KV decode attention launchers (drop-in for optiz_qwen/kernels/qserve_int4_attention.py).
 
 Signatures, return shapes and error behaviour follow the reference launchers
 (:516-660): ``fn(query [B, Hq, 1, D] CUDA, layer, *, scaling) -> [B, 1, Hq, D]``
 in the query dtype; ``RuntimeError`` when the query is not a one-token CUDA
 tensor or the layer holds no packed KV; ``ValueError`` on a non-integer GQA
-ratio.  Both launchers run the same sm_100a kernel (C ABI
+ratio.  The INT4 launchers run one sm_100a kernel (C ABI
 ``oq_decode_attn_int4_paged``): the one-pass backend gives each (sequence, KV
 head) a single CTA, the split backend cuts the KV range over CTAs and merges
-the partials by log-sum-exp in the same launch.
+the partials by log-sum-exp in the same launch.  The INT8 launcher runs the
+8-bit instance of the same kernel (``oq_decode_attn_int8_paged``), split-KV.
 """
 
 from __future__ import annotations
@@ -28,7 +29,7 @@ int4_decode_available = triton_int4_decode_available
 
 
 def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: int, what: str,
-                  gate: torch.Tensor | None = None) -> torch.Tensor:
+                  gate: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
     if not (query.is_cuda and query.shape[-2] == 1):
         raise RuntimeError(f"{what} requires a CUDA query with sequence length 1.")
     paged = getattr(layer, "paged", None)
@@ -41,8 +42,10 @@ def _paged_decode(query: torch.Tensor, layer: Any, scaling: float, num_splits: i
     q = query[:, :, 0, :]
     if gate is not None:  # the decode forward's output gate, [B, 1, Hq * D] -> [B, Hq, D]
         gate = gate.reshape(batch, num_heads, head_dim)
-    out = cabi.decode_attention_int4(q, paged.pool, paged.block_table, paged.seq_lens, scaling,
-                                     workspace=layer.decode_workspace(num_heads), num_splits=num_splits, gate=gate)
+    if paged.pool.bits != bits:
+        raise RuntimeError(f"{what} requires a {bits}-bit cache; this layer holds {paged.pool.bits}-bit codes.")
+    out = cabi.decode_attention(q, paged.pool, paged.block_table, paged.seq_lens, scaling,
+                                workspace=layer.decode_workspace(num_heads), num_splits=num_splits, gate=gate)
     return out.unsqueeze(1)
 
 
@@ -63,6 +66,9 @@ def qserve_int4_split_decode_attention(query: torch.Tensor, layer: Any, *, scali
     return _paged_decode(query, layer, scaling, 0, "INT4 split decode", gate)
 
 
-def qserve_int8_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float) -> torch.Tensor:
-    """The 8-bit KV backend is not built on this path yet (the layer rejects k_bits=8)."""
-    raise NotImplementedError("INT8 paged decode attention is not implemented on this build.")
+def qserve_int8_decode_attention(query: torch.Tensor, layer: Any, *, scaling: float,
+                                 gate: torch.Tensor | None = None) -> torch.Tensor:
+    """Attend to an 8-bit packed cache (reference :548-573); split-KV with the in-launch merge.
+
+    ``gate``: as for :func:`qserve_int4_decode_attention`."""
+    return _paged_decode(query, layer, scaling, 0, "INT8 decode attention", gate, bits=8)

@@ -64,7 +64,8 @@ def _qserve_fused_forward(self, hidden_states: torch.Tensor, position_embeddings
                                                              gate=gate)
             gated = True
         elif backend == "triton_int8_decode":
-            attn_output = qserve_int8_decode_attention(query_states, cache_layer, scaling=self.scaling)
+            attn_output = qserve_int8_decode_attention(query_states, cache_layer, scaling=self.scaling, gate=gate)
+            gated = True
         else:
             attn_output = qserve_int4_decode_attention(query_states, cache_layer, scaling=self.scaling, gate=gate)
             gated = True

@@ -125,6 +125,23 @@ def dequantize_tokens_int4(packed, scale16, min16) -> np.ndarray:
     return np.asarray(min16, np.float32)[..., None] + codes * np.asarray(scale16, np.float32)[..., None]
 
 
+def quantize_tokens_int8(x: np.ndarray):
+    """The 8-bit variant of :func:`quantize_tokens_int4` (the reference's ``bits=8`` path of
+    ``_quantize_groupwise``, qserve_kv_cache.py:313-335: 255 levels, codes unpacked).
+
+    Returns ``(codes u8 [..., D], scale f16 [...], min f16 [...])``.
+    """
+    d = x.shape[-1]
+    codes, scale, gmin = quantize_groupwise(x, d, 8)
+    return codes, scale[..., 0].astype(np.float16), gmin[..., 0].astype(np.float16)
+
+
+def dequantize_tokens_int8(codes, scale16, min16) -> np.ndarray:
+    """fp32 dequantisation of 8-bit codes with the stored fp16 scale/min."""
+    c = np.asarray(codes, np.uint8).astype(np.float32)
+    return np.asarray(min16, np.float32)[..., None] + c * np.asarray(scale16, np.float32)[..., None]
+
+
 # --------------------------------------------------------------------------- paged layout
 
 META_K_SCALE, META_K_MIN, META_V_SCALE, META_V_MIN = 0, 1, 2, 3
@@ -157,16 +174,19 @@ def build_block_table(lengths, page_size: int, num_pages: int, max_pages_per_seq
 
 
 class PagedKvOracle:
-    """numpy mirror of the paged INT4 pool.
+    """numpy mirror of the paged INT4 (or INT8) pool.
 
-    ``kv_codes``: uint8 ``[num_pages, Hkv, 2, page_size, D/2]`` (index 0 = K, 1 = V)
+    ``kv_codes``: uint8 ``[num_pages, Hkv, 2, page_size, D * bits / 8]`` (index 0 = K, 1 = V)
     ``kv_meta`` : float16 ``[num_pages, Hkv, 4, page_size]`` (k_scale, k_min, v_scale, v_min)
     """
 
-    def __init__(self, num_pages, num_kv_heads, head_dim, page_size, block_table, seq_lens):
+    def __init__(self, num_pages, num_kv_heads, head_dim, page_size, block_table, seq_lens, bits: int = 4):
+        if bits not in (4, 8):
+            raise ValueError("bits must be 4 or 8")
         self.page_size = page_size
         self.head_dim = head_dim
-        self.kv_codes = np.zeros((num_pages, num_kv_heads, 2, page_size, head_dim // 2), np.uint8)
+        self.bits = bits
+        self.kv_codes = np.zeros((num_pages, num_kv_heads, 2, page_size, head_dim * bits // 8), np.uint8)
         self.kv_meta = np.zeros((num_pages, num_kv_heads, 4, page_size), np.float16)
         self.block_table = np.asarray(block_table, np.int32)
         self.seq_lens = np.asarray(seq_lens, np.int64).copy()
@@ -176,8 +196,9 @@ class PagedKvOracle:
 
         ``rows`` names the batch rows the tokens belong to (default: all rows in order).
         """
-        kp, ks, km = quantize_tokens_int4(keys)
-        vp, vs, vm = quantize_tokens_int4(values)
+        quant = quantize_tokens_int4 if self.bits == 4 else quantize_tokens_int8
+        kp, ks, km = quant(keys)
+        vp, vs, vm = quant(values)
         batch, _, n, _ = keys.shape
         rows = range(batch) if rows is None else rows
         for i, b in enumerate(rows):
@@ -203,13 +224,14 @@ class PagedKvOracle:
         meta = self.kv_meta[pages]                       # [np, H, 4, P]
         codes = codes.transpose(1, 2, 0, 3, 4).reshape(codes.shape[1], 2, -1, codes.shape[-1])[:, :, :length]
         meta = meta.transpose(1, 2, 0, 3).reshape(meta.shape[1], 4, -1)[:, :, :length]
-        k = dequantize_tokens_int4(codes[:, 0], meta[:, META_K_SCALE], meta[:, META_K_MIN])
-        v = dequantize_tokens_int4(codes[:, 1], meta[:, META_V_SCALE], meta[:, META_V_MIN])
+        deq = dequantize_tokens_int4 if self.bits == 4 else dequantize_tokens_int8
+        k = deq(codes[:, 0], meta[:, META_K_SCALE], meta[:, META_K_MIN])
+        v = deq(codes[:, 1], meta[:, META_V_SCALE], meta[:, META_V_MIN])
         return k, v
 
 
 def fill_paged_cache(rng: np.random.Generator, lengths, num_kv_heads, head_dim, page_size,
-                     num_pages=None, max_pages_per_seq=None, seed_pages=None, chunk=4096):
+                     num_pages=None, max_pages_per_seq=None, seed_pages=None, chunk=4096, bits: int = 4):
     """Build a populated ``PagedKvOracle`` with bf16-valued N(0,1) K/V (config-0 distribution).
 
     Returns the oracle; its pool arrays can be uploaded to the device as-is.
@@ -219,7 +241,7 @@ def fill_paged_cache(rng: np.random.Generator, lengths, num_kv_heads, head_dim, 
     num_pages = num_pages or need
     max_pages_per_seq = max_pages_per_seq or max(1, max(-(-n // page_size) for n in lengths))
     table = build_block_table(lengths, page_size, num_pages, max_pages_per_seq, seed_pages)
-    cache = PagedKvOracle(num_pages, num_kv_heads, head_dim, page_size, table, np.zeros(len(lengths)))
+    cache = PagedKvOracle(num_pages, num_kv_heads, head_dim, page_size, table, np.zeros(len(lengths)), bits=bits)
     for b, n in enumerate(lengths):
         start = 0
         while start < n:

@@ -46,8 +46,8 @@ def upload_pool(cache: kq.PagedKvOracle, device="cuda"):
     """Copy an oracle cache into a device PagedKvPool + block table + seq_lens."""
     from optiz_qwen_b200.cabi import PagedKvPool
 
-    num_pages, hkv, _, page, half = cache.kv_codes.shape
-    pool = PagedKvPool(num_pages, hkv, half * 2, page, device)
+    num_pages, hkv, _, page, _ = cache.kv_codes.shape
+    pool = PagedKvPool(num_pages, hkv, cache.head_dim, page, device, bits=cache.bits)
     pool.kv_codes.copy_(torch.from_numpy(cache.kv_codes))
     pool.kv_meta.copy_(torch.from_numpy(cache.kv_meta))
     table = torch.from_numpy(cache.block_table.astype(np.int32)).to(device)

@@ -20,7 +20,8 @@ def declared_symbols() -> set[str]:
 
 def test_header_declares_entry_points():
     names = declared_symbols()
-    for required in ("oq_append_quant_int4", "oq_decode_attn_int4_paged", "oq_lse_merge", "oq_gdn_recurrent"):
+    for required in ("oq_append_quant_int4", "oq_decode_attn_int4_paged", "oq_lse_merge", "oq_gdn_recurrent",
+                     "oq_append_quant_int8", "oq_decode_attn_int8_paged", "oq_gather_dequant_int8"):
         assert required in names
 
 

@@ -35,7 +35,8 @@ def _oracle_over_layer(query, layer):
     lens = layer.paged.seq_lens.cpu().numpy()
     cache = kq.PagedKvOracle.__new__(kq.PagedKvOracle)
     cache.kv_codes, cache.kv_meta, cache.block_table, cache.seq_lens = codes, meta, table, lens.astype(np.int64)
-    cache.page_size, cache.head_dim = 64, codes.shape[-1] * 2
+    cache.bits = layer.paged.pool.bits
+    cache.page_size, cache.head_dim = 64, codes.shape[-1] * 8 // cache.bits
     keys, values = zip(*(cache.gather(b) for b in range(len(lens))))
     out, _ = decode_attention(query.float().cpu().numpy()[:, :, 0], keys, values, 256 ** -0.5)
     return out

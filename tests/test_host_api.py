@@ -102,11 +102,23 @@ def test_qserve_config_validation(kwargs):
         QServeKvConfig(**kwargs).validate()
 
 
-def test_8bit_layers_are_rejected_on_this_build():
+def test_8bit_layers_build_an_8bit_pool_and_dispatch_to_the_8bit_entry_points():
+    from optiz_qwen_b200 import cabi
+
     cfg = QServeKvConfig(k_bits=8, v_bits=8, attention_backend="triton_int8_decode")
     cfg.validate()
-    with pytest.raises(ValueError, match="8-bit"):
-        QServeDeferredSplitFusedAttentionLayer(cfg)
+    layer = QServeDeferredSplitFusedAttentionLayer(cfg)
+    assert layer.config.k_bits == 8
+    pool8 = cabi.PagedKvPool(2, 2, 256, 64, "cpu", bits=8)
+    pool4 = cabi.PagedKvPool(2, 2, 256, 64, "cpu")
+    assert tuple(pool8.kv_codes.shape) == (2, 2, 2, 64, 256)
+    assert tuple(pool4.kv_codes.shape) == (2, 2, 2, 64, 128)
+    assert cabi._bits_entry("decode_attn", pool8, None) == "oq_decode_attn_int8"
+    assert cabi._bits_entry("append_quant", pool4, 4) == "oq_append_quant_int4"
+    with pytest.raises(ValueError, match="8-bit codes"):
+        cabi._bits_entry("gather_dequant", pool8, 4)
+    with pytest.raises(ValueError, match="bits must be 4 or 8"):
+        cabi.PagedKvPool(2, 2, 256, 64, "cpu", bits=2)
 
 
 def test_removed_kv_chain_names_are_rejected():

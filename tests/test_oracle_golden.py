@@ -154,3 +154,20 @@ def test_sigmoid_gate_matches_reference_expression():
     got = ep.sigmoid_gate(_bf16_from_bits(g["gate_attn"]), _bf16_from_bits(g["gate_g"]), rnd=kq.round_bf16)
     want = _bf16_from_bits(g["gate_y"])
     assert np.array_equal(got, want)
+
+
+def test_int8_token_format_matches_the_reference_quantiser(quant):
+    """The B200 8-bit token format = the reference's bits=8 quantiser with group = head_dim,
+    scale/min rounded to fp16; the paged oracle round-trips it."""
+    x = kq.bf16_bits_to_f32(quant["x_bf16"])
+    codes, scale, mn = kq.quantize_tokens_int8(x)
+    ref_codes, ref_scale, ref_min = kq.quantize_groupwise(x, x.shape[-1], 8)
+    np.testing.assert_array_equal(codes, ref_codes)
+    np.testing.assert_array_equal(scale, ref_scale[..., 0].astype(np.float16))
+    deq = kq.dequantize_tokens_int8(codes, scale, mn)
+    assert np.all(np.abs(deq - x) <= 0.51 * scale.astype(np.float32)[..., None] + 2e-3 * np.abs(x).max())
+    rng = np.random.default_rng(2)
+    cache = kq.fill_paged_cache(rng, [70, 5], 2, 256, 64, seed_pages=3, bits=8)
+    assert cache.kv_codes.shape[-1] == 256
+    k, v = cache.gather(0)
+    assert k.shape == (2, 70, 256) and v.shape == (2, 70, 256)
