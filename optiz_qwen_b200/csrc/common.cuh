@@ -207,6 +207,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
       : "memory");
 }
 
+// Brings a tensor map (a kernel parameter) into the TMA unit's descriptor cache ahead of
+// its first copy.
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int32_t x, int32_t y, int32_t z,
                                             uint64_t* bar) {
@@ -340,5 +346,17 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads().
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier over `count` threads that also ORs `pred` across them (every participant
+// gets the result), the named-barrier form of __syncthreads_or.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.cta.red.or.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 }  // namespace oq

@@ -34,18 +34,10 @@ constexpr int kStages = 4;
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 
-constexpr int kPageIdSlots = 1024;  // page ids of a CTA's range kept in shared memory
-
 struct __align__(16) SmemTail {
-  union {
-    uint32_t qfrag[4][32][8];        // prologue: per k-step, per lane B-operand digit fragments
-    int32_t page_ids[kPageIdSlots];  // main loop: block-table entries of this CTA's page range
-  } u;
+  uint32_t qfrag[4][32][8];  // prologue: per k-step, per lane B-operand digit fragments
   uint64_t full[kStages];
   int stage_ok[kStages];
-  int q_exp[kMaxGroup];      // per head: q ~ q_int * 2^-q_exp
-  float q_scale[kMaxGroup];  // 2^-q_exp
-  float q_sum[kMaxGroup];    // sum(q) (exact fp32)
   float warp_m[kWarps][kMaxGroup];
   float warp_l[kWarps][kMaxGroup];
   float warp_f[kWarps][kMaxGroup];  // 2^(m_w - M) merge factor of each warp
@@ -55,12 +47,19 @@ struct __align__(16) SmemTail {
 };
 
 // Page formats: INT4 (two codes per byte, 16 KB of codes per page and KV head, 4 stages)
-// and INT8 (one code per byte, 32 KB, 3 stages so that two CTAs still share an SM).
+// and INT8 (one code per byte, 32 KB, 3 stages).  A CTA holds kWG warp groups of 4 warps,
+// each with its own stage ring, barriers and share of the CTA's pages: 3 groups for INT4
+// and 2 for INT8, one CTA per SM (the shared memory of the rings and the registers of
+// 384 threads at up to 170 per thread).
 template <int kBits>
 struct PageFormat {
   static constexpr int kCodeBytes = 2 * kPage * kHeadDim * kBits / 8;
   static constexpr int kStagesN = kBits == 8 ? 3 : kStages;
-  static constexpr size_t kSmem = 1024 /*alignment slack*/ + kStagesN * (kCodeBytes + kStageMetaBytes) + sizeof(SmemTail);
+  static constexpr int kWG = kBits == 8 ? 2 : 3;
+  // one warp group's region, 1024-aligned: stage codes | stage metas | tail
+  static constexpr size_t kWgBytes =
+      (size_t(kStagesN) * (kCodeBytes + kStageMetaBytes) + sizeof(SmemTail) + 1023) / 1024 * 1024;
+  static constexpr size_t kSmem = 1024 /*alignment slack*/ + kWG * kWgBytes;
 };
 
 // ---- q.k on integer tensor cores.
@@ -118,18 +117,29 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
 }
 
 template <typename T, bool kDual, int kBits>
-__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                               AttnParams p) {
+__global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmap, AttnParams p) {
   constexpr int kSt = PageFormat<kBits>::kStagesN;
   constexpr int kCB = PageFormat<kBits>::kCodeBytes;
+  constexpr int kWG = PageFormat<kBits>::kWG;
+  constexpr int kNT = kWG * kThreads;  // threads of the CTA
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* codes = smem;                                       // kSt x kCB bytes, 1024-aligned
-  uint8_t* metas = smem + kSt * kCB;                           // kSt x 512 B
+  // Warp group wg runs the page loop below on its own region; `tid`, `warp` and every
+  // barrier of the loop are local to the group (named barrier 1 + wg over its 128 threads).
+  const int ctid = threadIdx.x;
+  const int wg = ctid / kThreads;
+  const int bar_wg = 1 + wg;
+  uint8_t* codes = smem + wg * PageFormat<kBits>::kWgBytes;  // kSt x kCB bytes, 1024-aligned
+  uint8_t* metas = codes + kSt * kCB;                           // kSt x 512 B
   SmemTail* tail = reinterpret_cast<SmemTail*>(metas + kSt * kStageMetaBytes);
+  auto tail_of = [&](int g) {
+    return reinterpret_cast<SmemTail*>(smem + g * PageFormat<kBits>::kWgBytes + kSt * (kCB + kStageMetaBytes));
+  };
 
-  const int tid = threadIdx.x;
+  const int tid = ctid - wg * kThreads;
   const int lane = tid & 31;
+  if (tid == 0) prefetch_tensormap(&tmap);  // the first copies are issued in a few microseconds
   const int warp = tid >> 5;
   const int r = lane >> 2;  // mma groupID
   const int c = lane & 3;   // mma thread-in-group
@@ -138,8 +148,37 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int64_t b = blockIdx.z;
   const int G = p.group;
 
+  // ---- every independent global load of the prologue is issued first, so their latencies
+  // overlap.  Group wg takes pages cta_begin + wg + kWG * i of the CTA's range (round robin,
+  // so the groups' shares differ by at most one page), which makes the page ids of its first
+  // kSt pages known before the sequence length is: they go out with the length and the 64
+  // query elements this lane needs.
+  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
+  const int cta_begin = split * p.pages_per_split;
+  auto page_at = [&](int i) { return cta_begin + wg + kWG * i; };  // sequence page of this group's page i
+  const int32_t* bt_row = p.block_table + b * p.bt_stride;
+  const bool pre_ok = warp == 0 && lane < kSt && int64_t(page_at(lane)) < p.max_pages;
+  // This lane feeds q.k MMA column r: head (packed) r & 3, digit hi for r < 4 and lo for
+  // r >= 4; (dual) head r, both digits.  It holds dims 64c .. 64c+63 of that head, so the
+  // four lanes (r, 0..3) hold the whole head.
+  const int f_head = kDual ? r : (r & 3);
+  const bool f_has = f_head < G;
   pdl_wait();  // (one long wave: the successor is allowed to launch only after the page loop)
-  const int len = max(p.seq_lens[b], 0);
+  const int32_t len_raw = p.seq_lens[b];
+  const int first_pre = pre_ok ? bt_row[page_at(lane)] : -1;
+  uint4 qv[8];
+  {
+    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (f_has ? f_head : 0)) * p.q_sh +
+                    64 * c;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qv[i] = f_has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
+  }
+  if (tid == 0) {
+    for (int s2 = 0; s2 < kSt; ++s2) mbar_init(&tail->full[s2], 1);
+    fence_mbar_init();
+  }
+
+  const int len = max(len_raw, 0);
   const int len_pages = (len + kPage - 1) / kPage;
   const int npages_b = int(min(int64_t(len_pages), p.max_pages));
   const int nsplit_b = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
@@ -147,82 +186,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     pdl_allow_next();
     return;
   }
-  if (len_pages > p.max_pages && tid == 0 && split == 0) report(p.status, OQ_DEV_OVERFLOW);
-  const int page_begin = split * p.pages_per_split;
-  const int n = max(0, min(npages_b, page_begin + p.pages_per_split) - page_begin);
+  if (len_pages > p.max_pages && ctid == 0 && split == 0) report(p.status, OQ_DEV_OVERFLOW);
+  const int cta_n = max(0, min(npages_b, cta_begin + p.pages_per_split) - cta_begin);
+  // this group's share of the CTA's pages (an empty share is fine: m = -inf, l = 0)
+  const int n = cta_n > wg ? (cta_n - wg + kWG - 1) / kWG : 0;
+  const int first_page = (warp == 0 && lane < min(n, kSt)) ? first_pre : -1;
+  // thread 0 loads the page id of the page it issues next one loop iteration ahead
+  int next_pid = (tid == 0 && kSt < n) ? bt_row[page_at(kSt)] : 0;
 
-  // ---- every independent global load of the prologue is issued first, so their
-  // latencies overlap: the first kSt page ids (one lane each), this thread's
-  // share of the remaining page ids, and the query elements this thread needs.
-  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
-  constexpr int kPidRegs = kPageIdSlots / kThreads;
-  const int32_t* bt_row = p.block_table + b * p.bt_stride;
-  const int n_smem = min(n, kPageIdSlots);
-  const int first_page = (warp == 0 && lane < min(n, kSt)) ? bt_row[page_begin + lane] : -1;
-  int pid_reg[kPidRegs];
-#pragma unroll
-  for (int j = 0; j < kPidRegs; ++j) {
-    const int idx = kSt + tid + j * kThreads;
-    pid_reg[j] = idx < n_smem ? bt_row[page_begin + idx] : 0;
-  }
-  // warp 0: a quarter of one head per lane (head lane/4, dims 64*(lane%4) ..) for the exponents
-  const int e_head = lane >> 2, e_part = lane & 3;
-  uint4 qe[8];
-  {
-    const bool has = warp == 0 && e_head < G;
-    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (has ? e_head : 0)) * p.q_sh +
-                    64 * e_part;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qe[i] = has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
-  }
-  // every warp: the 16 dims of k-step `warp` for this lane's MMA column (see below)
-  const int f_head = kDual ? r : (r & 3);
-  const bool f_has = f_head < G;
-  uint4 qf[2];
-  {
-    const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (f_has ? f_head : 0)) * p.q_sh +
-                    64 * c + 16 * warp;
-#pragma unroll
-    for (int half = 0; half < 2; ++half)
-      qf[half] = f_has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * half)) : make_uint4(0, 0, 0, 0);
-  }
-
-  if (tid == 0) {
-    for (int s = 0; s < kSt; ++s) mbar_init(&tail->full[s], 1);
-    fence_mbar_init();
-  }
-  // warp 0: per-head fixed-point exponent and sum(q)
-  if (warp == 0) {
-    float amax = 0.0f, sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const T* e = reinterpret_cast<const T*>(&qe[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float v = to_float<T>(e[j]);
-        amax = fmaxf(amax, fabsf(v));
-        sum += v;
-      }
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (e_part == 0) {
-      int ex = 0;
-      if (amax > 0.0f) {
-        frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &ex);  // kQMax / amax = f * 2^ex, f in [0.5, 1)
-        ex -= 1;                                            // 2^ex <= kQMax / amax
-      }
-      tail->q_exp[e_head] = ex;
-      tail->q_scale[e_head] = ldexpf(1.0f, -ex);
-      tail->q_sum[e_head] = sum;
-    }
-  }
-  __syncthreads();  // barriers initialised, exponents known
-
-  // page id of range page i: the first kSt were fetched by warp 0's lanes,
-  // later ones come from the shared-memory copy made after the prologue
   auto issue = [&](int i, int s, int64_t page) {
     if (page < 0 || page >= p.num_pages) {
       tail->stage_ok[s] = 0;
@@ -240,6 +211,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
     bulk_load(metas + s * kStageMetaBytes, p.kv_meta + blk * 4 * kPage, kStageMetaBytes, &tail->full[s]);
   };
+  // warp 0: the first copies (thread 0 initialised the barriers above; the other threads
+  // first wait on them after the group barrier at the end of the prologue)
   int issued = 0;
   if (warp == 0) {
 #pragma unroll
@@ -250,19 +223,49 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     issued = min(n, kSt);
   }
 
-  // ---- query digits (B operand of q.k).  This lane feeds MMA column r: head
-  // (packed) r & 3, digit hi for r < 4 and lo for r >= 4; (dual) head r, both
-  // digits.  Lane c supplies dims 64c .. 64c+63; k-step s covers dims
-  // 64c + 16s + {0..15}: the even dims in the "low nibble" MMA, the odd dims in
-  // the "high nibble" MMA.  Warp w builds k-step w for all 32 lanes.  INT8: the
-  // same 16 dims feed two MMAs, 2w (dims 64c + 16w + 0..7) and 2w + 1 (+ 8..15),
-  // each taking 4 dims per word: words (b0, b1) of MMA 2w, then of MMA 2w + 1.
+  // ---- query digits (B operand of q.k).
+  // Per head: 15-bit fixed point with exponent e (2^e <= kQMax / max|q|), from the
+  // largest element of the head (the four lanes of the head reduce by shuffles), and
+  // sum(q).  k-step s covers dims 64c + 16s + {0..15}: the even dims in the "low
+  // nibble" MMA, the odd dims in the "high nibble" MMA.  INT8: the same 16 dims feed
+  // two MMAs, 2s (dims 64c + 16s + 0..7) and 2s + 1 (+ 8..15), each taking 4 dims per
+  // word: words (b0, b1) of MMA 2s, then of MMA 2s + 1.
+  float amax = 0.0f, qsum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const T* e = reinterpret_cast<const T*>(&qv[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = to_float<T>(e[j]);
+      amax = fmaxf(amax, fabsf(v));
+      qsum += v;
+    }
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  int q_exp = 0;
+  if (amax > 0.0f) {
+    frexpf(float(kQMax) / fmaxf(amax, 1e-30f), &q_exp);  // kQMax / amax = f * 2^e, f in [0.5, 1)
+    q_exp -= 1;                                           // 2^e <= kQMax / amax
+  }
+  const float q_scale = ldexpf(1.0f, -q_exp);
+  // warp w builds k-step w for all 32 lanes; the fragments are exchanged in shared memory
   {
-    const float up = f_has ? ldexpf(1.0f, tail->q_exp[f_head]) : 0.0f;
+    const float up = f_has ? ldexpf(1.0f, q_exp) : 0.0f;
+    uint4 qw[2] = {qv[0], qv[1]};  // the 16 dims of k-step `warp` (selected with constant indices)
+#pragma unroll
+    for (int w = 1; w < 4; ++w) {
+      if (warp == w) {
+        qw[0] = qv[2 * w];
+        qw[1] = qv[2 * w + 1];
+      }
+    }
     uint32_t frag[8];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {  // word 2s (b0) and word 2s+1 (b1) of the step
-      const T* e = reinterpret_cast<const T*>(&qf[half]);
+      const T* e = reinterpret_cast<const T*>(&qw[half]);
       int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -285,10 +288,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         ho = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
         lo = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
       }
-      if (kDual) {
-        frag[half] = he;          // set 0 (hi digits): low-nibble MMA
-        frag[2 + half] = ho;      //                     high-nibble MMA
-        frag[4 + half] = le;      // set 1 (lo digits)
+      if constexpr (kDual) {
+        frag[half] = he;      // set 0 (hi digits): low-nibble MMA
+        frag[2 + half] = ho;  //                     high-nibble MMA
+        frag[4 + half] = le;  // set 1 (lo digits)
         frag[6 + half] = lo;
       } else {
         frag[half] = r < 4 ? he : le;
@@ -297,34 +300,28 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         frag[6 + half] = 0;
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(tail->u.qfrag[warp][lane]);
+    uint4* dst = reinterpret_cast<uint4*>(tail->qfrag[warp][lane]);
     dst[0] = make_uint4(frag[0], frag[1], frag[2], frag[3]);
     dst[1] = make_uint4(frag[4], frag[5], frag[6], frag[7]);
   }
-  __syncthreads();
+  named_bar_sync(bar_wg, kThreads);  // fragments written; the stage barriers are initialised
   uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const uint4* src = reinterpret_cast<const uint4*>(tail->u.qfrag[s][lane]);
+  for (int st4 = 0; st4 < 4; ++st4) {
+    const uint4* src = reinterpret_cast<const uint4*>(tail->qfrag[st4][lane]);
 #pragma unroll
     for (int k = 0; k < kSets; ++k) {
       const uint4 f = src[k];
-      bq_lo[k][s][0] = f.x;
-      bq_lo[k][s][1] = f.y;
-      bq_hi[k][s][0] = f.z;
-      bq_hi[k][s][1] = f.w;
+      bq_lo[k][st4][0] = f.x;
+      bq_lo[k][st4][1] = f.y;
+      bq_hi[k][st4][0] = f.z;
+      bq_hi[k][st4][1] = f.w;
     }
   }
-  __syncthreads();  // every warp holds its fragments: the union now takes the page ids
-#pragma unroll
-  for (int j = 0; j < kPidRegs; ++j) {
-    const int idx = kSt + tid + j * kThreads;
-    if (idx < n_smem) tail->u.page_ids[idx] = pid_reg[j];
-  }
-  __syncthreads();
-  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds
-  const float qs_a = tail->q_sum[2 * c], qs_b = tail->q_sum[2 * c + 1];
-  const float qx_a = tail->q_scale[2 * c], qx_b = tail->q_scale[2 * c + 1];
+  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds: lanes
+  // 8c (r = 2c) and 8c + 4 (r = 2c + 1) hold them
+  const float qs_a = __shfl_sync(0xffffffffu, qsum, 8 * c), qs_b = __shfl_sync(0xffffffffu, qsum, 8 * c + 4);
+  const float qx_a = __shfl_sync(0xffffffffu, q_scale, 8 * c), qx_b = __shfl_sync(0xffffffffu, q_scale, 8 * c + 4);
   const bool ha_ok = (kDual || c < 2) && 2 * c < G;
   const bool hb_ok = (kDual || c < 2) && 2 * c + 1 < G;
 
@@ -340,20 +337,70 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int tok1 = tok0 + 8;
   bool aborted = false;
 
+  // p.v of one page: acc += V^T P' with the V codes of stage `stv` and P' (B operand) pv0, pv1
+  auto pv_page = [&](const uint8_t* stv, uint32_t pv0, uint32_t pv1) {
+    const int tb = warp * 16 + kPage;  // V rows follow the 64 K rows
+    // ---------------- values: A = V^T codes (16 dims x 16 tokens), B = P' (16 tokens x 8 heads)
+    if constexpr (kBits == 8) {
+      // half hf, lane r: 16-byte chunk 8 hf + r of the four token rows; MMA 8 hf + k has
+      // row r = dim 128 hf + 16 r + 2k, row r + 8 = that dim + 1, each code as fp16 1024 + c
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint4 xa = *swz8(stv, tb + 2 * c, 8 * hf + r), xb = *swz8(stv, tb + 2 * c + 1, 8 * hf + r);
+        const uint4 xc = *swz8(stv, tb + 2 * c + 8, 8 * hf + r), xd = *swz8(stv, tb + 2 * c + 9, 8 * hf + r);
+        const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w}, wb[4] = {xb.x, xb.y, xb.z, xb.w};
+        const uint32_t wc[4] = {xc.x, xc.y, xc.z, xc.w}, wd[4] = {xd.x, xd.y, xd.z, xd.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t pb = 2u * uint32_t(k & 1);  // bytes pb, pb + 1 of word k / 2
+          const uint32_t sel = pb | ((4u + pb) << 4) | ((pb + 1u) << 8) | ((5u + pb) << 12);
+          const uint32_t x = prmt(wa[k >> 1], wb[k >> 1], sel);  // tokens 2c, 2c+1: dims 2k, 2k+1 of the chunk
+          const uint32_t y = prmt(wc[k >> 1], wd[k >> 1], sel);  // tokens 2c+8, 2c+9
+          uint32_t a[4];
+          a[0] = prmt(x, kFp16Hi, 0x4140u);  // row r: dim 2k, 1024 + c
+          a[1] = prmt(x, kFp16Hi, 0x4342u);  // row r+8: dim 2k + 1
+          a[2] = prmt(y, kFp16Hi, 0x4140u);
+          a[3] = prmt(y, kFp16Hi, 0x4342u);
+          mma_f16_16816(acc[8 * hf + k], a, pv0, pv1);
+        }
+      }
+    } else {
+      const uint4 va = *swz(stv, tb + 2 * c, r), vb = *swz(stv, tb + 2 * c + 1, r);
+      const uint4 vc = *swz(stv, tb + 2 * c + 8, r), vd = *swz(stv, tb + 2 * c + 9, r);
+      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+      const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w}, wd[4] = {vd.x, vd.y, vd.z, vd.w};
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+        for (int bs = 0; bs < 4; ++bs) {
+          const uint32_t x = prmt(wa[wi], wb[wi], byte_pair_sel(bs));  // tokens 2c, 2c+1: dims 2bs, 2bs+1
+          const uint32_t y = prmt(wc[wi], wd[wi], byte_pair_sel(bs));  // tokens 2c+8, 2c+9
+          uint32_t a[4];
+          a[0] = lop3_and_or(x, 0x000F000Fu, kFp16Bias);  // row r: even dim, 1024 + c
+          a[1] = lop3_and_or(x, 0x00F000F0u, kFp16Bias);  // row r+8: odd dim, 1024 + 16 c
+          a[2] = lop3_and_or(y, 0x000F000Fu, kFp16Bias);
+          a[3] = lop3_and_or(y, 0x00F000F0u, kFp16Bias);
+          mma_f16_16816(acc[4 * wi + bs], a, pv0, pv1);
+        }
+      }
+    }
+    
+  };
+
+  // Page i: q.k, softmax and p.v; then the stage is refilled with page i + kSt.  (Running
+  // the p.v of page i - 1 in the same block as the q.k of page i was measured: no faster.)
   for (int i = 0; i < n; ++i) {
     const int s = i % kSt;
-    const uint32_t parity = (i / kSt) & 1;
-    bool ready = wait_stage(&tail->full[s], parity);
+    bool ready = wait_stage(&tail->full[s], (i / kSt) & 1);
     ready = __all_sync(0xffffffffu, ready);
-    const int page_tokens = min(kPage, len - (page_begin + i) * kPage);
-    if (ready && tail->stage_ok[s] && warp * 16 < page_tokens) {
+    // tokens of page i (0 when its copy failed: every score is masked)
+    const int page_tokens = (ready && tail->stage_ok[s]) ? min(kPage, len - page_at(i) * kPage) : 0;
+    if (warp * 16 < page_tokens) {
       const uint8_t* st = codes + s * kCB;
       const __half* meta = reinterpret_cast<const __half*>(metas + s * kStageMetaBytes);
-      const int tb = warp * 16 + kPage;  // V rows follow the 64 K rows
 
       // ---------------- integer q.k: A = K codes (16 tokens x 32 dims, u8), B = q digits (s8)
       int dot_a0, dot_b0, dot_a1, dot_b1;  // (token r, head 2c), (r, 2c+1), (r+8, 2c), (r+8, 2c+1)
-      uint4 va, vb, vc, vd;
       if constexpr (kBits == 8) {
         // lane c holds dims 64c .. 64c + 63 of both token rows (16 words each); MMA "lo" of
         // step s takes words 4s (b0 dims) and 4s + 2, MMA "hi" words 4s + 1 and 4s + 3,
@@ -396,10 +443,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       } else {
         const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
         const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
-        va = *swz(st, tb + 2 * c, r);
-        vb = *swz(st, tb + 2 * c + 1, r);
-        vc = *swz(st, tb + 2 * c + 8, r);
-        vd = *swz(st, tb + 2 * c + 9, r);
         const uint32_t w0[8] = {k00.x, k00.y, k00.z, k00.w, k01.x, k01.y, k01.z, k01.w};
         const uint32_t w1[8] = {k10.x, k10.y, k10.z, k10.w, k11.x, k11.y, k11.z, k11.w};
         int lo[kSets][4], hi[kSets][4];
@@ -496,75 +539,32 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         sp_b += r0.y + r1.y;
       }
       // transpose into the B operand of p.v
-      const uint32_t pb0 = movmatrix_trans(blk0);
-      const uint32_t pb1 = movmatrix_trans(blk1);
-
-      // ---------------- values: A = V^T codes (16 dims x 16 tokens), B = P' (16 tokens x 8 heads)
-      if constexpr (kBits == 8) {
-        // half hf, lane r: 16-byte chunk 8 hf + r of the four token rows; MMA 8 hf + k has
-        // row r = dim 128 hf + 16 r + 2k, row r + 8 = that dim + 1, each code as fp16 1024 + c
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint4 xa = *swz8(st, tb + 2 * c, 8 * hf + r), xb = *swz8(st, tb + 2 * c + 1, 8 * hf + r);
-          const uint4 xc = *swz8(st, tb + 2 * c + 8, 8 * hf + r), xd = *swz8(st, tb + 2 * c + 9, 8 * hf + r);
-          const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w}, wb[4] = {xb.x, xb.y, xb.z, xb.w};
-          const uint32_t wc[4] = {xc.x, xc.y, xc.z, xc.w}, wd[4] = {xd.x, xd.y, xd.z, xd.w};
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t pb = 2u * uint32_t(k & 1);  // bytes pb, pb + 1 of word k / 2
-            const uint32_t sel = pb | ((4u + pb) << 4) | ((pb + 1u) << 8) | ((5u + pb) << 12);
-            const uint32_t x = prmt(wa[k >> 1], wb[k >> 1], sel);  // tokens 2c, 2c+1: dims 2k, 2k+1 of the chunk
-            const uint32_t y = prmt(wc[k >> 1], wd[k >> 1], sel);  // tokens 2c+8, 2c+9
-            uint32_t a[4];
-            a[0] = prmt(x, kFp16Hi, 0x4140u);  // row r: dim 2k, 1024 + c
-            a[1] = prmt(x, kFp16Hi, 0x4342u);  // row r+8: dim 2k + 1
-            a[2] = prmt(y, kFp16Hi, 0x4140u);
-            a[3] = prmt(y, kFp16Hi, 0x4342u);
-            mma_f16_16816(acc[8 * hf + k], a, pb0, pb1);
-          }
-        }
-      } else {
-        const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-        const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w}, wd[4] = {vd.x, vd.y, vd.z, vd.w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-#pragma unroll
-          for (int bs = 0; bs < 4; ++bs) {
-            const uint32_t x = prmt(wa[wi], wb[wi], byte_pair_sel(bs));  // tokens 2c, 2c+1: dims 2bs, 2bs+1
-            const uint32_t y = prmt(wc[wi], wd[wi], byte_pair_sel(bs));  // tokens 2c+8, 2c+9
-            uint32_t a[4];
-            a[0] = lop3_and_or(x, 0x000F000Fu, kFp16Bias);  // row r: even dim, 1024 + c
-            a[1] = lop3_and_or(x, 0x00F000F0u, kFp16Bias);  // row r+8: odd dim, 1024 + 16 c
-            a[2] = lop3_and_or(y, 0x000F000Fu, kFp16Bias);
-            a[3] = lop3_and_or(y, 0x00F000F0u, kFp16Bias);
-            mma_f16_16816(acc[4 * wi + bs], a, pb0, pb1);
-          }
-        }
-      }
+      pv_page(st, movmatrix_trans(blk0), movmatrix_trans(blk1));
     }
-    const bool stop = __syncthreads_or(!ready);
+    const bool stop = named_bar_or(bar_wg, kThreads, !ready);
     if (stop) {
       aborted = true;
       break;
     }
     if (tid == 0 && i + kSt < n) {
       const int nxt = i + kSt;
-      issue(nxt, s, nxt < kPageIdSlots ? tail->u.page_ids[nxt] : bt_row[page_begin + nxt]);
+      issue(nxt, s, next_pid);
       ++issued;
+      if (nxt + 1 < n) next_pid = bt_row[page_at(nxt + 1)];
     }
   }
 
   pdl_allow_next();
-  if (aborted) {
+  if (aborted && tid == 0) {
     // Leave no copy in flight before the CTA exits: wait (bounded) for every issued stage.
-    if (tid == 0) {
-      report(p.status, OQ_DEV_TIMEOUT);
-      for (int i = max(0, issued - kSt); i < issued; ++i) {
-        wait_stage(&tail->full[i % kSt], (i / kSt) & 1);
-      }
+    report(p.status, OQ_DEV_TIMEOUT);
+    for (int i = max(0, issued - kSt); i < issued; ++i) {
+      wait_stage(&tail->full[i % kSt], (i / kSt) & 1);
     }
-    return;
   }
+  // The groups finish their page loops at different times; from here on the whole CTA
+  // works together (every stage of every group has been consumed).
+  if (__syncthreads_or(aborted)) return;
 
   // ---- reduce this warp's per-lane sums over the 8 token rows
 #pragma unroll
@@ -582,25 +582,36 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     tail->warp_l[warp][2 * c] = l_a;
     tail->warp_l[warp][2 * c + 1] = l_b;
   }
-  __syncthreads();  // also: every stage has been consumed, codes[] is free for reuse
+  const int outputs = G * kHeadDim;
+  const bool single = nsplit_b == 1;
+  __syncthreads();
 
-  if (tid < G) {
+  // per head, over every warp of every group: M = the largest reference max, L = the sums at
+  // M, and each warp's factor 2^(m_w - M)
+  if (ctid < G) {
     float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail->warp_m[w][tid]);
-    float L = 0.0f;
-    for (int w = 0; w < kWarps; ++w) {
-      const float f = M == -INFINITY ? 0.0f : exp2f(tail->warp_m[w][tid] - M);
-      tail->warp_f[w][tid] = f;
-      L += tail->warp_l[w][tid] * f;
+#pragma unroll
+    for (int g = 0; g < kWG; ++g) {
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, tail_of(g)->warp_m[w][ctid]);
     }
-    tail->head_m[tid] = M;
-    tail->head_l[tid] = L;
+    float L = 0.0f;
+#pragma unroll
+    for (int g = 0; g < kWG; ++g) {
+      SmemTail* tg = tail_of(g);
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = M == -INFINITY ? 0.0f : exp2f(tg->warp_m[w][ctid] - M);
+        tg->warp_f[w][ctid] = f;
+        L = fmaf(tg->warp_l[w][ctid], f, L);
+      }
+    }
+    tail_of(0)->head_m[ctid] = M;
+    tail_of(0)->head_l[ctid] = L;
   }
   __syncthreads();
 
-  // ---- merge the 4 warps: red[w][h][d] = numerator_w * 2^(m_w - M), with
+  // ---- each warp's numerators at the common max: red[w][h][d] = numerator_w * 2^(m_w - M),
   //      numerator = 2^kTau * (acc - 1024 sum(P')) / (1 or 16) + sum(p * v_min)
-  float* red = reinterpret_cast<float*>(codes);  // kWarps * kMaxGroup rows of kRedStride floats
+  float* red = reinterpret_cast<float*>(codes);  // this group's kWarps * kMaxGroup rows of kRedStride floats
   {
     const int ha = 2 * c, hb = 2 * c + 1;
     const float fa = ha < G ? tail->warp_f[warp][ha] : 0.0f;
@@ -622,36 +633,52 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
   }
+  // this thread's outputs are e = ctid + j * kNT; their gate elements go out before the barrier
+  constexpr int kPerThread = (kMaxGroup * kHeadDim + kNT - 1) / kNT;
+  float gv[kPerThread];
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int e = ctid + j * kNT;
+    gv[j] = single && e < outputs ? gate_value<T>(p, b, int64_t(kvh) * G + e / kHeadDim, e % kHeadDim) : 0.0f;
+  }
   __syncthreads();
 
-  const int outputs = G * kHeadDim;
+  // ---- sum the warps of every group: the CTA's output (one split) or its partial record
   const int64_t unit = b * p.num_kv_heads + kvh;
-  const bool single = nsplit_b == 1;
   const int rec_floats = G * (kHeadDim + 2);
   float* my_rec = p.partials + (unit * p.max_splits + split) * rec_floats;
-
-  for (int e = tid; e < outputs; e += kThreads) {
-    const int h = e / kHeadDim;
-    const int d = e - h * kHeadDim;
-    const float M = tail->head_m[h], L = tail->head_l[h];
-    const float gv = single ? gate_value<T>(p, b, int64_t(kvh) * G + h, d) : 0.0f;
-    float num = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) num += red[red_index(w, h, d)];
-    if (single) {
-      store_out_g<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L, gv);
-    } else {
-      my_rec[e] = num;
-      if (d == 0) {
-        my_rec[outputs + h] = M;
-        my_rec[outputs + G + h] = L;
+  for (int j = 0; j < kPerThread; ++j) {
+    const int e = ctid + j * kNT;
+    if (e < outputs) {
+      const int h = e / kHeadDim;
+      const int d = e - h * kHeadDim;
+      float num = 0.0f;
+#pragma unroll
+      for (int g = 0; g < kWG; ++g) {
+        const float* rg = reinterpret_cast<const float*>(smem + g * PageFormat<kBits>::kWgBytes);
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) num += rg[red_index(w, h, d)];
+      }
+      const float M = tail_of(0)->head_m[h], L = tail_of(0)->head_l[h];
+      if (single) {
+        store_out_g<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L, gv[j]);
+      } else {
+        my_rec[e] = num;
+        if (d == 0) {
+          my_rec[outputs + h] = M;
+          my_rec[outputs + G + h] = L;
+        }
       }
     }
   }
   if (single || p.defer_merge) return;
 
-  // ---- split-KV merge by the last CTA of this (sequence, KV head)
-  merge_splits_last_cta<T, kThreads>(p, b, kvh, nsplit_b, tid, reinterpret_cast<float*>(codes), &tail->is_last, 1);
+  // ---- split-KV merge by the last CTA of this (sequence, KV head); its scratch is group
+  // 0's reduction buffer, free once every thread is past the loop above (the helper's first
+  // barrier)
+  merge_splits_last_cta<T, kNT>(p, b, kvh, nsplit_b, ctid, reinterpret_cast<float*>(smem), &tail_of(0)->is_last,
+                                1 + kWG);
 }
 
 // ---- split-KV merge for many splits: one CTA per (sequence x KV head, query head),
@@ -838,6 +865,7 @@ int decode_attn_impl(
                               : (group > 4 ? decode_attn_kernel<__half, true, 4> : decode_attn_kernel<__half, false, 4>);
   }
   const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
+  const int threads = (bits == 8 ? PageFormat<8>::kWG : PageFormat<4>::kWG) * kThreads;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
 
   // Split heuristic: as many KV ranges per (sequence, KV head) as fill one wave of
@@ -845,7 +873,7 @@ int decode_attn_impl(
   const int64_t units = batch * num_kv_heads;
   int splits = num_splits;
   if (splits <= 0) {
-    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), kThreads, smem_bytes);
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), threads, smem_bytes);
     // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
     splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
                                    std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
@@ -902,7 +930,7 @@ int decode_attn_impl(
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  launch_plain(kernel, grid, dim3(kThreads), smem_bytes, s, tmap, p);
+  launch_plain(kernel, grid, dim3(threads), smem_bytes, s, tmap, p);
   if (p.defer_merge) {
     const dim3 mgrid((unsigned)units, (unsigned)group);
     if (dtype == OQ_BF16) {

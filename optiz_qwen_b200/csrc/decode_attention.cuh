@@ -105,13 +105,13 @@ __device__ void merge_splits_last_cta(const AttnParams& p, int64_t b, int kvh, i
   const int outputs = G * kHeadDim;
   const int64_t unit = b * p.num_kv_heads + kvh;
   const int rec_floats = G * (kHeadDim + 2);
-  constexpr int kMaxPer = kMaxGroup * kHeadDim / kNT;
-  const int per = outputs / kNT;
+  // this thread's outputs: e = tid + j * kNT < outputs (kNT need not divide them)
+  constexpr int kMaxPer = (kMaxGroup * kHeadDim + kNT - 1) / kNT;
   float gv[kMaxPer];  // gate elements of this thread's outputs, in flight across the atomic
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) {
     const int e = tid + j * kNT;
-    gv[j] = j < per ? gate_value<T>(p, b, int64_t(kvh) * G + e / kHeadDim, e % kHeadDim) : 0.0f;
+    gv[j] = e < outputs ? gate_value<T>(p, b, int64_t(kvh) * G + e / kHeadDim, e % kHeadDim) : 0.0f;
   }
   __threadfence();
   named_bar_sync(bar_id, kNT);
@@ -158,16 +158,14 @@ __device__ void merge_splits_last_cta(const AttnParams& p, int64_t b, int kvh, i
     const float* rec = recs + s * rec_floats;
 #pragma unroll
     for (int j = 0; j < kMaxPer; ++j) {
-      if (j < per) {
-        const int e = tid + j * kNT;
-        num[j] = fmaf(wm[s * G + e / kHeadDim], __ldcg(rec + e), num[j]);
-      }
+      const int e = tid + j * kNT;
+      if (e < outputs) num[j] = fmaf(wm[s * G + e / kHeadDim], __ldcg(rec + e), num[j]);
     }
   }
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) {
-    if (j < per) {
-      const int e = tid + j * kNT;
+    const int e = tid + j * kNT;
+    if (e < outputs) {
       const int h = e / kHeadDim;
       const float L = head_l[h];
       store_out_g<T>(p, b, int64_t(kvh) * G + h, e - h * kHeadDim, L > 0.0f ? num[j] / L : 0.0f, head_m[h], L,
