@@ -9,7 +9,10 @@
 // launch in each direction, however many tokens the launch steps through:
 //   S *= exp(g);  kv = S^T k;  delta = beta (v - kv);  S += k delta^T;  o = S^T q.
 // Column sums over the 128 state rows are reduced with warp shuffles and a
-// 4-warp shared-memory step.
+// 4-warp shared-memory step.  The plain step with a given initial state (the decode
+// step) keeps the slice in shared memory instead (gdn_smem_kernel below), which lets twice
+// as many slices be in flight per SM.  The fused conv / norm variants
+// and the zero-initial-state case hold the slice in registers.
 //
 // Optional gated RMSNorm epilogue: the GDN layer's Qwen3_5RMSNormGated(o, z)
 // (modeling_qwen3_5.py:175-190, call site :527-529) over each head's 128 outputs.  The
@@ -17,6 +20,7 @@
 // on a per-(sequence, head) counter; the last to arrive reads the head's outputs back
 // (from L2) and rewrites them normalised.  No CTA waits for another (a cluster-wide
 // exchange measured ~8 us slower per launch on B200).
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -56,6 +60,7 @@ struct GdnParams {
   const void* norm_w;  // [Dv] in T
   float norm_eps;
   int* norm_counters;  // [B * H] zeroed; every launch leaves them zero
+  int32_t* status_word;  // OQ_DEV_* bits of the shared-memory kernel's bounded wait (may be null)
 };
 
 constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
@@ -280,6 +285,190 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
   }
 }
 
+// ---- Shared-memory form of the plain step (no fused conv or norm; an initial state is
+// given): one CTA per (sequence, head, 32-column slice) as above, but the slice lives in
+// shared memory instead of registers.  One TMA copy brings it in; phase 1 reads it
+// (decayed on the fly) for kv, phase 2 reads it again, applies the decay and the rank-1
+// update and writes it back for the next token; the final values go straight to global
+// memory.  Without 32 state floats per thread the CTA needs about half the registers, so
+// twice as many slices are in flight per SM.  The arithmetic is that of
+// gdn_recurrent_kernel, operation for operation (the decay product is recomputed in
+// phase 2 with the same rounding).
+constexpr int kSliceFloats = kDk * kCols;  // 16 KB
+constexpr size_t kSmemSlice = size_t(kSliceFloats) * 4 + 128;
+
+// Bounded wait on a copy's mbarrier (sleeping in try_wait, ~2 s in all); false if it ran out.
+__device__ __forceinline__ bool wait_bar_bounded(uint64_t* bar, uint32_t parity) {
+  for (int i = 0; i < 100000; ++i) {
+    if (mbar_try_wait_suspend(bar, parity, 20000)) return true;
+  }
+  return false;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) gdn_smem_kernel(const __grid_constant__ CUtensorMap tmap, GdnParams p) {
+  extern __shared__ uint8_t slice_raw[];
+  float* sl = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(slice_raw) + 127) & ~uintptr_t(127));
+  __shared__ uint64_t full;
+  __shared__ float q_s[kDk], k_s[kDk], v_s[kCols];
+  __shared__ float red_kv[4][kCols], red_o[4][kCols];
+  __shared__ float norm_q[4], norm_k[4];
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int cg = lane & 7;                // column group: columns 4cg .. 4cg+3 of the slice
+  const int rg = (lane >> 3) + 4 * warp;  // row group: rows rg + 16 i
+  const int v0 = blockIdx.x * kCols;
+  const int64_t h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t H = p.num_heads;
+
+  if (tid == 0) {
+    mbar_init(&full, 1);
+    fence_mbar_init();
+  }
+  // The state is the dominant traffic.  With prefetch_state the caller guarantees no
+  // kernel still running ahead of this one writes it, so its copy goes out before the
+  // dependency wait and overlaps the previous kernel's tail.
+  if (!p.prefetch_state) pdl_wait();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&full, kSliceFloats * 4);
+    tma_load_2d(sl, &tmap, v0, int32_t((b * H + h) * kDk), &full);
+  }
+  if (p.prefetch_state) pdl_wait();
+  pdl_allow_next();
+
+  // this thread's elements: rows rg + 16 i, columns 4cg .. 4cg+3 of the slice
+  auto elem = [&](int i) { return reinterpret_cast<float4*>(sl + (rg + 16 * i) * kCols + 4 * cg); };
+  bool landed = false;  // the copy is waited for once, after the first token's inputs are loaded
+
+  for (int64_t t = 0; t < p.seq_len; ++t) {
+    const T* qrow = static_cast<const T*>(p.q) + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+    const T* krow = static_cast<const T*>(p.k) + b * p.ks[0] + t * p.ks[1] + h * p.ks[2];
+    const T* vrow = static_cast<const T*>(p.v) + b * p.vs[0] + t * p.vs[1] + h * p.vs[2];
+    const float qv = to_float<T>(qrow[tid]);
+    const float kvv = to_float<T>(krow[tid]);
+    if (tid < kCols) v_s[tid] = to_float<T>(vrow[v0 + tid]);
+    q_s[tid] = qv;
+    k_s[tid] = kvv;
+    if (p.l2norm) {
+      float sq = qv * qv, sk = kvv * kvv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      }
+      if (lane == 0) {
+        norm_q[warp] = sq;
+        norm_k[warp] = sk;
+      }
+    }
+    const int64_t gi = (b * p.seq_len + t) * H + h;
+    const float gt = load_as_float(p.g, p.g_dtype, gi);
+    const float bt = load_as_float(p.beta, p.beta_dtype, gi);
+    if (!landed) {
+      const bool ok = wait_bar_bounded(&full, 0);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) report(p.status_word, OQ_DEV_TIMEOUT);
+        return;  // (a copy that has not landed in ~2 s will not; nothing else is in flight)
+      }
+      landed = true;
+    } else {
+      __syncthreads();
+    }
+
+    float inv_q = 1.0f, inv_k = 1.0f;
+    if (p.l2norm) {
+      // l2norm: x * rsqrt(sum(x*x) + 1e-6)  (modeling_qwen3_5.py:228-231)
+      inv_q = 1.0f / sqrtf((norm_q[0] + norm_q[1]) + (norm_q[2] + norm_q[3]) + 1e-6f);
+      inv_k = 1.0f / sqrtf((norm_k[0] + norm_k[1]) + (norm_k[2] + norm_k[3]) + 1e-6f);
+    }
+    const float decay = expf(gt);
+
+    // phase 1: partial kv = sum_rows (S * exp(g)) * k
+    float kv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float kr[kRowsPerThread];
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      kr[i] = __fmul_rn(k_s[rg + 16 * i], inv_k);
+      const float4 x = *elem(i);
+      kv[0] = fmaf(__fmul_rn(x.x, decay), kr[i], kv[0]);
+      kv[1] = fmaf(__fmul_rn(x.y, decay), kr[i], kv[1]);
+      kv[2] = fmaf(__fmul_rn(x.z, decay), kr[i], kv[2]);
+      kv[3] = fmaf(__fmul_rn(x.w, decay), kr[i], kv[3]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], 8);
+      kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], 16);
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red_kv[warp][4 * cg + j] = kv[j];
+    }
+    __syncthreads();
+
+    // phase 2: delta = beta (v - kv); S = S exp(g) + k delta^T; partial o = sum_rows S * q
+    float delta[4], o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = 4 * cg + j;
+      const float kvs = (red_kv[0][col] + red_kv[1][col]) + (red_kv[2][col] + red_kv[3][col]);
+      delta[j] = __fmul_rn(__fsub_rn(v_s[col], kvs), bt);
+    }
+    const bool last = t + 1 == p.seq_len;
+    const int64_t state_off = ((b * H + h) * kDk) * kDv + v0 + 4 * cg;
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+      const float qr = __fmul_rn(__fmul_rn(q_s[rg + 16 * i], inv_q), p.scale);
+      float4 x = *elem(i);
+      x.x = fmaf(kr[i], delta[0], __fmul_rn(x.x, decay));
+      x.y = fmaf(kr[i], delta[1], __fmul_rn(x.y, decay));
+      x.z = fmaf(kr[i], delta[2], __fmul_rn(x.z, decay));
+      x.w = fmaf(kr[i], delta[3], __fmul_rn(x.w, decay));
+      o[0] = fmaf(x.x, qr, o[0]);
+      o[1] = fmaf(x.y, qr, o[1]);
+      o[2] = fmaf(x.z, qr, o[2]);
+      o[3] = fmaf(x.w, qr, o[3]);
+      if (last) {
+        if (p.s_out != nullptr) *reinterpret_cast<float4*>(p.s_out + state_off + int64_t(rg + 16 * i) * kDv) = x;
+      } else {
+        *elem(i) = x;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o[j] += __shfl_xor_sync(0xffffffffu, o[j], 8);
+      o[j] += __shfl_xor_sync(0xffffffffu, o[j], 16);
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red_o[warp][4 * cg + j] = o[j];
+    }
+    __syncthreads();
+    if (tid < kCols) {
+      const float ov = (red_o[0][tid] + red_o[1][tid]) + (red_o[2][tid] + red_o[3][tid]);
+      static_cast<T*>(p.out)[((b * p.seq_len + t) * H + h) * kDv + v0 + tid] = from_float<T>(ov);
+    }
+  }
+  if (p.seq_len == 0) {
+    // no token: the state passes through unchanged
+    const bool ok = wait_bar_bounded(&full, 0);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) report(p.status_word, OQ_DEV_TIMEOUT);
+      return;
+    }
+    if (p.s_out != nullptr) {
+      const int64_t state_off = ((b * H + h) * kDk) * kDv + v0 + 4 * cg;
+#pragma unroll
+      for (int i = 0; i < kRowsPerThread; ++i) {
+        *reinterpret_cast<float4*>(p.s_out + state_off + int64_t(rg + 16 * i) * kDv) = *elem(i);
+      }
+    }
+  }
+}
+
 // Early (programmatic) launch only when the caller allows the state prefetch.
 void launch_gdn(void (*kernel)(GdnParams), dim3 grid, cudaStream_t s, const GdnParams& p) {
   if (p.prefetch_state) {
@@ -353,6 +542,36 @@ void set_norm(GdnParams& p, const NormArgs* norm) {
   p.norm_counters = norm ? norm->counters : nullptr;
 }
 
+// 2-D map over the fp32 state [B * H * 128 rows, 128 columns]: box = one 32-column slice
+// of a head's 128 rows (16 KB, no swizzle).
+int encode_state_map(CUtensorMap* map, const float* state, int64_t rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr) return fail(OQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {cuuint64_t(kDv), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(kDv) * 4};
+  const cuuint32_t box[2] = {cuuint32_t(kCols), cuuint32_t(kDk)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(state), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return fail(OQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(res));
+  return OQ_OK;
+}
+
+template <typename T>
+int launch_smem(const GdnParams& p, int64_t batch, cudaStream_t s) {
+  CUtensorMap tmap;
+  if (int st = encode_state_map(&tmap, p.s_in, batch * p.num_heads * kDk); st != OQ_OK) return st;
+  cudaFuncSetAttribute(gdn_smem_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemSlice));
+  const dim3 grid(unsigned(kDv / kCols), unsigned(p.num_heads), unsigned(batch));
+  if (p.prefetch_state) {
+    launch_pdl(gdn_smem_kernel<T>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
+  } else {
+    launch_plain(gdn_smem_kernel<T>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
+  }
+  return OQ_OK;
+}
+
 int gdn_recurrent_impl(
     const void* q, const void* k, const void* v, int qkv_dtype,
     int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
@@ -397,8 +616,19 @@ int gdn_recurrent_impl(
   p.l2norm = use_qk_l2norm;
   p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
   set_norm(p, norm);
-  dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (norm == nullptr && initial_state != nullptr && batch * num_heads * kDk < (int64_t(1) << 31)) {
+    // the plain step keeps the state slice in shared memory (the decode step's form)
+    int st = OQ_OK;
+    switch (qkv_dtype) {
+      case OQ_F32: st = launch_smem<float>(p, batch, s); break;
+      case OQ_F16: st = launch_smem<__half>(p, batch, s); break;
+      default: st = launch_smem<__nv_bfloat16>(p, batch, s); break;
+    }
+    if (st != OQ_OK) return st;
+    return check_launch("gdn_recurrent");
+  }
+  dim3 grid((unsigned)(kDv / kCols), (unsigned)num_heads, (unsigned)batch);
   launch_gdn(gdn_kernel_for<false>(qkv_dtype, norm != nullptr), grid, s, p);
   return check_launch("gdn_recurrent");
 }
