@@ -156,6 +156,7 @@ class HybridDecodeStack:
                 self.gdn.append(layer)
         self._alloc_io()
         self.graph: torch.cuda.CUDAGraph | None = None
+        self.io_graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(self.device)
 
     @property
@@ -226,6 +227,16 @@ class HybridDecodeStack:
                 out_specs += [(("gdn", i, "out"), shp)]
         n_in = sum(math.prod(shp) for _, shp in in_specs)
         n_out = sum(math.prod(shp) for _, shp in out_specs)
+        # each layer's inputs and outputs are contiguous ranges of the flat buffers (the
+        # host-facing step copies them layer by layer)
+        self._in_range: dict = {}
+        self._out_range: dict = {}
+        for specs, ranges in ((in_specs, self._in_range), (out_specs, self._out_range)):
+            off = 0
+            for (kind, i, _), shp in specs:
+                lo, hi = ranges.get((kind, i), (off, off))
+                ranges[(kind, i)] = (lo, off + math.prod(shp))
+                off += math.prod(shp)
         # g stays fp32 (the module computes it in fp32): a separate flat buffer
         n_g = len(self.gdn) * b * s.gdn_heads
         self.in_dev = torch.empty(n_in, dtype=self.dtype, device=self.device)
@@ -260,11 +271,15 @@ class HybridDecodeStack:
         self.in_host.copy_(self.in_dev)
 
     # ------------------------------------------------------------------ the step
-    def step_device(self, kinds=("attn", "gdn", "append")) -> None:
+    def step_device(self, kinds=("attn", "gdn", "append"), before=None, after=None) -> None:
+        """Enqueue one step's launches; `before` / `after` (optional) are called with each
+        layer's (kind, index) around its launches."""
         s = self.shape
         scaling = s.head_dim ** -0.5
         prev = None  # (kind, index) of the previous launch in this step
         for kind, i in self.order:
+            if before is not None:
+                before((kind, i))
             if kind == "attn":
                 layer = self.attn[i]
                 p = layer.paged
@@ -303,6 +318,8 @@ class HybridDecodeStack:
                 if layer.z is not None:
                     cabi.rmsnorm_gated(layer.out, layer.z, layer.norm_w, 1e-6, out=layer.out)
                 prev = ("gdn", i)
+            if after is not None:
+                after((kind, i))
 
     def capture(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
         """Capture one step's launches in a CUDA graph (after one eager warm-up step)."""
@@ -315,15 +332,60 @@ class HybridDecodeStack:
             self.step_device(kinds)
         return graph
 
+    def capture_io(self) -> torch.cuda.CUDAGraph:
+        """The host-facing step as one graph with its transfers: a copy stream brings each
+        layer's inputs (and g) from the pinned host buffers in layer order, each layer's
+        launches wait for their own inputs only, and a second copy stream returns each
+        layer's outputs as soon as the layer is done.  The copies of later layers run under
+        the kernels of earlier ones."""
+        dev = self.device
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):  # eager warm-up of the launches
+            self.step_device()
+        torch.cuda.current_stream(dev).wait_stream(self.stream)
+        copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        b, heads = self.shape.batch, self.shape.gdn_heads
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            main = self.stream
+            fork = torch.cuda.Event()
+            fork.record(main)
+            copy_in.wait_event(fork)
+            copy_out.wait_event(fork)
+            ready = {}
+            with torch.cuda.stream(copy_in):
+                for key in self.order:
+                    lo, hi = self._in_range[key]
+                    self.in_dev[lo:hi].copy_(self.in_host[lo:hi], non_blocking=True)
+                    if key[0] == "gdn":
+                        g0 = key[1] * b * heads
+                        self.g_dev[g0:g0 + b * heads].copy_(self.g_host[g0:g0 + b * heads], non_blocking=True)
+                    ready[key] = torch.cuda.Event()
+                    ready[key].record(copy_in)
+
+            def before(key):
+                main.wait_event(ready[key])
+
+            def after(key):
+                done = torch.cuda.Event()
+                done.record(main)
+                copy_out.wait_event(done)
+                with torch.cuda.stream(copy_out):
+                    lo, hi = self._out_range[key]
+                    self.out_host[lo:hi].copy_(self.out_dev[lo:hi], non_blocking=True)
+
+            self.step_device(before=before, after=after)
+            main.wait_stream(copy_in)
+            main.wait_stream(copy_out)
+        return graph
+
     def step(self) -> torch.Tensor:
-        """Host-facing step: pinned inputs -> device, graph replay, outputs -> pinned host buffer."""
-        if self.graph is None:
-            self.graph = self.capture()
-        cur = torch.cuda.current_stream(self.device)
-        self.in_dev.copy_(self.in_host, non_blocking=True)
-        self.g_dev.copy_(self.g_host, non_blocking=True)
-        self.graph.replay()
-        self.out_host.copy_(self.out_dev, non_blocking=True)
+        """Host-facing step: pinned inputs -> device, the step's kernels, outputs -> the pinned
+        host buffer, as one graph replay on the current stream (transfers overlap the kernels
+        layer by layer).  The caller synchronises before reading the returned buffer."""
+        if self.io_graph is None:
+            self.io_graph = self.capture_io()
+        self.io_graph.replay()
         return self.out_host
 
     # ------------------------------------------------------------------ accounting

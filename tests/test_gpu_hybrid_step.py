@@ -139,3 +139,36 @@ def test_graph_step_with_epilogues(conv):
         cache.kv_meta[...] = p.pool.kv_meta.cpu().numpy()
         ref, _ = oracle_attention(cache, f(layer.q), shape.head_dim ** -0.5)
         assert_attn_close(f(layer.out), ep.sigmoid_gate(ref, f(layer.gate), rnd=kq.round_bf16))
+
+
+def test_host_facing_step_copies_overlap_and_match_the_device_graph():
+    """`step()` (one graph: per-layer input copies from pinned host memory, the kernels, per-layer
+    output copies back) gives the device-only graph's outputs and states bit for bit; the device
+    input buffer and the host output buffer are cleared first, so only the step's own copies can
+    produce the match."""
+    from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
+
+    shape = HybridShape(batch=3, context=[70, 130, 5], num_layers=8)
+    stack = HybridDecodeStack(shape, device="cuda", seed=5)
+    stack.fill_inputs()
+    states0 = [layer.state.clone() for layer in stack.gdn]
+    graph = stack.capture()
+    for layer, s0 in zip(stack.gdn, states0):
+        layer.state.copy_(s0)
+    graph.replay()
+    torch.cuda.synchronize()
+    want_out = stack.out_dev.clone()
+    want_states = [layer.state.clone() for layer in stack.gdn]
+
+    stack.io_graph = stack.capture_io()  # (runs one eager step first)
+    for layer, s0 in zip(stack.gdn, states0):
+        layer.state.copy_(s0)
+    stack.in_dev.zero_()
+    stack.g_dev.zero_()
+    stack.out_host.zero_()
+    torch.cuda.synchronize()
+    got = stack.step()
+    torch.cuda.synchronize()
+    assert torch.equal(got.to("cuda"), want_out)
+    for layer, s in zip(stack.gdn, want_states):
+        assert torch.equal(layer.state, s)
