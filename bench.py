@@ -575,9 +575,13 @@ def run_prefill(args):
     dq = [_prefill_inputs(b, 1, h, d, gen, device) for _ in range(tail)]
     dout = torch.empty((b, 1, h, d), dtype=torch.bfloat16, device=device)
 
+    # the two-phase form's per-chunk workspace, shared by the layers (they run in order)
+    chunk_ws = torch.empty(cabi.gdn_chunk_workspace_bytes(b, t, h), dtype=torch.uint8, device=device)
+
     def prefill():
         for (q, k, v, g, beta), si, so in zip(ins, s0, states):
-            cabi.gdn_chunk_fwd(q, k, v, g, beta, initial_state=si, final_state=so, out=out, use_qk_l2norm=True)
+            cabi.gdn_chunk_fwd(q, k, v, g, beta, initial_state=si, final_state=so, out=out, use_qk_l2norm=True,
+                               workspace=chunk_ws)
 
     def decode_tail():
         for step, (q, k, v, g, beta) in enumerate(dq):
@@ -660,7 +664,7 @@ def run_prefill(args):
         "e2e": {"value": round(b * t * world * 1000.0 / e2e_ms / layers, 1), "unit": "prefill tokens/s",
                 "h2d_bytes_per_step": h2d * layers, "d2h_bytes_per_step": d2h * layers,
                 "note": "one layer through chunk_gated_delta_rule with pinned host buffers, scaled to 18 layers"},
-        "gpu_launches": layers * steps,
+        "gpu_launches": 2 * layers * steps,  # per layer: the per-chunk factors, then the state walk
         "roofline": {"bound": "hbm", "kernel": "gdn_chunk", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(gbs / hbm_peak, 4), "traffic": dram_traffic("gdn_chunk"), "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": bytes_layer, "us_per_launch": round(layer_us, 1),

@@ -385,6 +385,27 @@ int oq_gdn_chunk_fwd(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int64_t chunk_size, int32_t* device_status, void* stream);
 
+/* The same chunked recurrence in two launches (the same reference hook; same arguments
+ * and results as oq_gdn_chunk_fwd, to the last bit).  The first launch does, for all
+ * chunks of all (sequence, head) at once, the work that does not depend on the state
+ * (norms, decays, the Gram matrix, the triangular solve, the P and W / U factors) and
+ * writes it to `workspace`.  The second walks each (sequence, head)'s chunks in order
+ * and only does the state products.  workspace: oq_gdn_chunk_workspace_bytes(batch,
+ * seq_len, num_heads) bytes (about 49 KB per 64-token chunk and head), 128-byte aligned,
+ * no initialisation needed; launches that share it must be ordered on one stream. */
+size_t oq_gdn_chunk_workspace_bytes(int64_t batch, int64_t seq_len, int64_t num_heads);
+
+int oq_gdn_chunk_fwd_ws(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int64_t chunk_size, void* workspace, size_t workspace_bytes,
+    int32_t* device_status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

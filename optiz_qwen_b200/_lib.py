@@ -68,6 +68,9 @@ SIGNATURES = {
                                f32, i32, i32, p]),
     "oq_gdn_chunk_fwd": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i64, p, p]),
+    "oq_gdn_chunk_workspace_bytes": (sz, [i64, i64, i64]),
+    "oq_gdn_chunk_fwd_ws": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                  p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i64, p, sz, p, p]),
 }
 
 _lib = None

@@ -419,11 +419,16 @@ def rmsnorm_gated(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: f
 def gdn_chunk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, *,
                   scale: float | None = None, initial_state: torch.Tensor | None = None,
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                  use_qk_l2norm: bool = False, device_status: torch.Tensor | None = None) -> torch.Tensor:
+                  use_qk_l2norm: bool = False, device_status: torch.Tensor | None = None,
+                  two_phase: bool = True, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Chunked gated delta rule (prefill) on the tensor cores; same contract as :func:`gdn_recurrent`.
 
     q, k, v must be bf16 with unit stride along the head dim and 16-byte-multiple
-    strides (a slice of a fused projection qualifies); Dk = Dv = 128.
+    strides (a slice of a fused projection qualifies); Dk = Dv = 128.  ``two_phase``
+    (default) runs ``oq_gdn_chunk_fwd_ws``: the state-independent per-chunk work for all
+    chunks in one parallel launch, then the sequential state walk; ``workspace`` (uint8,
+    :func:`gdn_chunk_workspace_bytes` bytes) is allocated when not given.  With
+    ``two_phase=False`` one launch does both (``oq_gdn_chunk_fwd``).  Results are identical.
     """
     require_cuda(q, k, v, g, beta, initial_state, final_state)
     if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
@@ -445,13 +450,27 @@ def gdn_chunk_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
     elif out.dtype != torch.bfloat16 or tuple(out.shape) != (bsz, t, h, dv) or not out.is_contiguous():
         raise ValueError("out must be contiguous bf16 [B, T, H, Dv]")
     scale = dk ** -0.5 if scale is None else float(scale)
-    call("oq_gdn_chunk_fwd", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
-         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
-         v.stride(0), v.stride(1), v.stride(2),
-         ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
-         ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
-         CHUNK_SIZE, ptr(device_status), stream_ptr(q.device))
+    args = (ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
+            q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+            v.stride(0), v.stride(1), v.stride(2),
+            ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
+            ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
+            CHUNK_SIZE)
+    if two_phase and t > 0:
+        need = gdn_chunk_workspace_bytes(bsz, t, h)
+        if workspace is None:
+            workspace = torch.empty(max(need, 128), dtype=torch.uint8, device=q.device)
+        require_cuda(workspace)
+        call("oq_gdn_chunk_fwd_ws", *args, ptr(workspace), workspace.numel() * workspace.element_size(),
+             ptr(device_status), stream_ptr(q.device))
+    else:
+        call("oq_gdn_chunk_fwd", *args, ptr(device_status), stream_ptr(q.device))
     return out
+
+
+def gdn_chunk_workspace_bytes(batch: int, seq_len: int, num_heads: int) -> int:
+    """Bytes of the two-phase chunked form's workspace (about 49 KB per 64-token chunk and head)."""
+    return int(_lib.load().oq_gdn_chunk_workspace_bytes(batch, seq_len, num_heads))
 
 
 def pages_for(length: int, page_size: int = PAGE_SIZE) -> int:

@@ -93,8 +93,16 @@ struct Bars {
   uint64_t v;
   uint64_t mma;
   uint64_t drain;
+  uint64_t ab;  // two-phase form: a chunk's Ar / Ab tiles and scalars
+  uint64_t pp;  // two-phase form: its P tiles
   uint32_t tmem_base;
 };
+
+// Workspace image of one (sequence, head, chunk) in the two-phase form (see below).
+constexpr uint32_t kImgP = 4 * kTile;                   // P hi | P lo after the Ar / Ab tiles
+constexpr uint32_t kImgScal = 6 * kTile;                // sfac[64], cq[64], gamma, padding
+constexpr uint32_t kImgScalBytes = 160 * 4;
+constexpr uint32_t kImgBytes = 6 * kTile + 1024;        // per (sequence, head, chunk)
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) {
   for (int i = 0; i < kWaitPolls; ++i) {
@@ -151,9 +159,12 @@ __device__ __forceinline__ float row_sumsq(const uint8_t* lo_half, const uint8_t
   return (ss[0] + ss[1]) + (ss[2] + ss[3]);
 }
 
+// kPre: the two-phase form's second phase, reading the state-independent per-chunk tiles
+// from `images` (written by gdn_chunk_prep_kernel) instead of computing them.
+template <bool kPre>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_chunk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, ChunkParams p) {
+                     const __grid_constant__ CUtensorMap tm_v, ChunkParams p, const uint8_t* images) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sa = smem_addr(sm);
@@ -183,6 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->v, 1);
     mbar_init(&bars->mma, 1);
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->ab, 1);
+    mbar_init(&bars->pp, 1);
     fence_mbar_init();
   }
   __syncwarp();
@@ -220,9 +233,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ++v_issued;
   };
+  int ab_issued = 0, ab_waited = 0, p_issued = 0, p_waited = 0;
+  auto img_of = [&](int cc) {
+    return images + ((int64_t(b) * H + h) * n_chunks + cc) * int64_t(kImgBytes);
+  };
+  // (thread 0; the regions it refills were last touched by the generic proxy or the MMAs,
+  // both finished at the block barrier before each call)
+  auto issue_ab = [&](int cc) {
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars->ab, 4 * kTile + kImgScalBytes);
+      bulk_load(sm + kOffW, img_of(cc), 4 * kTile, &bars->ab);
+      bulk_load(tok(cc & 1, 5), img_of(cc) + kImgScal, kImgScalBytes, &bars->ab);
+    }
+    ++ab_issued;
+  };
+  auto issue_p = [&](int cc) {
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars->pp, 2 * kTile);
+      bulk_load(sm + kOffP, img_of(cc) + kImgP, 2 * kTile, &bars->pp);
+    }
+    ++p_issued;
+  };
   if (n_chunks > 0) {
     issue_kq(0, 0);
     issue_v(0);
+    if constexpr (kPre) {
+      issue_ab(0);
+      issue_p(0);
+    }
   }
   if (n_chunks > 1) issue_kq(1, 1);
   __syncwarp();  // tcgen05.ld / st below are warp-collective
@@ -320,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
 
-  if (n_chunks > 0) {
+  if (!kPre && n_chunks > 0) {
     if (wait_all(&bars->kq[0], 0)) {
       aborted = true;
     } else {
@@ -350,7 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* s_rfac = tok(st, 7);
     const float* s_gcl = tok(st, 8);
     const bool last = c + 1 == n_chunks;
-    float g_next, b_next;
+    float g_next = 0.0f, b_next = 0.0f;
+    if constexpr (kPre) {
+      // this chunk's K / Q tiles, and its Ar / Ab tiles and scalars from the first phase
+      if (wait_all(&bars->kq[st], kq_waited[st] & 1)) { aborted = true; break; }
+      ++kq_waited[st];
+      if (wait_all(&bars->ab, ab_waited & 1)) { aborted = true; break; }
+      ++ab_waited;
+    } else {
     load_gb(c + 1, g_next, b_next);
 
     // (G of this chunk and its per-token scalars are ready.)
@@ -498,6 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_proxy_async_smem();
     __syncthreads();
+    }  // (kPre: copied in by the first phase)
 
     // ---- W^T = K^T Ar^T (lanes = dk), U^T = V^T Ab^T (lanes = dv)
     if (wait_all(&bars->v, v_waited & 1)) { aborted = true; break; }
@@ -555,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     {
-      const float gamma = expf(s_gc[kC - 1]);
+      const float gamma = kPre ? tok(st, 7)[0] : expf(s_gc[kC - 1]);  // (the image holds e^{gc_last} there)
 #pragma unroll 1
       for (int q4 = 2 * half; q4 < 2 * half + 2; ++q4) {
         float sv[32];
@@ -568,6 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     if (mma_done()) { aborted = true; break; }
+    if constexpr (kPre) {
+      if (!last) issue_ab(c + 1);  // the W tiles are consumed: the region takes the next chunk's tiles
+    }
 
     // ---- Vn^T = U^T - (WS)^T; Vs^T = Vn^T diag(sfac): split K-major tiles [l][t] over S^T's tiles
     {
@@ -592,6 +643,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- Vn^T P^T (3 products) and S^T += Vs^T K (2 products); then the next chunk's G, whose
     // per-token scalars are computed while the tensor cores run.
+    if constexpr (kPre) {
+      if (wait_all(&bars->pp, p_waited & 1)) { aborted = true; break; }
+      ++p_waited;
+    }
     if (tid == 0) {
       tc_fence_after();
       const uint32_t vnh = sa + kOffS, vnl = vnh + 16384, vsh = vnh + 32768, vsl = vnh + 49152;
@@ -612,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_bf16(tmem + kColS, a_sl, b_k, kIdescN128BMn, true);
       }
     }
-    if (!last) {
+    if (!kPre && !last) {
       if (wait_all(&bars->kq[st ^ 1], kq_waited[st ^ 1] & 1)) {
         if (tid == 0) umma_commit(&bars->mma);
         aborted = true;
@@ -622,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tid == 0) issue_gram(c + 1);
     }
     if (tid == 0) umma_commit(&bars->mma);
-    if (!last) prep_scalars(c + 1, g_next, b_next);
+    if (!kPre && !last) prep_scalars(c + 1, g_next, b_next);
     if (mma_done()) { aborted = true; break; }
     if (c + 2 < n_chunks) issue_kq(c + 2, st);
     __syncwarp();
@@ -661,6 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPre) {
+      if (!last) issue_p(c + 1);  // the output staging in the P region has been read
+    }
   }
 
   pdl_allow_next();
@@ -673,6 +731,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (kq_waited[s] < kq_issued[s]) wait_bar(&bars->kq[s], (kq_waited[s]++) & 1);
     }
     while (v_waited < v_issued) wait_bar(&bars->v, (v_waited++) & 1);
+    while (ab_waited < ab_issued) wait_bar(&bars->ab, (ab_waited++) & 1);
+    while (p_waited < p_issued) wait_bar(&bars->pp, (p_waited++) & 1);
   } else if (p.s_out != nullptr) {
     tc_fence_after();
 #pragma unroll 1
@@ -686,6 +746,314 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------- two-phase form
+// Phase 1 (gdn_chunk_prep_kernel) does, for every chunk of every (sequence, head) at once,
+// the part of a chunk's work that does not depend on the state: the norms and decays, the
+// Gram matrix, N and P, X = (I - N)^-1 and the split Ar / Ab tiles.  It writes them to a
+// workspace as the exact shared-memory images phase 2 uses (per chunk: Ar hi | Ar lo |
+// Ab hi | Ab lo, then P hi | P lo, 8 KB each in the 128-byte swizzle, then sfac[64], cq[64],
+// e^{gc_last}).  Phase 2 (gdn_chunk_kernel<true>) walks the chunks of a (sequence, head) in
+// order as before, but copies those images in instead of computing them, so its per-chunk
+// chain keeps only the state products.  The arithmetic is the single-kernel form's.
+// phase-1 shared memory (1024-aligned base): the K / Q tiles of the chunk; once the Gram MMA
+// and the norms are done, X and the solve scratch reuse them
+constexpr uint32_t kP1OffX = 0;                         // [64][68] fp32
+constexpr uint32_t kP1OffT = 17408;                     // solve scratch, up to [32][36] fp32
+constexpr uint32_t kP1OffN = kKQBytes;                  // [64][65] fp32
+constexpr uint32_t kP1OffTok = kP1OffN + 16640;         // 9 per-token arrays of 64 floats
+constexpr uint32_t kP1OffBars = kP1OffTok + kTokArrays * kC * 4;
+constexpr uint32_t kP1Smem = kP1OffBars + 64 + 1024;
+constexpr uint32_t kP1TmemCols = 64;
+
+struct PrepBars {
+  uint64_t kq;
+  uint64_t mma;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kThreads)
+    gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          ChunkParams p, uint8_t* workspace) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sa = smem_addr(sm);
+  float* f_small = reinterpret_cast<float*>(sm + kP1OffTok);
+  auto tok = [&](int, int k) { return f_small + k * kC; };  // one buffer
+  float* s_T = reinterpret_cast<float*>(sm + kP1OffT);
+  float* s_N = reinterpret_cast<float*>(sm + kP1OffN);
+  float* s_X = reinterpret_cast<float*>(sm + kP1OffX);
+  PrepBars* bars = reinterpret_cast<PrepBars*>(sm + kP1OffBars);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 127;
+  const int half = tid >> 7;
+  const int c = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int H = p.num_heads;
+  const int64_t T = p.seq_len;
+  const int n_chunks = int((T + kC - 1) / kC);
+  uint8_t* img = workspace + ((int64_t(b) * H + h) * n_chunks + c) * int64_t(kImgBytes);
+
+  if (tid == 0) {
+    mbar_init(&bars->kq, 1);
+    mbar_init(&bars->mma, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, kP1TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+  pdl_wait();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars->kq, kKQBytes);
+    const int t0 = c * kC;
+    tma_load_4d(sm, &tm_k, 0, h, t0, b, &bars->kq);
+    tma_load_4d(sm + kTile, &tm_q, 0, h, t0, b, &bars->kq);
+    tma_load_4d(sm + 2 * kTile, &tm_k, 64, h, t0, b, &bars->kq);
+    tma_load_4d(sm + 3 * kTile, &tm_q, 64, h, t0, b, &bars->kq);
+  }
+  float gv = 0.0f, bv = 0.0f;
+  {
+    const int64_t t = int64_t(c) * kC + tid;
+    if (tid < kC && t < T) {
+      const int64_t gi = (int64_t(b) * T + t) * H + h;
+      gv = load_as_float(p.g, p.g_dtype, gi);
+      bv = load_as_float(p.beta, p.beta_dtype, gi);
+    }
+  }
+  bool issued_mma = false;
+  bool ok = wait_bar(&bars->kq, 0);
+  if (__syncthreads_or(!ok) == 0) {
+    // G = [K; Q] K^T (M = 128: 64 keys then 64 queries; N = 64 keys; K = d)
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = sa + (kk >> 2) * 2 * kTile + (kk & 3) * 32;
+        umma_bf16(tmem + kColG, smem_desc_sw128(off, 16, 1024), smem_desc_sw128(off, 16, 1024), kIdescN64, kk > 0);
+      }
+      umma_commit(&bars->mma);
+    }
+    issued_mma = true;
+    // per-token scalars: g, beta, inverse norms, in-chunk cumulative decay and the factors
+    const uint8_t* kqc = sm;
+    if (tid < kC) {
+      tok(0, 0)[tid] = gv;
+      tok(0, 2)[tid] = bv;
+      tok(0, 3)[tid] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kqc, kqc + 2 * kTile, tid) + 1e-6f) : 1.0f;
+    } else if (tid < 2 * kC) {
+      const int r = tid - kC;
+      tok(0, 4)[r] = p.l2norm ? 1.0f / sqrtf(row_sumsq(kqc + kTile, kqc + 3 * kTile, r) + 1e-6f) : 1.0f;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float a0 = tok(0, 0)[2 * tid], a1 = tok(0, 0)[2 * tid + 1];
+      float incl = a0 + a1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+      if (tid == 0) excl = 0.0f;
+      const float gc[2] = {excl + a0, (excl + a0) + a1};
+      const float gl = __shfl_sync(0xffffffffu, gc[1], 31);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * tid + e;
+        const float dk = tok(0, 3)[t];
+        tok(0, 1)[t] = gc[e];
+        tok(0, 8)[t] = gc[e] * 1.4426950408889634f;
+        tok(0, 5)[t] = dk * expf(gl - gc[e]);
+        tok(0, 6)[t] = p.scale * tok(0, 4)[t] * expf(gc[e]);
+        tok(0, 7)[t] = tok(0, 2)[t] * expf(gc[e]) * dk;
+      }
+    }
+    ok = wait_bar(&bars->mma, 0);
+    if (__syncthreads_or(!ok) == 0) {
+      tc_fence_after();
+      const float* s_gc = tok(0, 1);
+      const float* s_beta = tok(0, 2);
+      const float* s_dk = tok(0, 3);
+      const float* s_dq = tok(0, 4);
+      const float* s_rfac = tok(0, 7);
+      const float* s_gcl = tok(0, 8);
+      (void)s_gc;
+    // ---- rows of N (lanes 0..63) and P (lanes 64..127) from the Gram lanes; each thread
+    // takes 32 of the 64 columns
+    {
+      float gr[32];
+      tmem_ld32(lane_base + kColG + 32 * half, gr);
+      const int j0 = 32 * half;
+      if (lane < kC) {
+        const int i = lane;
+        const float fi = -s_beta[i] * s_dk[i];
+        const float gli = s_gcl[i];
+        float* nrow = s_N + i * kNStride + j0;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = j0 + jj;
+          nrow[jj] = j < i ? fi * s_dk[j] * gr[jj] * exp2f(gli - s_gcl[j]) : 0.0f;
+        }
+      } else {
+        const int i = lane - kC;
+        const float fi = p.scale * s_dq[i];
+        const float gli = s_gcl[i];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float pv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = j0 + 8 * cc + e;
+            pv[e] = j <= i ? fi * s_dk[j] * gr[8 * cc + e] * exp2f(gli - s_gcl[j]) : 0.0f;
+          }
+          store_split8(img + kImgP, img + kImgP + kTile, swz(i, 4 * half + cc), pv);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- X = (I - N)^-1 by doubling.  16x16 diagonal blocks by forward substitution
+    // (one column per thread), zeroing the blocks right of blocks 0 and 2 ...
+    if (tid < kC) {
+      const int o = 16 * (tid >> 4), jj = tid & 15;
+      float x[16];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) x[m] = m == jj ? 1.0f : 0.0f;
+#pragma unroll
+      for (int ii = 1; ii < 16; ++ii) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int m = 0; m < ii; ++m) acc = fmaf(s_N[(o + ii) * kNStride + o + m], x[m], acc);
+        if (ii > jj) x[ii] = acc;
+      }
+#pragma unroll
+      for (int ii = 0; ii < 16; ++ii) s_X[(o + ii) * kXStride + o + jj] = x[ii];
+      if ((o & 16) == 0) {
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) s_X[(o + ii) * kXStride + o + 16 + jj] = 0.0f;
+      }
+    }
+    __syncthreads();
+    // ... then the 32x32 diagonal blocks: X_10 = X_11 N_10 X_00 and X_32 = X_33 N_32 X_22
+    // (1x2 outputs per thread) ...
+    {
+      const int blk = tid >> 7, I = 16 * (1 + 2 * blk), J = 32 * blk;
+      const int r = (tid & 127) >> 3, c0 = (tid & 7) * 2;
+      float* tb = s_T + blk * 16 * kT2Stride;
+      float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float n = s_N[(I + r) * kNStride + J + m];
+        const float2 x = *reinterpret_cast<const float2*>(&s_X[(J + m) * kXStride + J + c0]);
+        a0 = fmaf(n, x.x, a0);
+        a1 = fmaf(n, x.y, a1);
+      }
+      *reinterpret_cast<float2*>(&tb[r * kT2Stride + c0]) = make_float2(a0, a1);
+      __syncthreads();
+      a0 = a1 = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float x = s_X[(I + r) * kXStride + I + m];
+        const float2 t = *reinterpret_cast<const float2*>(&tb[m * kT2Stride + c0]);
+        a0 = fmaf(x, t.x, a0);
+        a1 = fmaf(x, t.y, a1);
+      }
+      *reinterpret_cast<float2*>(&s_X[(I + r) * kXStride + J + c0]) = make_float2(a0, a1);
+    }
+    __syncthreads();
+    // ... and the lower-left 32x32 block: X[32:, :32] = X[32:, 32:] N[32:, :32] X[:32, :32]
+    // Warp w computes columns 4w..4w+3 of T = N[32:, :32] X[:32, :32] (lane = row; X[m][c] = 0
+    // for m < c), then rows 4w..4w+3 of X[32:, 32:] T (lane = column; X[32 + r][32 + m] = 0 for m > r).
+    {
+      const int c0 = 4 * warp, r = tid & 31;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+      for (int m = c0; m < 32; ++m) {
+        const float n = s_N[(32 + r) * kNStride + m];
+        const float4 x = *reinterpret_cast<const float4*>(&s_X[m * kXStride + c0]);
+        acc[0] = fmaf(n, x.x, acc[0]);
+        acc[1] = fmaf(n, x.y, acc[1]);
+        acc[2] = fmaf(n, x.z, acc[2]);
+        acc[3] = fmaf(n, x.w, acc[3]);
+      }
+      *reinterpret_cast<float4*>(&s_T[r * kT3Stride + c0]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      __syncthreads();
+      const int r0 = 4 * warp, col = tid & 31;
+      float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+      for (int m0 = 0; m0 < r0 + 4; m0 += 4) {
+        float tcol[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tcol[i] = s_T[(m0 + i) * kT3Stride + col];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float4 x = *reinterpret_cast<const float4*>(&s_X[(32 + r0 + a) * kXStride + 32 + m0]);
+          o[a] = fmaf(x.x, tcol[0], o[a]);
+          o[a] = fmaf(x.y, tcol[1], o[a]);
+          o[a] = fmaf(x.z, tcol[2], o[a]);
+          o[a] = fmaf(x.w, tcol[3], o[a]);
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) s_X[(32 + r0 + a) * kXStride + col] = o[a];
+    }
+    __syncthreads();
+
+    // ---- Ar = X diag(beta e^gc dk), Ab = X diag(beta): split K-major tiles [t][m] (over N)
+    {
+      const int t = tid >> 2, qq = tid & 3;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c8 = 2 * qq + cc;
+        float xr[8], ar[8], ab[8];
+        *reinterpret_cast<float4*>(xr) = *reinterpret_cast<const float4*>(&s_X[t * kXStride + 8 * c8]);
+        *reinterpret_cast<float4*>(xr + 4) = *reinterpret_cast<const float4*>(&s_X[t * kXStride + 8 * c8 + 4]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int m = 8 * c8 + e;
+          const float xv = m > t ? 0.0f : (m == t ? 1.0f : xr[e]);
+          ar[e] = xv * s_rfac[m];
+          ab[e] = xv * s_beta[m];
+        }
+        store_split8(img, img + kTile, swz(t, c8), ar);
+        store_split8(img + 2 * kTile, img + 3 * kTile, swz(t, c8), ab);
+      }
+    }
+
+
+      // the scalars phase 2 needs: sfac, cq and e^{gc_last}
+      float* scal = reinterpret_cast<float*>(img + kImgScal);
+      if (tid < kC) {
+        scal[tid] = tok(0, 5)[tid];
+      } else if (tid < 2 * kC) {
+        scal[tid] = tok(0, 6)[tid - kC];
+      } else if (tid == 2 * kC) {
+        scal[tid] = expf(tok(0, 1)[kC - 1]);
+      }
+    }
+  }
+  pdl_allow_next();
+  if (!ok) {
+    if (tid == 0) report(p.status, OQ_DEV_TIMEOUT);
+    // let the copy and the MMA land before shared and tensor memory go away
+    if (tid == 0) wait_bar(&bars->kq, 0);
+    if (issued_mma && tid == 0) wait_bar(&bars->mma, 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kP1TmemCols);
 }
 
 // 4-D map over a [B, T, H, 128] bf16 tensor: box = 64 head-dim elements x 1 head x 64 tokens x 1 sequence.
@@ -709,7 +1077,12 @@ bool stride_ok(int64_t s) { return s > 0 && (s * 2) % 16 == 0 && s * 2 < (int64_
 }  // namespace
 }  // namespace oq
 
-extern "C" int oq_gdn_chunk_fwd(
+namespace oq {
+namespace {
+
+// workspace == nullptr: the single-kernel form; otherwise the two-phase form with the
+// per-chunk images in `workspace` (gdn_chunk_workspace_bytes).
+int gdn_chunk_impl(
     const void* q, const void* k, const void* v, int qkv_dtype,
     int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
     int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
@@ -717,8 +1090,8 @@ extern "C" int oq_gdn_chunk_fwd(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, int64_t chunk_size, int32_t* device_status, void* stream) {
-  using namespace oq;
+    float scale, int use_qk_l2norm, int64_t chunk_size, void* workspace, size_t workspace_bytes,
+    int32_t* device_status, void* stream) {
   if (qkv_dtype != OQ_BF16) return fail(OQ_ERR_UNSUPPORTED, "gdn_chunk_fwd: q, k, v must be bf16");
   if (!valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) return fail(OQ_ERR_UNSUPPORTED, "gdn_chunk_fwd: unknown dtype");
   if (k_dim != kD || v_dim != kD) return fail(OQ_ERR_UNSUPPORTED, "gdn_chunk_fwd: k_dim = v_dim = 128 required");
@@ -750,15 +1123,32 @@ extern "C" int oq_gdn_chunk_fwd(
   } else {
     memset(maps, 0, sizeof(maps));
   }
-  static bool attr_set[64] = {};
+  const int64_t n_chunks = (seq_len + kC - 1) / kC;
+  const bool two_phase = workspace != nullptr;
+  if (two_phase) {
+    const size_t need = size_t(batch * num_heads * n_chunks) * kImgBytes;
+    if (workspace_bytes < need) {
+      return fail(OQ_ERR_WORKSPACE, "gdn_chunk_fwd: workspace of %zu bytes needed", need);
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) % 128) {
+      return fail(OQ_ERR_MISALIGNED, "gdn_chunk_fwd: workspace must be 128-byte aligned");
+    }
+    if (n_chunks > 65535) return fail(OQ_ERR_UNSUPPORTED, "gdn_chunk_fwd: more than 65535 chunks");
+  }
+  static bool attr_set[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(gdn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
-        cudaSuccess) {
-      return check_launch("gdn_chunk_fwd: shared memory attribute");
+  if (dev >= 0 && dev < 64 && !attr_set[dev][two_phase]) {
+    cudaError_t e = two_phase
+                        ? cudaFuncSetAttribute(gdn_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(kSmemBytes))
+                        : cudaFuncSetAttribute(gdn_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(kSmemBytes));
+    if (e == cudaSuccess && two_phase) {
+      e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP1Smem));
     }
-    attr_set[dev] = true;
+    if (e != cudaSuccess) return check_launch("gdn_chunk_fwd: shared memory attribute");
+    attr_set[dev][two_phase] = true;
   }
   ChunkParams p;
   p.g = g;
@@ -774,7 +1164,58 @@ extern "C" int oq_gdn_chunk_fwd(
   p.l2norm = use_qk_l2norm;
   p.status = device_status;
   dim3 grid((unsigned)num_heads, (unsigned)batch);
-  launch_plain(gdn_chunk_kernel, grid, dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), maps[0], maps[1],
-             maps[2], p);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (two_phase) {
+    if (n_chunks > 0) {
+      const dim3 pgrid((unsigned)n_chunks, (unsigned)num_heads, (unsigned)batch);
+      launch_plain(gdn_chunk_prep_kernel, pgrid, dim3(kThreads), kP1Smem, s, maps[0], maps[1], p,
+                   static_cast<uint8_t*>(workspace));
+    }
+    launch_plain(gdn_chunk_kernel<true>, grid, dim3(kThreads), kSmemBytes, s, maps[0], maps[1], maps[2], p,
+                 static_cast<const uint8_t*>(workspace));
+  } else {
+    launch_plain(gdn_chunk_kernel<false>, grid, dim3(kThreads), kSmemBytes, s, maps[0], maps[1], maps[2], p,
+                 static_cast<const uint8_t*>(nullptr));
+  }
   return check_launch("gdn_chunk_fwd");
+}
+
+}  // namespace
+}  // namespace oq
+
+extern "C" size_t oq_gdn_chunk_workspace_bytes(int64_t batch, int64_t seq_len, int64_t num_heads) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return 0;
+  return size_t(batch * num_heads * ((seq_len + oq::kC - 1) / oq::kC)) * oq::kImgBytes;
+}
+
+extern "C" int oq_gdn_chunk_fwd(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int64_t chunk_size, int32_t* device_status, void* stream) {
+  return oq::gdn_chunk_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
+                            k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
+                            initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
+                            use_qk_l2norm, chunk_size, nullptr, 0, device_status, stream);
+}
+
+extern "C" int oq_gdn_chunk_fwd_ws(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* g, int g_dtype, const void* beta, int beta_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int64_t chunk_size, void* workspace, size_t workspace_bytes,
+    int32_t* device_status, void* stream) {
+  if (workspace == nullptr) return oq::fail(OQ_ERR_WORKSPACE, "gdn_chunk_fwd_ws: null workspace");
+  return oq::gdn_chunk_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
+                            k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
+                            initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
+                            use_qk_l2norm, chunk_size, workspace, workspace_bytes, device_status, stream);
 }

@@ -185,3 +185,40 @@ def test_config4_shape_matches_recurrent_kernel():
     # both outputs are bf16 roundings of fp32 values that agree to ~1e-5: at most one bf16 step apart
     diff = (o_chunk.float() - o_rec.float()).abs()
     assert (diff <= 2.0 ** -7 * o_rec.float().abs() + 1e-3).all()
+
+
+@pytest.mark.parametrize("b,t,h,init", [(1, 1, 2, True), (2, 63, 3, True), (1, 64, 2, False), (2, 65, 2, True),
+                                        (3, 300, 4, True), (1, 1000, 2, False)])
+def test_two_phase_form_matches_the_single_kernel_bit_for_bit(b, t, h, init):
+    """oq_gdn_chunk_fwd_ws (state-independent work for all chunks first, then the state walk)
+    gives the single-kernel form's outputs and final state exactly."""
+    from optiz_qwen_b200.cabi import gdn_chunk_fwd, gdn_chunk_workspace_bytes
+
+    gen = torch.Generator(device="cuda").manual_seed(b * 1000 + t)
+    q, k, v = (torch.randn((b, t, h, 128), generator=gen, device="cuda").to(torch.bfloat16) for _ in range(3))
+    g = -torch.nn.functional.softplus(torch.randn((b, t, h), generator=gen, device="cuda"))
+    beta = torch.sigmoid(torch.randn((b, t, h), generator=gen, device="cuda"))
+    s0 = 0.05 * torch.randn((b, h, 128, 128), generator=gen, device="cuda") if init else None
+    results = []
+    for two_phase in (False, True):
+        s_out = torch.empty((b, h, 128, 128), device="cuda")
+        ws = None
+        if two_phase:  # a dirty, exactly sized workspace: nothing in it may be read before written
+            ws = torch.full((gdn_chunk_workspace_bytes(b, t, h),), 0x7F, dtype=torch.uint8, device="cuda")
+        out = gdn_chunk_fwd(q, k, v, g, beta, initial_state=s0, final_state=s_out, use_qk_l2norm=True,
+                            two_phase=two_phase, workspace=ws)
+        results.append((out, s_out))
+    torch.cuda.synchronize()
+    assert torch.equal(results[0][0], results[1][0])
+    assert torch.equal(results[0][1], results[1][1])
+
+
+def test_two_phase_form_rejects_a_short_workspace():
+    from optiz_qwen_b200.cabi import gdn_chunk_fwd, gdn_chunk_workspace_bytes
+
+    q = torch.zeros((1, 130, 2, 128), dtype=torch.bfloat16, device="cuda")
+    g = torch.zeros((1, 130, 2), device="cuda")
+    need = gdn_chunk_workspace_bytes(1, 130, 2)
+    assert need == 3 * 2 * 50176
+    with pytest.raises(ValueError, match="workspace of 301056 bytes needed"):
+        gdn_chunk_fwd(q, q, q, g, g, workspace=torch.empty(need - 128, dtype=torch.uint8, device="cuda"))
