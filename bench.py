@@ -303,7 +303,9 @@ def run_b200(args):
                 "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": counts.launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": dk["GB_s"], "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(dk["GB_s"] / hbm_peak, 4), "traffic": dram_traffic(dominant),
+                     "frac": round(dk["GB_s"] / hbm_peak, 4),
+                     # the committed capture is of the default workload's launch; other shapes have none
+                     "traffic": dram_traffic(dominant) if args.workload == "hybrid" else None,
                      "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": dk["bytes_per_launch"]},
         "kernels": kernels,
