@@ -336,7 +336,8 @@ class HybridDecodeStack:
         """The host-facing step as one graph with its transfers: a copy stream brings the
         inputs (and g) from the pinned host buffers in layer order, in groups of 1, 2, 4, 8,
         ... layers (one copy per group; a layer's launches wait for its group), and a second
-        copy stream returns each layer's outputs as soon as the layer is done.  The copies of
+        copy stream returns the outputs in groups that shrink toward the end (..., 2, 1
+        layers).  The copies of
         later layers run under the kernels of earlier ones.  (Measured at B = 64: host-to-
         device copies slow to about a third of their idle rate while the step's kernels load
         HBM, so the compute can catch up with them; growing groups beat one copy per layer,
@@ -376,13 +377,25 @@ class HybridDecodeStack:
                 if key in ready:
                     main.wait_event(ready[key])
 
+            # outputs go back in groups that shrink toward the end (..., 4, 2, 1 layers), so
+            # that the copy left after the last kernel is one layer's
+            out_last, i, n = set(), len(order) - 1, 1
+            while i >= 0:
+                out_last.add(order[i])
+                i, n = i - n, 2 * n
+            pending = []
+
             def after(key):
+                pending.append(key)
+                if key not in out_last:
+                    return
                 done = torch.cuda.Event()
                 done.record(main)
                 copy_out.wait_event(done)
                 with torch.cuda.stream(copy_out):
-                    lo, hi = self._out_range[key]
+                    lo, hi = self._out_range[pending[0]][0], self._out_range[pending[-1]][1]
                     self.out_host[lo:hi].copy_(self.out_dev[lo:hi], non_blocking=True)
+                pending.clear()
 
             self.step_device(before=before, after=after)
             main.wait_stream(copy_in)
