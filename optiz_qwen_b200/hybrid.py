@@ -201,6 +201,7 @@ class HybridDecodeStack:
     def _alloc_io(self) -> None:
         """One flat input buffer and one flat output buffer, viewed per layer."""
         s = self.shape
+        self._esize = torch.tensor([], dtype=self.dtype).element_size()
         b = s.batch
         in_specs, out_specs = [], []
         self._conv_out: list[torch.Tensor] = []
@@ -222,6 +223,9 @@ class HybridDecodeStack:
                 else:
                     in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp)]
                 in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
+                # g stays fp32 (the module computes it in fp32): its bits take two 16-bit slots
+                # per value inside the layer's input range, so the layer's inputs are one copy
+                in_specs += [(("gdn", i, "g_bits"), (b * s.gdn_heads * 4 // self._esize,))]
                 if self.epilogues:
                     in_specs += [(("gdn", i, "z"), shp)]
                 out_specs += [(("gdn", i, "out"), shp)]
@@ -237,35 +241,35 @@ class HybridDecodeStack:
                 lo, hi = ranges.get((kind, i), (off, off))
                 ranges[(kind, i)] = (lo, off + math.prod(shp))
                 off += math.prod(shp)
-        # g stays fp32 (the module computes it in fp32): a separate flat buffer
-        n_g = len(self.gdn) * b * s.gdn_heads
         self.in_dev = torch.empty(n_in, dtype=self.dtype, device=self.device)
-        self.g_dev = torch.empty(n_g, dtype=torch.float32, device=self.device)
         self.out_dev = torch.empty(n_out, dtype=self.dtype, device=self.device)
         self.in_host = torch.empty(n_in, dtype=self.dtype, pin_memory=True)
-        self.g_host = torch.empty(n_g, dtype=torch.float32, pin_memory=True)
         self.out_host = torch.empty(n_out, dtype=self.dtype, pin_memory=True)
         off = 0
+        self._g_host: list[torch.Tensor] = []
         for (kind, i, name), shp in in_specs:
+            assert off % 2 == 0  # every range starts 4-byte aligned (the fp32 g views need it)
             view = self.in_dev[off:off + math.prod(shp)].view(shp)
-            setattr((self.attn if kind == "attn" else self.gdn)[i], name, view)
+            if name == "g_bits":
+                self.gdn[i].g = view.view(torch.float32).view(b, 1, s.gdn_heads)
+                self._g_host.append(self.in_host[off:off + math.prod(shp)].view(torch.float32))
+            else:
+                setattr((self.attn if kind == "attn" else self.gdn)[i], name, view)
             off += math.prod(shp)
         off = 0
         for (kind, i, name), shp in out_specs:
             view = self.out_dev[off:off + math.prod(shp)].view(shp)
             setattr((self.attn if kind == "attn" else self.gdn)[i], name, view)
             off += math.prod(shp)
-        for i, layer in enumerate(self.gdn):
-            layer.g = self.g_dev[i * b * s.gdn_heads:(i + 1) * b * s.gdn_heads].view(b, 1, s.gdn_heads)
 
     def fill_inputs(self) -> None:
         """Synthetic step inputs with the config-0 distributions (q/k/v bf16 N(0,1), beta = sigmoid(N),
         g = -softplus(N)), written to the pinned host buffers and the device buffers."""
         gen = torch.Generator().manual_seed(12345)
         self.in_host.copy_(torch.randn(self.in_host.shape, generator=gen).to(self.dtype))
-        self.g_host.copy_(-torch.nn.functional.softplus(torch.randn(self.g_host.shape, generator=gen)))
+        for gh in self._g_host:
+            gh.copy_(-torch.nn.functional.softplus(torch.randn(gh.shape, generator=gen)))
         self.in_dev.copy_(self.in_host)
-        self.g_dev.copy_(self.g_host)
         for layer in self.gdn:
             layer.beta.copy_(torch.sigmoid(layer.beta.float()).to(self.dtype))
         self.in_host.copy_(self.in_dev)
@@ -348,7 +352,6 @@ class HybridDecodeStack:
             self.step_device()
         torch.cuda.current_stream(dev).wait_stream(self.stream)
         copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        b, heads = self.shape.batch, self.shape.gdn_heads
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=self.stream):
             main = self.stream
@@ -365,11 +368,7 @@ class HybridDecodeStack:
             with torch.cuda.stream(copy_in):
                 for grp in groups:
                     lo, hi = self._in_range[grp[0]][0], self._in_range[grp[-1]][1]
-                    self.in_dev[lo:hi].copy_(self.in_host[lo:hi], non_blocking=True)
-                    gdn = [key[1] for key in grp if key[0] == "gdn"]
-                    if gdn:  # the group's GDN layers are consecutive in the g buffer
-                        g0, g1 = min(gdn) * b * heads, (max(gdn) + 1) * b * heads
-                        self.g_dev[g0:g1].copy_(self.g_host[g0:g1], non_blocking=True)
+                    self.in_dev[lo:hi].copy_(self.in_host[lo:hi], non_blocking=True)  # (g included)
                     ready[grp[0]] = torch.cuda.Event()
                     ready[grp[0]].record(copy_in)
 
@@ -434,7 +433,7 @@ class HybridDecodeStack:
             attn_bytes=attn_bytes_layer * n_attn,
             gdn_bytes=gdn_bytes_layer * n_gdn,
             append_bytes=append_bytes_layer * n_attn,
-            h2d_bytes=self.in_dev.numel() * esize + self.g_dev.numel() * 4,
+            h2d_bytes=self.in_dev.numel() * esize,
             d2h_bytes=self.out_dev.numel() * esize,
             per_kernel={"decode_attn_int4_paged": attn_bytes_layer, "gdn_recurrent": gdn_bytes_layer,
                         "append_quant_int4": append_bytes_layer},

@@ -163,8 +163,7 @@ def test_host_facing_step_copies_overlap_and_match_the_device_graph():
     stack.io_graph = stack.capture_io()  # (runs one eager step first)
     for layer, s0 in zip(stack.gdn, states0):
         layer.state.copy_(s0)
-    stack.in_dev.zero_()
-    stack.g_dev.zero_()
+    stack.in_dev.zero_()  # (g lives in the input buffer too)
     stack.out_host.zero_()
     torch.cuda.synchronize()
     got = stack.step()
