@@ -54,6 +54,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["hybrid", "serving", "longctx", "prefill"], default="hybrid")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-bits", type=int, choices=[4, 8], default=4,
+                    help="hybrid/serving: width of the paged KV cache codes (8: the reference's k_bits=8 preset)")
     ap.add_argument("--conv", choices=["separate", "fused"], default=None,
                     help="hybrid/serving: feed each GDN layer its raw projection output and run its causal conv1d "
                          "update (separate kernel, or fused into the GDN step)")
@@ -188,12 +190,12 @@ def build_stack(args, world, rank, device):
     if args.workload == "hybrid":
         shape = HybridShape(batch=64, context=4096)
         stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv,
-                                  epilogues=args.epilogues)
+                                  epilogues=args.epilogues, kv_bits=args.kv_bits)
         desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
                 "epilogues": EPILOGUES if args.epilogues else "none",
                 "workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
-                            "INT4 paged KV, page 64, permuted pages), 3:1 interleave, hidden 2048",
+                            f"INT{args.kv_bits} paged KV, page 64, permuted pages), 3:1 interleave, hidden 2048",
                 "batch_per_gpu": 64, "global_batch": 64 * world, "context": 4096, "layers": 24,
                 "context_held": "each step appends the new token at slot 4096 and attends over 4097",
                 "l2": "no flush: ~2 GB per-step working set > 126 MB L2", "parallelism": f"dp{world} (sequences)"}
@@ -203,11 +205,11 @@ def build_stack(args, world, rank, device):
     mine = [lengths[i] for i in shards[rank]]
     shape = HybridShape(batch=len(mine), context=mine)
     stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv,
-                              epilogues=args.epilogues)
+                              epilogues=args.epilogues, kv_bits=args.kv_bits)
     desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
             "epilogues": EPILOGUES if args.epilogues else "none",
             "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
-                        "cost across GPUs, 24-layer hybrid hot path", "global_batch": 1024,
+                        f"cost across GPUs, 24-layer hybrid hot path, INT{args.kv_bits} paged KV", "global_batch": 1024,
             "batch_this_rank": len(mine), "layers": 24, "l2": "no flush: working set far above L2",
             "parallelism": f"sequence-sharded x{world}"}
     return stack, 1024, desc
@@ -257,8 +259,8 @@ def run_b200(args):
     kernels = {}
     reps = max(20, min(200, args.steps // 5))
     for kind, name, launches in (("gdn", "gdn_recurrent", len(stack.gdn)),
-                                 ("attn", "decode_attn_int4_paged", len(stack.attn)),
-                                 ("append", "append_quant_int4", len(stack.attn))):
+                                 ("attn", f"decode_attn_int{stack.kv_bits}_paged", len(stack.attn)),
+                                 ("append", f"append_quant_int{stack.kv_bits}", len(stack.attn))):
         g = stack.capture((kind,))
         for _ in range(3):
             g.replay()
@@ -270,7 +272,7 @@ def run_b200(args):
                          "frac_of_hbm": round(nbytes / us / 1e3 / hbm_peak, 4),
                          "share_of_step": round(per_step / ms_local, 3)}
         del g
-    dominant = max((k for k in kernels if k != "append_quant_int4"),
+    dominant = max((k for k in kernels if not k.startswith("append_quant")),
                    key=lambda k: kernels[k]["us_per_launch"] * kernels[k]["launches_per_step"])
     dk = kernels[dominant]
 
@@ -292,10 +294,11 @@ def run_b200(args):
 
     step_bytes = counts.attn_bytes + counts.gdn_bytes + counts.append_bytes
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if stack.kv_bits == 4 else METRIC.replace("INT4", "INT8"), "value": round(value, 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak" if args.workload == "hybrid" else "strong", "vs_baseline": None,
-        "dtype": "int4 KV codes x bf16/fp16 tensor-core dots, fp32 softmax/accumulate; fp32 GDN state",
+        "dtype": f"int{stack.kv_bits} KV codes x bf16/fp16 tensor-core dots, fp32 softmax/accumulate; fp32 GDN state",
         "data": "synthetic, seeded (config-0 distributions)", "config": desc,
         "clocks": clocks.summary(),
         "e2e": {"value": round(global_batch * 1000.0 / e2e_ms, 1), "unit": "tokens/s",
@@ -313,7 +316,7 @@ def run_b200(args):
                      "frac": round(step_bytes / ms_local / 1e6 / hbm_peak, 4)},
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(stack.shape, args.cpu_seconds, args.epilogues)
+        line["cpu_baseline"] = cpu_baseline(stack.shape, args.cpu_seconds, args.epilogues, bits=stack.kv_bits)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph, stack
@@ -327,7 +330,8 @@ class OracleStep:
     per attention layer the reference quantiser on the new token, dequantisation of the whole
     INT4 cache and fp32 attention; per GDN layer the recurrent gated delta rule."""
 
-    def __init__(self, shape, seqs: int, layer_fraction: float = 1.0, seed: int = 0, epilogues: bool = False):
+    def __init__(self, shape, seqs: int, layer_fraction: float = 1.0, seed: int = 0, epilogues: bool = False,
+                 bits: int = 4):
         import numpy as np
 
         rng = np.random.default_rng(seed)
@@ -340,7 +344,8 @@ class OracleStep:
         self.n_gdn = max(1, round(shape.layer_types.count("linear_attention") * layer_fraction))
         self.scale_layers = (shape.layer_types.count("full_attention") + shape.layer_types.count(
             "linear_attention")) / (self.n_attn + self.n_gdn)
-        self.codes = rng.integers(0, 256, (hkv, 2, ctx + 1, d // 2), dtype=np.uint8)
+        self.bits = bits
+        self.codes = rng.integers(0, 256, (hkv, 2, ctx + 1, d * bits // 8), dtype=np.uint8)
         self.meta = (rng.random((hkv, 4, ctx + 1)) * 0.4).astype(np.float16)
         self.q = rng.standard_normal((1, shape.num_heads, d)).astype(np.float32)
         self.knew = rng.standard_normal((1, hkv, 1, d)).astype(np.float32)
@@ -359,9 +364,11 @@ class OracleStep:
         from oracle import kv_quant as kq
 
         for _ in range(self.n_attn):
-            kq.quantize_tokens_int4(self.knew)
-            k = kq.dequantize_tokens_int4(self.codes[:, 0], self.meta[:, 0], self.meta[:, 1])
-            v = kq.dequantize_tokens_int4(self.codes[:, 1], self.meta[:, 2], self.meta[:, 3])
+            quant, deq = ((kq.quantize_tokens_int4, kq.dequantize_tokens_int4) if self.bits == 4
+                          else (kq.quantize_tokens_int8, kq.dequantize_tokens_int8))
+            quant(self.knew)
+            k = deq(self.codes[:, 0], self.meta[:, 0], self.meta[:, 1])
+            v = deq(self.codes[:, 1], self.meta[:, 2], self.meta[:, 3])
             o, _ = oattn.decode_attention(self.q, [k], [v], self.shape.head_dim ** -0.5)
             if self.epilogues:
                 ep.sigmoid_gate(o, self.gate, rnd=kq.round_bf16)
@@ -377,11 +384,11 @@ class OracleStep:
         return (time.perf_counter() - t0) * self.scale_layers / self.seqs
 
 
-def cpu_baseline(shape, budget_s: float, epilogues: bool = False):
+def cpu_baseline(shape, budget_s: float, epilogues: bool = False, bits: int = 4):
     import concurrent.futures as cf
 
     cores = os.cpu_count() or 1
-    step = OracleStep(shape, seqs=cores, epilogues=epilogues)
+    step = OracleStep(shape, seqs=cores, epilogues=epilogues, bits=bits)
     with cf.ThreadPoolExecutor(cores) as pool:
         step.run(pool)                                     # warm-up
         t0, times = time.perf_counter(), []
@@ -419,7 +426,8 @@ def run_reference(args):
         budget_per_step = 150.0 / max(1, args.steps + args.warmup)
         frac = min(1.0, budget_per_step / max(t_seq, 1e-9))
         seqs = max(1, min(cores, int(budget_per_step / max(t_seq, 1e-9))))
-        step = OracleStep(shape, seqs=seqs, layer_fraction=frac if seqs == 1 else 1.0, epilogues=args.epilogues)
+        step = OracleStep(shape, seqs=seqs, layer_fraction=frac if seqs == 1 else 1.0, epilogues=args.epilogues,
+                          bits=args.kv_bits)
         for _ in range(args.warmup):
             step.run(pool)
         times = [step.run(pool) for _ in range(args.steps)]
@@ -427,7 +435,8 @@ def run_reference(args):
     value = 1.0 / sec_per_token
     sample = (f"per step {step.seqs} sequence(s) x {step.n_attn} attention + {step.n_gdn} GDN layers on "
               f"{cores} threads, scaled to the 24-layer stack; numpy oracle of the reference's CPU torch path")
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": METRIC if args.kv_bits == 4 else METRIC.replace("INT4", "INT8"),
+            "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec_per_token * 1000 * step.seqs, 3),
             "higher_is_better": True, "scaling": "weak" if args.workload == "hybrid" else "strong",
             "vs_baseline": None, "dtype": "fp32 (numpy)", "data": "synthetic, seeded", "config": desc,

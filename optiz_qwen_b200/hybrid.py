@@ -115,13 +115,18 @@ class HybridDecodeStack:
 
     CONV_KERNEL = 4
 
-    KV_BYTES_PER_TOKEN_HEAD = 264  # 2 x 128 B codes + 4 x 2 B fp16 scale/min
+    KV_BYTES_PER_TOKEN_HEAD = 264  # INT4: 2 x 128 B codes + 4 x 2 B fp16 scale/min (INT8: 520)
 
     def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
                  hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16,
-                 conv: str | None = None, epilogues: bool = False):
+                 conv: str | None = None, epilogues: bool = False, kv_bits: int = 4):
         if conv not in (None, "separate", "fused"):
             raise ValueError("conv must be None, 'separate' or 'fused'")
+        if kv_bits not in (4, 8):
+            raise ValueError("kv_bits must be 4 or 8")
+        self.kv_bits = kv_bits
+        # K + V codes and the four fp16 scale / min values of one token and KV head
+        self.kv_bytes_per_token_head = 2 * shape.head_dim * kv_bits // 8 + 8
         self.shape = shape
         self.conv = conv
         self.epilogues = epilogues
@@ -167,7 +172,7 @@ class HybridDecodeStack:
     def _make_attn_layer(self, lengths, extra_tokens, page_seed) -> _AttnLayer:
         s = self.shape
         need = [cabi.pages_for(n + 1 + extra_tokens, s.page_size) for n in lengths]
-        pool = cabi.PagedKvPool(sum(need), s.num_kv_heads, s.head_dim, s.page_size, self.device)
+        pool = cabi.PagedKvPool(sum(need), s.num_kv_heads, s.head_dim, s.page_size, self.device, bits=self.kv_bits)
         paged = PagedKvState(pool, s.batch, max_pages=max(need), allocator=PageAllocator(sum(need), page_seed))
         paged.reserve([n + 1 + extra_tokens for n in lengths])
         # populate each sequence's history with bf16 N(0,1) K/V, quantised by the append kernel itself;
@@ -185,7 +190,7 @@ class HybridDecodeStack:
                 shp = (len(rows), s.num_kv_heads, m, s.head_dim)
                 k = torch.randn(shp, generator=self.gen, device=self.device, dtype=torch.float32).to(self.dtype)
                 v = torch.randn(shp, generator=self.gen, device=self.device, dtype=torch.float32).to(self.dtype)
-                cabi.append_quant_int4(k, v, pool, table, lens, advance=True)
+                cabi.append_quant(k, v, pool, table, lens, advance=True)
                 del k, v
             paged.seq_lens.index_copy_(0, idx, lens)
         torch.cuda.synchronize(self.device)
@@ -288,11 +293,11 @@ class HybridDecodeStack:
                 layer = self.attn[i]
                 p = layer.paged
                 if "append" in kinds:
-                    cabi.append_quant_int4(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
+                    cabi.append_quant(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
                                            advance=not self.hold_context)
                     prev = ("append", i)
                 if "attn" in kinds:
-                    cabi.decode_attention_int4(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
+                    cabi.decode_attention(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
                                                out=layer.out, workspace=layer.workspace, gate=layer.gate)
                     prev = ("attn", i)
             elif "gdn" in kinds:
@@ -415,7 +420,7 @@ class HybridDecodeStack:
         s = self.shape
         lengths = np.array(s.lengths)
         attend = lengths + 1 if self.hold_context else lengths
-        attn_bytes_layer = int(attend.sum()) * s.num_kv_heads * self.KV_BYTES_PER_TOKEN_HEAD
+        attn_bytes_layer = int(attend.sum()) * s.num_kv_heads * self.kv_bytes_per_token_head
         gdn_bytes_layer = 2 * s.batch * s.gdn_heads * s.gdn_dim * s.gdn_dim * 4
         if self.conv:  # conv state read + written, plus the weights
             esz = torch.tensor([], dtype=self.dtype).element_size()
@@ -425,7 +430,7 @@ class HybridDecodeStack:
             esz = torch.tensor([], dtype=self.dtype).element_size()
             attn_bytes_layer += s.batch * s.num_heads * s.head_dim * esz
             gdn_bytes_layer += (s.batch * s.gdn_heads + 1) * s.gdn_dim * esz
-        append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.KV_BYTES_PER_TOKEN_HEAD)
+        append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.kv_bytes_per_token_head)
         n_attn, n_gdn = len(self.attn), len(self.gdn)
         esize = self.in_dev.element_size()
         return StepCounts(
@@ -435,6 +440,6 @@ class HybridDecodeStack:
             append_bytes=append_bytes_layer * n_attn,
             h2d_bytes=self.in_dev.numel() * esize,
             d2h_bytes=self.out_dev.numel() * esize,
-            per_kernel={"decode_attn_int4_paged": attn_bytes_layer, "gdn_recurrent": gdn_bytes_layer,
-                        "append_quant_int4": append_bytes_layer},
+            per_kernel={f"decode_attn_int{self.kv_bits}_paged": attn_bytes_layer, "gdn_recurrent": gdn_bytes_layer,
+                        f"append_quant_int{self.kv_bits}": append_bytes_layer},
         )
