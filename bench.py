@@ -502,7 +502,8 @@ def run_longctx(args):
             "data": "synthetic, seeded",
             "config": {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
                                    "KV range split evenly across GPUs, NCCL all-gather of fp32 (out, lse) partials "
-                                   "+ LSE merge per layer, step captured in a CUDA graph", "global_batch": 1},
+                                   "+ LSE merge per layer (one GPU: the attention kernel writes the output, no "
+                                   "exchange), step captured in a CUDA graph", "global_batch": 1},
             "step_hbm": {"kv_bytes_per_step_total": kv_bytes,
                          "GB_s_per_gpu": round(kv_bytes / world / ms / 1e6, 1),
                          "frac_per_gpu": round(kv_bytes / world / ms / 1e6 / hbm_peak, 4), "peak_source": peak_src}}

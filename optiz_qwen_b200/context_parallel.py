@@ -59,6 +59,9 @@ class PartialFns:
 
     partial: Callable[[torch.Tensor], tuple[torch.Tensor, torch.Tensor]]  # q [B,Hq,D] -> (out_f32, lse)
     merge: Callable[[torch.Tensor, torch.Tensor], torch.Tensor]          # (part_out, part_lse) -> out [R, D]
+    # optional, one rank: q -> out [B, Hq, D] straight from the attention kernel.  The merge of a
+    # single partial is the identity, so the fp32 partial, its packing and the merge are skipped.
+    single: Callable[[torch.Tensor], torch.Tensor] | None = None
 
 
 def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> torch.Tensor:
@@ -68,9 +71,11 @@ def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> 
     """
     import torch.distributed as dist
 
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1 and fns.single is not None:
+        return fns.single(q).reshape(q.shape)
     out_f32, lse = fns.partial(q)
     msg = pack_partial(out_f32, lse)
-    world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
         part_out, part_lse = unpack_partials(msg.view(1, *msg.shape), q.shape[-1])
         return fns.merge(part_out, part_lse).reshape(q.shape)
@@ -146,19 +151,29 @@ class ContextParallelDecoder:
             self.paged.append(key, value)
             self.range = (self.range[0], self.range[1] + int(key.shape[-2]))
 
+    def _workspace(self, q: torch.Tensor) -> torch.Tensor:
+        if self._ws is None:
+            b, hq, _ = q.shape
+            self._ws = self.cabi.new_decode_workspace(b, hq, self.num_kv_heads, self.paged.max_pages, self.device)
+        return self._ws
+
     def _partial(self, q: torch.Tensor):
         b, hq, d = q.shape
         out_f32 = torch.empty((b, hq, d), dtype=torch.float32, device=self.device)
         lse = torch.empty((b, hq), dtype=torch.float32, device=self.device)
-        if self._ws is None:
-            self._ws = self.cabi.new_decode_workspace(b, hq, self.num_kv_heads, self.paged.max_pages, self.device)
         self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
-                                        self.head_dim ** -0.5, out_f32=out_f32, out_lse=lse, workspace=self._ws,
-                                        want_out=False)
+                                        self.head_dim ** -0.5, out_f32=out_f32, out_lse=lse,
+                                        workspace=self._workspace(q), want_out=False)
         return out_f32, lse
+
+    def _single(self, q: torch.Tensor) -> torch.Tensor:
+        return self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
+                                               self.head_dim ** -0.5, workspace=self._workspace(q))
 
     def _merge(self, part_out: torch.Tensor, part_lse: torch.Tensor) -> torch.Tensor:
         return self.cabi.lse_merge(part_out, part_lse, dtype=self.out_dtype)
 
     def decode(self, q: torch.Tensor) -> torch.Tensor:
-        return context_parallel_attention(q, PartialFns(self._partial, self._merge), self.group)
+        # one rank with the output in the query's dtype: the kernel writes the output itself
+        single = self._single if q.dtype == self.out_dtype else None
+        return context_parallel_attention(q, PartialFns(self._partial, self._merge, single), self.group)

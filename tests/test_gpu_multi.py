@@ -90,3 +90,31 @@ def test_long_context_split_over_two_gpus_matches_one_gpu_and_oracle():
         assert_attn_close(out[1], ref1)
         assert_attn_close(out[0], single0)
     assert np.array_equal(outs[0], outs[1])        # every rank holds the same merged output
+
+
+def test_one_rank_path_matches_partial_and_merge_and_oracle():
+    """With one rank the decoder skips the fp32 partial, its packing and the merge: the attention
+    kernel writes the output.  Both paths, before and after an append, against the oracle."""
+    from oracle import kv_quant as kq
+    from oracle.attention import decode_attention
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder, PartialFns, context_parallel_attention
+    from tests._util import assert_attn_close
+
+    k, v, q, kn = _inputs()
+    dec = ContextParallelDecoder(2, 256, rank=0, world=1, device="cuda")
+    dec.prefill(torch.from_numpy(k).to(torch.bfloat16), torch.from_numpy(v).to(torch.bfloat16), capacity_tokens=16)
+    kd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([k, kn], axis=2)))[0]
+    vd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([v, kn], axis=2)))[0]
+    refs = [decode_attention(q[0], [kd[:, :LENGTH]], [vd[:, :LENGTH]], 1 / 16)[0],
+            decode_attention(q[1], [kd], [vd], 1 / 16)[0]]
+    for step in range(2):
+        if step == 1:
+            knt = torch.from_numpy(kn).cuda().to(torch.bfloat16)
+            dec.append(knt, knt)
+        qt = torch.from_numpy(q[step]).cuda().to(torch.bfloat16)
+        fast = dec.decode(qt)
+        general = context_parallel_attention(qt, PartialFns(dec._partial, dec._merge))
+        assert fast.dtype == torch.bfloat16 and fast.shape == qt.shape
+        assert_attn_close(fast.float().cpu().numpy(), refs[step])
+        assert_attn_close(general.float().cpu().numpy(), refs[step])
+        assert_attn_close(fast.float().cpu().numpy(), general.float().cpu().numpy())
