@@ -50,10 +50,11 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(f
 // scheduled while its predecessor in the stream is still finishing.  Every kernel
 // calls pdl_wait() before it reads memory an earlier kernel may write (results are
 // exactly those of plain stream order) and pdl_allow_next() once its successor may
-// be scheduled; both are no-ops for a plain launch.  Only the GDN step uses
-// launch_pdl, when its caller asks for it: measured on B200, early launches pay off
-// in a chain of GDN steps (state loads overlap the previous step's tail) but cost
-// more than they save between the attention / append kernels of a decode step.
+// be scheduled; both are no-ops for a plain launch.  launch_pdl is used where it was
+// measured to pay on B200: the GDN step when its caller asks for it (in a chain of GDN
+// steps the state loads overlap the previous step's tail), the split-KV merge after
+// its attention grid, and the standalone gated RMSNorm.  Between the attention /
+// append kernels of a decode step an early launch cost more than it saved.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_allow_next() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 

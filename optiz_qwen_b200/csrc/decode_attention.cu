@@ -932,11 +932,13 @@ int decode_attn_impl(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   launch_plain(kernel, grid, dim3(threads), smem_bytes, s, tmap, p);
   if (p.defer_merge) {
+    // early launch: the merge waits (griddepcontrol.wait) for the whole attention grid before
+    // it reads a partial, and its launch gap overlaps the attention's epilogue
     const dim3 mgrid((unsigned)units, (unsigned)group);
     if (dtype == OQ_BF16) {
-      launch_plain(split_merge_kernel<__nv_bfloat16>, mgrid, dim3(kMergeThreads), 0, s, p);
+      launch_pdl(split_merge_kernel<__nv_bfloat16>, mgrid, dim3(kMergeThreads), 0, s, p);
     } else {
-      launch_plain(split_merge_kernel<__half>, mgrid, dim3(kMergeThreads), 0, s, p);
+      launch_pdl(split_merge_kernel<__half>, mgrid, dim3(kMergeThreads), 0, s, p);
     }
   }
   return check_launch(name);
