@@ -47,15 +47,16 @@ struct __align__(16) SmemTail {
 };
 
 // Page formats: INT4 (two codes per byte, 16 KB of codes per page and KV head, 4 stages)
-// and INT8 (one code per byte, 32 KB, 3 stages).  A CTA holds kWG warp groups of 4 warps,
-// each with its own stage ring, barriers and share of the CTA's pages: 3 groups for INT4
-// and 2 for INT8, one CTA per SM (the shared memory of the rings and the registers of
-// 384 threads at up to 170 per thread).
+// and INT8 (one code per byte, 32 KB, 2 stages).  A CTA holds 3 warp groups of 4 warps,
+// each with its own stage ring, barriers and share of the CTA's pages, one CTA per SM (the
+// shared memory of the rings and the registers of 384 threads at up to 168 per thread).
+// For INT8, 3 groups x 2 stages beat 2 groups x 3 stages (the same 6 pages in flight per
+// SM, 12 warps instead of 8 to cover the page loop's latencies).
 template <int kBits>
 struct PageFormat {
   static constexpr int kCodeBytes = 2 * kPage * kHeadDim * kBits / 8;
-  static constexpr int kStagesN = kBits == 8 ? 3 : kStages;
-  static constexpr int kWG = kBits == 8 ? 2 : 3;
+  static constexpr int kStagesN = kBits == 8 ? 2 : kStages;
+  static constexpr int kWG = 3;
   // one warp group's region, 1024-aligned: stage codes | stage metas | tail
   static constexpr size_t kWgBytes =
       (size_t(kStagesN) * (kCodeBytes + kStageMetaBytes) + sizeof(SmemTail) + 1023) / 1024 * 1024;
