@@ -86,7 +86,8 @@ def dram_traffic(kernel: str):
 
 # ---------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while the GPU is under the bench's load
+    (the timed loop, the per-kernel timings and the end-to-end loop, back to back)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -101,7 +102,7 @@ class ClockSampler:
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu_index)], stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -244,12 +245,12 @@ def run_b200(args):
         graph.replay()
     barrier(dist, device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index if world == 1 else local) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index if world == 1 else local).__enter__()
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize(device)
     barrier(dist, device)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, dist, device)
@@ -291,6 +292,7 @@ def run_b200(args):
     e2.record()
     torch.cuda.synchronize(device)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e_steps, dist, device)
+    clocks.__exit__(None, None, None)
 
     step_bytes = counts.attn_bytes + counts.gdn_bytes + counts.append_bytes
     line = {
@@ -298,7 +300,9 @@ def run_b200(args):
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak" if args.workload == "hybrid" else "strong", "vs_baseline": None,
-        "dtype": f"int{stack.kv_bits} KV codes x bf16/fp16 tensor-core dots, fp32 softmax/accumulate; fp32 GDN state",
+        "dtype": (f"int{stack.kv_bits} KV codes: q.k as u8 x s8 integer MMA (q in 15-bit fixed point per head), "
+                  "p.v as fp16 MMA (P' as fp16 + fp16 remainder, codes as exact fp16 subnormals), fp32 "
+                  "softmax / accumulate; GDN fp32 state, bf16 q/k/v"),
         "data": "synthetic, seeded (config-0 distributions)", "config": desc,
         "clocks": clocks.summary(),
         "e2e": {"value": round(global_batch * 1000.0 / e2e_ms, 1), "unit": "tokens/s",
@@ -498,7 +502,8 @@ def run_longctx(args):
     kv_bytes = length * 2 * 264 * layers
     line = {"metric": METRIC, "value": round(1000.0 / ms, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int4 KV codes x int8/fp16 tensor-core dots, fp32 softmax/merge",
+            "vs_baseline": None, "dtype": "int4 KV codes: q.k as u8 x s8 integer MMA, p.v as fp16 MMA; fp32 "
+                                          "softmax / merge",
             "data": "synthetic, seeded",
             "config": {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
                                    "KV range split evenly across GPUs, NCCL all-gather of fp32 (out, lse) partials "

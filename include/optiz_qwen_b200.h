@@ -69,6 +69,16 @@ const char* oq_last_error(void);
 /* ABI version: bumped when a signature changes. */
 int oq_abi_version(void);
 
+/* Test hook (no reference counterpart): sets how many times a kernel polls a copy's
+ * mbarrier before it gives up, reports OQ_DEV_TIMEOUT in the device status word and
+ * winds down (each poll sleeps up to ~20 us; the default, 100000, is about 2 s).  It
+ * applies to launches made after the call, process-wide.  0 makes every bounded wait
+ * run out at once while the copies themselves still land, which is how the tests drive
+ * the timeout path without faulting or hanging a GPU.  Before a CTA exits it waits for
+ * its own copies with the default limit, whatever this setting.  polls < 0 restores the
+ * default.  Returns the previous value. */
+int oq_debug_set_wait_polls(int polls);
+
 /* ------------------------------------------------------------------ append-quantize
  * Replaces QServeAttentionLayer._append_keys/_append_values/_quantize_and_append_*
  * + _quantize_groupwise + _pack_uint4
@@ -271,7 +281,9 @@ int oq_gather_dequant_int8(
  * Per token: S *= exp(g); kv = S^T k; delta = beta (v - kv); S += k delta^T;
  * o = S^T (scale q).  With use_qk_l2norm, q and k are first scaled by
  * 1/sqrt(sum(x^2) + 1e-6).  k_dim = v_dim = 128 in this build.
- * flags: OQ_GDN_STATE_PREFETCH or 0.
+ * flags: OQ_GDN_STATE_PREFETCH or 0.  device_status (nullable) gets OQ_DEV_TIMEOUT if the
+ * bounded wait on a state copy gives up; that slice's state and outputs are then left
+ * untouched.
  */
 int oq_gdn_recurrent(
     const void* q, const void* k, const void* v, int qkv_dtype,
@@ -281,7 +293,7 @@ int oq_gdn_recurrent(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, int flags, void* stream);
+    float scale, int use_qk_l2norm, int flags, int32_t* device_status, void* stream);
 
 /* oq_gdn_recurrent with the GDN layer's output norm fused in:
  * out = Qwen3_5RMSNormGated(o, z) per head (transformers models/qwen3_5/modeling_qwen3_5.py:175-190,

@@ -6,8 +6,9 @@ Drop-in replacements behind the reference's own Python surface:
   (``QServeKvConfig``, ``QServeAttentionLayer`` ... ``QServeDeferredSplitFusedKvCache``)
   backed by a paged INT4 pool and the fused append-quantize kernel;
 * ``optiz_qwen_b200.kernels`` -- ``qserve_int4_decode_attention`` /
-  ``qserve_int4_split_decode_attention`` (split-KV INT4 decode attention),
-  ``install_qwen35_fused_attention``, the attention-backend switch;
+  ``qserve_int4_split_decode_attention`` (split-KV INT4 decode attention) and
+  ``qserve_int8_decode_attention``, the launchers the reference's decode-attention
+  adapter imports;
 * ``optiz_qwen_b200.gdn`` -- the Gated-DeltaNet hooks
   (``fused_recurrent_gated_delta_rule``, ``chunk_gated_delta_rule``) and
   ``install_gdn_fastpath``.

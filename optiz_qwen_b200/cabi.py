@@ -252,7 +252,8 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
                   final_state: torch.Tensor | None = None, out: torch.Tensor | None = None,
                   use_qk_l2norm: bool = False, prefetch_state: bool = False, z: torch.Tensor | None = None,
                   norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
-                  norm_workspace: torch.Tensor | None = None) -> torch.Tensor:
+                  norm_workspace: torch.Tensor | None = None,
+                  device_status: torch.Tensor | None = None) -> torch.Tensor:
     """Gated delta rule over ``T`` tokens: q, k ``[B, T, H, Dk]``, v ``[B, T, H, Dv]``, g/beta ``[B, T, H]``.
 
     Writes ``final_state`` (may alias ``initial_state``) and returns ``out`` ``[B, T, H, Dv]``.
@@ -262,6 +263,8 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
     ``prefetch_state`` (``OQ_GDN_STATE_PREFETCH``) lets the kernel read the state while the
     preceding kernel in the stream is still running: only for callers that know no such
     kernel writes it (a decode step, where layer l's state was written one step earlier).
+    ``device_status`` (int32 ``[1]``, optional; the step without the fused norm) collects
+    ``OQ_DEV_TIMEOUT`` if a bounded wait on a state copy gives up.
     """
     require_cuda(q, k, v, g, beta, initial_state, final_state)
     if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
@@ -303,7 +306,7 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
          v.stride(0), v.stride(1), v.stride(2),
          ptr(g), dtype_code(g.dtype), ptr(beta), dtype_code(beta.dtype),
          ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale), int(use_qk_l2norm),
-         GDN_STATE_PREFETCH if prefetch_state else 0, stream_ptr(q.device))
+         GDN_STATE_PREFETCH if prefetch_state else 0, ptr(device_status), stream_ptr(q.device))
     return out
 
 

@@ -23,6 +23,13 @@ int ok();
 // Maps the last launch error (if any) to OQ_ERR_CUDA.
 int check_launch(const char* what);
 
+// Polls of a bounded wait on a copy before it gives up (each poll sleeps up to ~20 us in
+// mbarrier.try_wait, so the default is about 2 s).  Launches read the current value from
+// wait_polls(); oq_debug_set_wait_polls changes it (tests use 0 to make a wait run out on
+// copies that do land).  Waits that drain copies before a CTA exits always use the default.
+constexpr int kDefaultWaitPolls = 100000;
+int wait_polls();
+
 // cuTensorMapEncodeTiled resolved from the driver once per process, or nullptr.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 

@@ -11,10 +11,10 @@
 //     shared memory by one TMA tensor copy (128-byte swizzle) and one bulk copy,
 //     four pages in flight per CTA, completion tracked by mbarriers with
 //     bounded waits;
-//   * q.k runs on the integer tensor cores: q is per-head 15-bit fixed point split
-//     into two s8 digits, the codes are u8 (nibbles masked in place, no shifts),
+//   * q.k runs on the integer tensor cores: q is per-head 21-bit fixed point split
+//     into three 8-bit digits, the codes are u8 (nibbles masked in place, no shifts),
 //     mma.sync m16n8k32 gives exact int32 dot products; p.v runs on fp16 tensor
-//     cores with the nibbles dropped into the mantissa of 1024.0 (lop3);
+//     cores with the nibbles as exact fp16 subnormals (masked in place);
 //     scale/min are applied after the dot products:
 //       q.k = scale * sum(q*code) + min * sum(q),  p.v = sum((p*scale)*code) + sum(p*min);
 //   * the KV range is split across CTAs and the partial (max, sum, acc) are
@@ -35,7 +35,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 
 struct __align__(16) SmemTail {
-  uint32_t qfrag[4][32][8];  // prologue: per k-step, per lane B-operand digit fragments
+  uint32_t qfrag[4][32][12];  // per k-step, per lane: B-operand digit fragments of up to 3 MMA sets
   uint64_t full[kStages];
   int stage_ok[kStages];
   float warp_m[kWarps][kMaxGroup];
@@ -64,28 +64,46 @@ struct PageFormat {
 };
 
 // ---- q.k on integer tensor cores.
-// Each query head is turned into 15-bit fixed point, q ~ q_int * 2^-e_h with
-// |q_int| <= 16383, split into two signed 8-bit digits q_int = 128 * hi + lo
-// (lo in [0, 127]).  mma.sync m16n8k32 u8 x s8 -> s32 then gives exact integer
-// dot products of the codes with each digit.  With at most 4 query heads per
-// KV head the 8 MMA columns hold (hi digits of heads 0-3, lo digits of heads
-// 0-3), so one MMA per 32 dims covers every head ("packed"); with 5-8 heads hi
-// and lo digits take one MMA each ("dual").
+// Each query head is turned into 21-bit fixed point, q ~ q_int * 2^-e_h with
+// |q_int| <= 2^21 - 1, split into three 8-bit digits q_int = 16384 d2 + 128 d1 + d0
+// (d2 signed, d1 and d0 in [0, 127]).  mma.sync m16n8k32 u8 x s8 -> s32 then gives
+// exact integer dot products of the codes with each digit, combined in fp32.  With
+// 21 bits every bf16 (fp16) element within 2^-13 (2^-10) of the head's largest is
+// represented exactly, so q.k is as exact as fp32 arithmetic on the codes.  With at
+// most 4 query heads per KV head two MMAs per 32 dims cover every head ("packed":
+// set 0 = d2 of heads 0-3 | d1 of heads 0-3, set 1 = d0 of heads 0-3 | zeros); with
+// 5-8 heads each digit takes one MMA ("dual": sets d2, d1, d0).  The fragments live in
+// shared memory and are read per k-step.
 //
 // Code unpacking needs no shifts: w & 0x0F0F0F0F gives the even dims' codes as
 // bytes, w & 0xF0F0F0F0 the odd dims' codes times 16; the two are accumulated
 // in separate MMA chains and the second is divided by 16 (exactly) at the end.
 constexpr uint32_t kLowNibbles = 0x0F0F0F0Fu;
 constexpr uint32_t kHighNibbles = 0xF0F0F0F0u;
-constexpr int kQMax = 16383;
+constexpr int kQMax = (1 << 21) - 1;
+
+// q_int = 16384 d2 + 128 d1 + d0 with d2 in [-128, 127] and d1, d0 in [0, 127].
+__device__ __forceinline__ void split_digits(int q, int& d2, int& d1, int& d0) {
+  d2 = q >> 14;
+  const int rem = q - (d2 << 14);
+  d1 = rem >> 7;
+  d0 = rem & 127;
+}
+
+// Dot products of the three digits combined: 16384 D2 + (128 D1 + D0), the last sum exact in
+// int32 (|128 D1 + D0| < 2^31 for 256 dims of 8-bit codes), the whole rounded once to fp32.
+__device__ __forceinline__ float combine_digits(int d2, int d1, int d0) {
+  return fmaf(16384.0f, float(d2), float(128 * d1 + d0));
+}
 
 // ---- p.v on fp16 tensor cores.  prmt pairs byte b of two tokens' words into
-// the two 16-bit lanes; lop3 then drops a nibble into the mantissa of fp16
-// 1024.0: mask 0x000F000F gives 1024 + c (even dim), mask 0x00F000F0 gives
-// 1024 + 16 c (odd dim).  The 1024 * sum(P') bias and the factor 16 of the odd
-// dims are removed in the epilogue.
-constexpr float kVBias = 1024.0f;
-constexpr uint32_t kFp16Bias = 0x64006400u;
+// the two 16-bit lanes; masking then leaves a nibble as the mantissa of an fp16
+// subnormal: mask 0x000F000F gives c * 2^-24 (even dim), mask 0x00F000F0 gives
+// 16 c * 2^-24 (odd dim), both exact.  The tensor cores multiply these exactly by
+// P' and accumulate in fp32 with no bias to remove afterwards (a 1024 + c encoding
+// would cost the accumulator ~7 bits); the epilogue scales by 2^24 (2^20 for the
+// odd dims), which is exact.
+constexpr float kVCodeUnscale = 16777216.0f;  // 2^24
 __device__ __forceinline__ uint32_t byte_pair_sel(int b) { return uint32_t(b) | (uint32_t(4 + b) << 8); }
 
 // Lazy softmax rescale: the running max only moves when a tile's max exceeds it
@@ -109,8 +127,6 @@ __device__ __forceinline__ const uint4* swz8(const uint8_t* base, int row, int c
   const int line = 2 * row + (chunk >> 3);
   return reinterpret_cast<const uint4*>(base + line * 128 + (((chunk & 7) ^ (line & 7)) << 4));
 }
-// fp16 pair (1024 + byte p of a, 1024 + byte p of b) for the INT8 p.v operand
-constexpr uint32_t kFp16Hi = 0x64646464u;
 
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
@@ -154,7 +170,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   // so the groups' shares differ by at most one page), which makes the page ids of its first
   // kSt pages known before the sequence length is: they go out with the length and the 64
   // query elements this lane needs.
-  constexpr int kSets = kDual ? 2 : 1;  // dual: set 0 = hi digits, set 1 = lo digits
+  constexpr int kSets = kDual ? 3 : 2;  // MMA column sets of the q digits (see split_digits)
   const int cta_begin = split * p.pages_per_split;
   auto page_at = [&](int i) { return cta_begin + wg + kWG * i; };  // sequence page of this group's page i
   const int32_t* bt_row = p.block_table + b * p.bt_stride;
@@ -225,7 +241,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   }
 
   // ---- query digits (B operand of q.k).
-  // Per head: 15-bit fixed point with exponent e (2^e <= kQMax / max|q|), from the
+  // Per head: 21-bit fixed point with exponent e (2^e <= kQMax / max|q|), from the
   // largest element of the head (the four lanes of the head reduce by shuffles), and
   // sum(q).  k-step s covers dims 64c + 16s + {0..15}: the even dims in the "low
   // nibble" MMA, the odd dims in the "high nibble" MMA.  INT8: the same 16 dims feed
@@ -253,6 +269,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   }
   const float q_scale = ldexpf(1.0f, -q_exp);
   // warp w builds k-step w for all 32 lanes; the fragments are exchanged in shared memory
+  // as words [set][nibble MMA (lo, hi)][b0, b1] per (k-step, lane)
   {
     const float up = f_has ? ldexpf(1.0f, q_exp) : 0.0f;
     uint4 qw[2] = {qv[0], qv[1]};  // the 16 dims of k-step `warp` (selected with constant indices)
@@ -263,68 +280,70 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
         qw[1] = qv[2 * w + 1];
       }
     }
-    uint32_t frag[8];
+    uint32_t* dst = tail->qfrag[warp][lane];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {  // word 2s (b0) and word 2s+1 (b1) of the step
       const T* e = reinterpret_cast<const T*>(&qw[half]);
-      int hi_e[4], lo_e[4], hi_o[4], lo_o[4];
+      int de[3][4], dodd[3][4];  // digit 2, 1, 0 -> [0], [1], [2] of the even / odd dims
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int q_e = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j]) * up)));
         const int q_o = max(-kQMax, min(kQMax, __float2int_rn(to_float<T>(e[2 * j + 1]) * up)));
-        hi_e[j] = q_e >> 7;
-        lo_e[j] = q_e - 128 * hi_e[j];
-        hi_o[j] = q_o >> 7;
-        lo_o[j] = q_o - 128 * hi_o[j];
+        split_digits(q_e, de[0][j], de[1][j], de[2][j]);
+        split_digits(q_o, dodd[0][j], dodd[1][j], dodd[2][j]);
       }
-      uint32_t he, le, ho, lo;
-      if constexpr (kBits == 8) {  // he / le: dims +0..3 (b0), ho / lo: dims +4..7 (b1) of MMA 2w + half
-        he = pack_s8x4(hi_e[0], hi_o[0], hi_e[1], hi_o[1]);
-        le = pack_s8x4(lo_e[0], lo_o[0], lo_e[1], lo_o[1]);
-        ho = pack_s8x4(hi_e[2], hi_o[2], hi_e[3], hi_o[3]);
-        lo = pack_s8x4(lo_e[2], lo_o[2], lo_e[3], lo_o[3]);
-      } else {
-        he = pack_s8x4(hi_e[0], hi_e[1], hi_e[2], hi_e[3]);
-        le = pack_s8x4(lo_e[0], lo_e[1], lo_e[2], lo_e[3]);
-        ho = pack_s8x4(hi_o[0], hi_o[1], hi_o[2], hi_o[3]);
-        lo = pack_s8x4(lo_o[0], lo_o[1], lo_o[2], lo_o[3]);
+      uint32_t wa[3], wb[3];  // per digit: the lo-nibble and hi-nibble MMA words of this half
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        if constexpr (kBits == 8) {  // a: dims +0..3 (b0), b: dims +4..7 (b1) of MMA 2w + half
+          wa[d] = pack_s8x4(de[d][0], dodd[d][0], de[d][1], dodd[d][1]);
+          wb[d] = pack_s8x4(de[d][2], dodd[d][2], de[d][3], dodd[d][3]);
+        } else {
+          wa[d] = pack_s8x4(de[d][0], de[d][1], de[d][2], de[d][3]);
+          wb[d] = pack_s8x4(dodd[d][0], dodd[d][1], dodd[d][2], dodd[d][3]);
+        }
       }
       if constexpr (kDual) {
-        frag[half] = he;      // set 0 (hi digits): low-nibble MMA
-        frag[2 + half] = ho;  //                     high-nibble MMA
-        frag[4 + half] = le;  // set 1 (lo digits)
-        frag[6 + half] = lo;
-      } else {
-        frag[half] = r < 4 ? he : le;
-        frag[2 + half] = r < 4 ? ho : lo;
-        frag[4 + half] = 0;
-        frag[6 + half] = 0;
+#pragma unroll
+        for (int k = 0; k < kSets; ++k) {  // set k = digit 2 - k of head r
+          dst[4 * k + half] = wa[k];
+          dst[4 * k + 2 + half] = wb[k];
+        }
+      } else {  // column r: set 0 = d2 (r < 4) | d1 (r >= 4) of head r & 3; set 1 = d0 (r < 4) | 0
+        dst[half] = r < 4 ? wa[0] : wa[1];
+        dst[2 + half] = r < 4 ? wb[0] : wb[1];
+        dst[4 + half] = r < 4 ? wa[2] : 0u;
+        dst[6 + half] = r < 4 ? wb[2] : 0u;
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(tail->qfrag[warp][lane]);
-    dst[0] = make_uint4(frag[0], frag[1], frag[2], frag[3]);
-    dst[1] = make_uint4(frag[4], frag[5], frag[6], frag[7]);
   }
   named_bar_sync(bar_wg, kThreads);  // fragments written; the stage barriers are initialised
-  uint32_t bq_lo[kSets][4][2], bq_hi[kSets][4][2];
-#pragma unroll
-  for (int st4 = 0; st4 < 4; ++st4) {
-    const uint4* src = reinterpret_cast<const uint4*>(tail->qfrag[st4][lane]);
-#pragma unroll
-    for (int k = 0; k < kSets; ++k) {
-      const uint4 f = src[k];
-      bq_lo[k][st4][0] = f.x;
-      bq_lo[k][st4][1] = f.y;
-      bq_hi[k][st4][0] = f.z;
-      bq_hi[k][st4][1] = f.w;
-    }
-  }
   // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds: lanes
   // 8c (r = 2c) and 8c + 4 (r = 2c + 1) hold them
   const float qs_a = __shfl_sync(0xffffffffu, qsum, 8 * c), qs_b = __shfl_sync(0xffffffffu, qsum, 8 * c + 4);
   const float qx_a = __shfl_sync(0xffffffffu, q_scale, 8 * c), qx_b = __shfl_sync(0xffffffffu, q_scale, 8 * c + 4);
-  const bool ha_ok = (kDual || c < 2) && 2 * c < G;
-  const bool hb_ok = (kDual || c < 2) && 2 * c + 1 < G;
+  // Packed (<= 4 heads): lanes c and c + 2 both compute heads 2 (c & 1), 2 (c & 1) + 1; lanes
+  // c < 2 feed P' rounded to fp16 to MMA columns 0-3, lanes c >= 2 its fp16 remainder to
+  // columns 4-7, so p.v sees P' to ~22 bits at no extra MMA.  Dual: lane c has heads 2c, 2c+1.
+  const int hc = kDual ? c : (c & 1);
+  const bool ha_ok = 2 * hc < G;
+  const bool hb_ok = 2 * hc + 1 < G;
+  const bool lo_lane = !kDual && c >= 2;
+  // Per-set dot products -> the four q.k values of this lane.  Dual: sets d2, d1, d0 of heads
+  // 2c, 2c+1.  Packed: lane c < 2 holds d2 (set 0) and d0 (set 1) of heads 2c, 2c+1, lane c + 2
+  // the same heads' d1 (set 0); both assemble the full products.
+  auto digit_dots = [&](const int (&tot)[kSets][4], float (&dot)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (kDual) {
+        dot[j] = combine_digits(tot[0][j], tot[1][j], tot[kSets - 1][j]);
+      } else {
+        const int x0 = __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
+        const int x1 = __shfl_xor_sync(0xffffffffu, tot[kSets - 1][j], 2);
+        dot[j] = lo_lane ? combine_digits(x0, tot[0][j], x1) : combine_digits(tot[0][j], x0, tot[kSets - 1][j]);
+      }
+    }
+  };
 
   float acc[16][4];
 #pragma unroll
@@ -332,7 +351,6 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   float m_a = -INFINITY, m_b = -INFINITY;  // reference max (log2 units) of heads 2c, 2c+1
   float l_a = 0.0f, l_b = 0.0f;            // this lane's share of sum(p)
   float mp_a = 0.0f, mp_b = 0.0f;          // ... of sum(p * v_min)
-  float sp_a = 0.0f, sp_b = 0.0f;          // ... of sum(P') with P' as rounded to fp16
 
   const int tok0 = warp * 16 + r;  // token rows of this lane in the page (A rows r and r+8)
   const int tok1 = tok0 + 8;
@@ -344,7 +362,8 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
     // ---------------- values: A = V^T codes (16 dims x 16 tokens), B = P' (16 tokens x 8 heads)
     if constexpr (kBits == 8) {
       // half hf, lane r: 16-byte chunk 8 hf + r of the four token rows; MMA 8 hf + k has
-      // row r = dim 128 hf + 16 r + 2k, row r + 8 = that dim + 1, each code as fp16 1024 + c
+      // row r = dim 128 hf + 16 r + 2k, row r + 8 = that dim + 1, each code as the fp16
+      // subnormal c * 2^-24 (the byte under a zero high byte)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const uint4 xa = *swz8(stv, tb + 2 * c, 8 * hf + r), xb = *swz8(stv, tb + 2 * c + 1, 8 * hf + r);
@@ -358,10 +377,10 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
           const uint32_t x = prmt(wa[k >> 1], wb[k >> 1], sel);  // tokens 2c, 2c+1: dims 2k, 2k+1 of the chunk
           const uint32_t y = prmt(wc[k >> 1], wd[k >> 1], sel);  // tokens 2c+8, 2c+9
           uint32_t a[4];
-          a[0] = prmt(x, kFp16Hi, 0x4140u);  // row r: dim 2k, 1024 + c
-          a[1] = prmt(x, kFp16Hi, 0x4342u);  // row r+8: dim 2k + 1
-          a[2] = prmt(y, kFp16Hi, 0x4140u);
-          a[3] = prmt(y, kFp16Hi, 0x4342u);
+          a[0] = prmt(x, 0u, 0x4140u);  // row r: dim 2k, c * 2^-24
+          a[1] = prmt(x, 0u, 0x4342u);  // row r+8: dim 2k + 1
+          a[2] = prmt(y, 0u, 0x4140u);
+          a[3] = prmt(y, 0u, 0x4342u);
           mma_f16_16816(acc[8 * hf + k], a, pv0, pv1);
         }
       }
@@ -377,10 +396,10 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
           const uint32_t x = prmt(wa[wi], wb[wi], byte_pair_sel(bs));  // tokens 2c, 2c+1: dims 2bs, 2bs+1
           const uint32_t y = prmt(wc[wi], wd[wi], byte_pair_sel(bs));  // tokens 2c+8, 2c+9
           uint32_t a[4];
-          a[0] = lop3_and_or(x, 0x000F000Fu, kFp16Bias);  // row r: even dim, 1024 + c
-          a[1] = lop3_and_or(x, 0x00F000F0u, kFp16Bias);  // row r+8: odd dim, 1024 + 16 c
-          a[2] = lop3_and_or(y, 0x000F000Fu, kFp16Bias);
-          a[3] = lop3_and_or(y, 0x00F000F0u, kFp16Bias);
+          a[0] = x & 0x000F000Fu;  // row r: even dim, c * 2^-24
+          a[1] = x & 0x00F000F0u;  // row r+8: odd dim, 16 c * 2^-24
+          a[2] = y & 0x000F000Fu;
+          a[3] = y & 0x00F000F0u;
           mma_f16_16816(acc[4 * wi + bs], a, pv0, pv1);
         }
       }
@@ -392,7 +411,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   // the p.v of page i - 1 in the same block as the q.k of page i was measured: no faster.)
   for (int i = 0; i < n; ++i) {
     const int s = i % kSt;
-    bool ready = wait_stage(&tail->full[s], (i / kSt) & 1);
+    bool ready = wait_stage(&tail->full[s], (i / kSt) & 1, p.wait_polls);
     ready = __all_sync(0xffffffffu, ready);
     // tokens of page i (0 when its copy failed: every score is masked)
     const int page_tokens = (ready && tail->stage_ok[s]) ? min(kPage, len - page_at(i) * kPage) : 0;
@@ -401,7 +420,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
       const __half* meta = reinterpret_cast<const __half*>(metas + s * kStageMetaBytes);
 
       // ---------------- integer q.k: A = K codes (16 tokens x 32 dims, u8), B = q digits (s8)
-      int dot_a0, dot_b0, dot_a1, dot_b1;  // (token r, head 2c), (r, 2c+1), (r+8, 2c), (r+8, 2c+1)
+      float dot[4];  // q_int . codes of (token r, head a), (r, b), (r+8, a), (r+8, b)
       if constexpr (kBits == 8) {
         // lane c holds dims 64c .. 64c + 63 of both token rows (16 words each); MMA "lo" of
         // step s takes words 4s (b0 dims) and 4s + 2, MMA "hi" words 4s + 1 and 4s + 3,
@@ -423,24 +442,15 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
         for (int st4 = 0; st4 < 4; ++st4) {
           const uint32_t al[4] = {w0[4 * st4], w1[4 * st4], w0[4 * st4 + 2], w1[4 * st4 + 2]};
           const uint32_t ah[4] = {w0[4 * st4 + 1], w1[4 * st4 + 1], w0[4 * st4 + 3], w1[4 * st4 + 3]};
+          const uint4* qf = reinterpret_cast<const uint4*>(tail->qfrag[st4][lane]);
 #pragma unroll
           for (int k = 0; k < kSets; ++k) {
-            imma_u8s8_16832(tot[k], al, bq_lo[k][st4][0], bq_lo[k][st4][1]);
-            imma_u8s8_16832(tot[k], ah, bq_hi[k][st4][0], bq_hi[k][st4][1]);
+            const uint4 f = qf[k];
+            imma_u8s8_16832(tot[k], al, f.x, f.y);
+            imma_u8s8_16832(tot[k], ah, f.z, f.w);
           }
         }
-        int dot[4];
-        if (kDual) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + tot[kSets - 1][j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
-        }
-        dot_a0 = dot[0];
-        dot_b0 = dot[1];
-        dot_a1 = dot[2];
-        dot_b1 = dot[3];
+        digit_dots(tot, dot);
       } else {
         const uint4 k00 = *swz(st, tok0, 2 * c), k01 = *swz(st, tok0, 2 * c + 1);
         const uint4 k10 = *swz(st, tok1, 2 * c), k11 = *swz(st, tok1, 2 * c + 1);
@@ -458,31 +468,21 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
                                   w0[2 * st4 + 1] & kLowNibbles, w1[2 * st4 + 1] & kLowNibbles};
           const uint32_t ah[4] = {w0[2 * st4] & kHighNibbles, w1[2 * st4] & kHighNibbles,
                                   w0[2 * st4 + 1] & kHighNibbles, w1[2 * st4 + 1] & kHighNibbles};
+          const uint4* qf = reinterpret_cast<const uint4*>(tail->qfrag[st4][lane]);
 #pragma unroll
           for (int k = 0; k < kSets; ++k) {
-            imma_u8s8_16832(lo[k], al, bq_lo[k][st4][0], bq_lo[k][st4][1]);
-            imma_u8s8_16832(hi[k], ah, bq_hi[k][st4][0], bq_hi[k][st4][1]);
+            const uint4 f = qf[k];
+            imma_u8s8_16832(lo[k], al, f.x, f.y);
+            imma_u8s8_16832(hi[k], ah, f.z, f.w);
           }
         }
         int tot[kSets][4];
 #pragma unroll
         for (int k = 0; k < kSets; ++k) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) tot[k][j] = lo[k][j] + (hi[k][j] >> 4);
+          for (int j = 0; j < 4; ++j) tot[k][j] = lo[k][j] + (hi[k][j] >> 4);  // (hi is a multiple of 16)
         }
-        int dot[4];
-        if (kDual) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + tot[kSets - 1][j];
-        } else {
-          // columns 2c, 2c+1 of lanes c < 2 hold hi digits; lane c + 2 holds the same heads' lo digits
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dot[j] = 128 * tot[0][j] + __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
-        }
-        dot_a0 = dot[0];
-        dot_b0 = dot[1];
-        dot_a1 = dot[2];
-        dot_b1 = dot[3];
+        digit_dots(tot, dot);
       }
       const bool v0 = tok0 < page_tokens, v1 = tok1 < page_tokens;
       const float ks0 = __half2float(meta[tok0]), km0 = __half2float(meta[kPage + tok0]);
@@ -491,10 +491,10 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
       const float vs1 = __half2float(meta[2 * kPage + tok1]), vm1 = __half2float(meta[3 * kPage + tok1]);
       // q.k = scale * 2^-e * sum(code * q_int) + min * sum(q), in log2 units
       const bool ok0a = v0 && ha_ok, ok0b = v0 && hb_ok, ok1a = v1 && ha_ok, ok1b = v1 && hb_ok;
-      const float s0a = ok0a ? fmaf(ks0 * qx_a, float(dot_a0), km0 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s0b = ok0b ? fmaf(ks0 * qx_b, float(dot_b0), km0 * qs_b) * p.scale_log2 : -INFINITY;
-      const float s1a = ok1a ? fmaf(ks1 * qx_a, float(dot_a1), km1 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s1b = ok1b ? fmaf(ks1 * qx_b, float(dot_b1), km1 * qs_b) * p.scale_log2 : -INFINITY;
+      const float s0a = ok0a ? fmaf(ks0 * qx_a, dot[0], km0 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s0b = ok0b ? fmaf(ks0 * qx_b, dot[1], km0 * qs_b) * p.scale_log2 : -INFINITY;
+      const float s1a = ok1a ? fmaf(ks1 * qx_a, dot[2], km1 * qs_a) * p.scale_log2 : -INFINITY;
+      const float s1b = ok1b ? fmaf(ks1 * qx_b, dot[3], km1 * qs_b) * p.scale_log2 : -INFINITY;
 
       // ---------------- online softmax with a lazily moved reference max
       float tm_a = fmaxf(s0a, s1a), tm_b = fmaxf(s0b, s1b);
@@ -513,8 +513,6 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
         l_b *= corr_b;
         mp_a *= corr_a;
         mp_b *= corr_b;
-        sp_a *= corr_a;
-        sp_b *= corr_b;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           acc[j][0] *= corr_a;
@@ -529,15 +527,16 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
       l_b += p0b + p1b;
       mp_a += (v0 ? p0a * vm0 : 0.0f) + (v1 ? p1a * vm1 : 0.0f);
       mp_b += (v0 ? p0b * vm0 : 0.0f) + (v1 ? p1b * vm1 : 0.0f);
-      // P' = p * v_scale * 2^-kTau in fp16, rows = tokens, cols = heads
+      // P' = p * v_scale * 2^-kTau in fp16, rows = tokens, cols = heads (packed: the fp16
+      // remainder P' - fp16(P') in the lo lanes' columns)
       const float ps0 = v0 ? vs0 * kPScale : 0.0f, ps1 = v1 ? vs1 * kPScale : 0.0f;
-      const uint32_t blk0 = pack_half2(p0a * ps0, p0b * ps0);
-      const uint32_t blk1 = pack_half2(p1a * ps1, p1b * ps1);
-      {
+      uint32_t blk0 = pack_half2(p0a * ps0, p0b * ps0);
+      uint32_t blk1 = pack_half2(p1a * ps1, p1b * ps1);
+      if (lo_lane) {
         const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&blk0));
         const float2 r1 = __half22float2(*reinterpret_cast<const __half2*>(&blk1));
-        sp_a += r0.x + r1.x;
-        sp_b += r0.y + r1.y;
+        blk0 = pack_half2(fmaf(p0a, ps0, -r0.x), fmaf(p0b, ps0, -r0.y));
+        blk1 = pack_half2(fmaf(p1a, ps1, -r1.x), fmaf(p1b, ps1, -r1.y));
       }
       // transpose into the B operand of p.v
       pv_page(st, movmatrix_trans(blk0), movmatrix_trans(blk1));
@@ -556,16 +555,25 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   }
 
   pdl_allow_next();
+  bool drained = true;
   if (aborted && tid == 0) {
-    // Leave no copy in flight before the CTA exits: wait (bounded) for every issued stage.
+    // A wait gave up.  The pages issued from this group's last refill on, [issued - kSt,
+    // issued), are still unconsumed; let every one of them land (bounded, at the default
+    // limit) before this shared memory is reused below or released at exit.  The
+    // group's sums cover the pages it finished; the status word marks the result.
     report(p.status, OQ_DEV_TIMEOUT);
     for (int i = max(0, issued - kSt); i < issued; ++i) {
-      wait_stage(&tail->full[i % kSt], (i / kSt) & 1);
+      drained = wait_stage(&tail->full[i % kSt], (i / kSt) & 1, kDefaultWaitPolls) && drained;
     }
   }
   // The groups finish their page loops at different times; from here on the whole CTA
   // works together (every stage of every group has been consumed).
-  if (__syncthreads_or(aborted)) return;
+  if (__syncthreads_or(!drained)) {
+    // a copy never landed: shared memory may still be written, so the CTA leaves without
+    // using it, keeping the merge counter consistent for the next launch
+    if (ctid == 0 && nsplit_b > 1 && !p.defer_merge) merge_arrive_only(p, b * p.num_kv_heads + kvh, nsplit_b);
+    return;
+  }
 
   // ---- reduce this warp's per-lane sums over the 8 token rows
 #pragma unroll
@@ -574,8 +582,6 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
     l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
     mp_a += __shfl_xor_sync(0xffffffffu, mp_a, o);
     mp_b += __shfl_xor_sync(0xffffffffu, mp_b, o);
-    sp_a += __shfl_xor_sync(0xffffffffu, sp_a, o);
-    sp_b += __shfl_xor_sync(0xffffffffu, sp_b, o);
   }
   if (r == 0) {
     tail->warp_m[warp][2 * c] = m_a;
@@ -611,26 +617,34 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   __syncthreads();
 
   // ---- each warp's numerators at the common max: red[w][h][d] = numerator_w * 2^(m_w - M),
-  //      numerator = 2^kTau * (acc - 1024 sum(P')) / (1 or 16) + sum(p * v_min)
+  //      numerator = 2^kTau * 2^24 * acc / (1 or 16) + sum(p * v_min)
   float* red = reinterpret_cast<float*>(codes);  // this group's kWarps * kMaxGroup rows of kRedStride floats
   {
+    if constexpr (!kDual) {
+      // packed: add the remainder columns (lanes c + 2) to the fp16 P' columns (lanes c)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], 2);
+      }
+    }
     const int ha = 2 * c, hb = 2 * c + 1;
     const float fa = ha < G ? tail->warp_f[warp][ha] : 0.0f;
     const float fb = hb < G ? tail->warp_f[warp][hb] : 0.0f;
-    const float off_a = -kVBias * sp_a, off_b = -kVBias * sp_b;
-    // INT4: row r = even dim 32r + 2j (weight 1), row r + 8 = odd dim (codes x 16);
-    // INT8: MMA j = 8 hf + k, row r = dim 128 hf + 16r + 2k, row r + 8 = the next dim (weight 1)
-    constexpr float kOddUnscale = kBits == 8 ? kPUnscale : kPUnscale / 16.0f;
+    // INT4: row r = even dim 32r + 2j (codes x 1), row r + 8 = odd dim (codes x 16);
+    // INT8: MMA j = 8 hf + k, row r = dim 128 hf + 16r + 2k, row r + 8 = the next dim (x 1)
+    constexpr float kEvenUnscale = kPUnscale * kVCodeUnscale;
+    constexpr float kOddUnscale = kBits == 8 ? kEvenUnscale : kEvenUnscale / 16.0f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int d0 = kBits == 8 ? 128 * (j >> 3) + 16 * r + 2 * (j & 7) : 32 * r + 2 * j;
       if (ha < G) {
-        red[red_index(warp, ha, d0)] = fmaf(acc[j][0] + off_a, kPUnscale, mp_a) * fa;
-        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2] + off_a, kOddUnscale, mp_a) * fa;
+        red[red_index(warp, ha, d0)] = fmaf(acc[j][0], kEvenUnscale, mp_a) * fa;
+        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2], kOddUnscale, mp_a) * fa;
       }
       if (hb < G) {
-        red[red_index(warp, hb, d0)] = fmaf(acc[j][1] + off_b, kPUnscale, mp_b) * fb;
-        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3] + off_b, kOddUnscale, mp_b) * fb;
+        red[red_index(warp, hb, d0)] = fmaf(acc[j][1], kEvenUnscale, mp_b) * fb;
+        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3], kOddUnscale, mp_b) * fb;
       }
     }
   }
@@ -773,7 +787,43 @@ int64_t resident_slots(const void* kernel, int threads, size_t smem) {
   return cache[dev][k];
 }
 
+using Kernel = void (*)(const CUtensorMap, AttnParams);
+
+Kernel pick_kernel(int bits, int dtype, int64_t group) {
+  if (bits == 8) {
+    return dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 8>
+                                         : decode_attn_kernel<__nv_bfloat16, false, 8>)
+                            : (group > 4 ? decode_attn_kernel<__half, true, 8> : decode_attn_kernel<__half, false, 8>);
+  }
+  return dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 4>
+                                       : decode_attn_kernel<__nv_bfloat16, false, 4>)
+                          : (group > 4 ? decode_attn_kernel<__half, true, 4> : decode_attn_kernel<__half, false, 4>);
+}
+
 }  // namespace
+
+int decode_attn_plan(int bits, int dtype, int64_t group, int64_t batch, int64_t num_kv_heads,
+                     int64_t max_pages_per_seq, int num_splits, int* pages_per_split) {
+  // Split heuristic: as many KV ranges per (sequence, KV head) as fill one wave of
+  // resident CTAs (SMs x CTAs per SM), so no SM idles behind a short last wave.
+  const int64_t units = std::max<int64_t>(1, batch * num_kv_heads);
+  int splits = num_splits;
+  if (splits <= 0) {
+    const Kernel kernel = pick_kernel(bits, dtype, group);
+    const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
+    const int threads = (bits == 8 ? PageFormat<8>::kWG : PageFormat<4>::kWG) * kThreads;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), threads, smem_bytes);
+    // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
+    splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
+                                   std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
+  }
+  // the merging CTA stages (max, sum) of every split in 64 KB of shared memory
+  splits = int(std::min<int64_t>(std::min<int64_t>(splits, max_pages_per_seq), kMaxSplits));
+  const int pps = int((max_pages_per_seq + splits - 1) / splits);
+  if (pages_per_split) *pages_per_split = pps;
+  return int((max_pages_per_seq + pps - 1) / pps);
+}
 
 // INT4: rows of 128 B, one box = the 128 K + V rows of a (page, KV head).  INT8: rows of
 // 256 B seen as {128 B, 2 halves, rows} (the 128-byte swizzle caps a box line at 128 B).
@@ -854,35 +904,14 @@ int decode_attn_impl(
     return fail(OQ_ERR_UNSUPPORTED, "%s: page pool too large for 32-bit TMA rows", name);
   }
 
-  using Kernel = void (*)(const CUtensorMap, AttnParams);
-  Kernel kernel;
-  if (bits == 8) {
-    kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 8>
-                                           : decode_attn_kernel<__nv_bfloat16, false, 8>)
-                              : (group > 4 ? decode_attn_kernel<__half, true, 8> : decode_attn_kernel<__half, false, 8>);
-  } else {
-    kernel = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 4>
-                                           : decode_attn_kernel<__nv_bfloat16, false, 4>)
-                              : (group > 4 ? decode_attn_kernel<__half, true, 4> : decode_attn_kernel<__half, false, 4>);
-  }
+  const Kernel kernel = pick_kernel(bits, dtype, group);
   const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
   const int threads = (bits == 8 ? PageFormat<8>::kWG : PageFormat<4>::kWG) * kThreads;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
 
-  // Split heuristic: as many KV ranges per (sequence, KV head) as fill one wave of
-  // resident CTAs (SMs x CTAs per SM), so no SM idles behind a short last wave.
   const int64_t units = batch * num_kv_heads;
-  int splits = num_splits;
-  if (splits <= 0) {
-    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), threads, smem_bytes);
-    // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
-    splits = int(std::min<int64_t>(std::max<int64_t>(1, slots / units),
-                                   std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
-  }
-  // the merging CTA stages (max, sum) of every split in 64 KB of shared memory
-  splits = int(std::min<int64_t>(std::min<int64_t>(splits, max_pages_per_seq), kMaxSplits));
-  const int pps = int((max_pages_per_seq + splits - 1) / splits);
-  splits = int((max_pages_per_seq + pps - 1) / pps);
+  int pps = 0;
+  int splits = decode_attn_plan(bits, dtype, group, batch, num_kv_heads, max_pages_per_seq, num_splits, &pps);
 
   if (splits > 1 || workspace) {
     const size_t need = oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, splits);
@@ -928,6 +957,7 @@ int decode_attn_impl(
   p.gate = gate;
   p.g_sb = gate_stride_b;
   p.g_sh = gate_stride_h;
+  p.wait_polls = wait_polls();
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

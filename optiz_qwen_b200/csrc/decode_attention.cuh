@@ -43,17 +43,33 @@ struct AttnParams {
   // optional output gate: out = o * sigmoid(gate), gate [B, Hq, 256] in the query dtype
   const void* gate;
   int64_t g_sb, g_sh;
+  int wait_polls;  // polls of a bounded wait on a page copy (wait_polls() at launch)
 };
 
+// The partition a decode-attention launch uses (host side): the number of KV ranges per
+// (sequence, KV head) for `num_splits` (<= 0: one wave of resident CTAs, at least
+// kMinPagesPerSplit pages per range), clamped to the pages and to kMaxSplits and rounded
+// to whole pages per range; *pages_per_split (may be null) receives the range length.
+int decode_attn_plan(int bits, int dtype, int64_t group, int64_t batch, int64_t num_kv_heads,
+                     int64_t max_pages_per_seq, int num_splits, int* pages_per_split);
+
 // Bounded wait for a stage: the thread sleeps in try_wait (up to 20 us per poll) and
-// gives up after kWaitPolls polls (~2 s): a copy that has not landed by then never will.
+// gives up after `polls` polls (kDefaultWaitPolls: ~2 s, after which a copy that has not
+// landed never will).
 constexpr uint32_t kWaitHintNs = 20000;
-constexpr int kWaitPolls = 100000;
-__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < kWaitPolls; ++i) {
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, int polls) {
+  for (int i = 0; i < polls; ++i) {
     if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
   }
   return false;
+}
+
+// A split CTA that leaves without merging still counts itself in on its unit's merge
+// counter, so that the counter is back at zero after every launch; the last to arrive
+// resets it (the unit's output is then not written, and the status word says why).
+__device__ __forceinline__ void merge_arrive_only(const AttnParams& p, int64_t unit, int nsplit_b) {
+  const int done = atomicAdd(&p.counters[unit], 1);
+  if (done == nsplit_b - 1) p.counters[unit] = 0;
 }
 
 __device__ __forceinline__ float lse_nat(float m_log2, float l) {

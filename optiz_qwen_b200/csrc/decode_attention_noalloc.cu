@@ -18,7 +18,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "common.cuh"
+#include "decode_attention.cuh"
 
 namespace {
 
@@ -70,15 +70,16 @@ extern "C" int oq_decode_attn_int4_paged_noalloc(
                                      num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h,
                                      out_f32, out_lse, nullptr, 0, 1, device_status, stream);
   }
-  // Split count: the caller's, or the regular heuristic capped to what the fixed scratch holds.
-  int splits = num_splits;
-  if (splits <= 0) {
-    const int64_t units = batch * num_kv_heads;
-    splits = int(std::min<int64_t>(std::min<int64_t>(std::max<int64_t>(1, (148 * 6 + units - 1) / units),
-                                                     max_pages_per_seq), 512));
+  // Split count: the one oq_decode_attn_int4_paged would launch with (the same heuristic and
+  // clamps), so both entry points run the same partition whenever its scratch fits; in auto
+  // mode a partition that does not fit is halved until it does.
+  const int64_t group = num_heads / num_kv_heads;
+  int splits = decode_attn_plan(4, dtype, group, batch, num_kv_heads, max_pages_per_seq, num_splits, nullptr);
+  if (num_splits <= 0) {
     while (splits > 1 && oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, splits) >
                              kNoAllocScratchBytes) {
-      splits = std::max(1, splits / 2);
+      splits = decode_attn_plan(4, dtype, group, batch, num_kv_heads, max_pages_per_seq, std::max(1, splits / 2),
+                                nullptr);
     }
   } else if (splits > 1) {
     const size_t need = oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, splits);

@@ -68,7 +68,6 @@ constexpr uint32_t kOffBars = kOffSmall + kSmallFloats * 4;
 constexpr uint32_t kSmemBytes = kOffBars + 64 + 1024;  // + alignment slack
 
 constexpr uint32_t kWaitHintNs = 20000;
-constexpr int kWaitPolls = 100000;  // ~2 s
 
 constexpr uint32_t kIdescN64 = idesc_bf16_f32(128, 64, false, false);
 constexpr uint32_t kIdescN64BMn = idesc_bf16_f32(128, 64, false, true);
@@ -86,6 +85,7 @@ struct ChunkParams {
   float scale;
   int l2norm;
   int32_t* status;
+  int wait_polls;  // polls of a bounded wait on a copy or an MMA (wait_polls() at launch)
 };
 
 struct Bars {
@@ -104,8 +104,10 @@ constexpr uint32_t kImgScal = 6 * kTile;                // sfac[64], cq[64], gam
 constexpr uint32_t kImgScalBytes = 160 * 4;
 constexpr uint32_t kImgBytes = 6 * kTile + 1024;        // per (sequence, head, chunk)
 
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < kWaitPolls; ++i) {
+// Bounded wait (sleeping in try_wait up to 20 us per poll); false if `polls` polls pass.  Waits
+// that drain copies and MMAs before a CTA exits use kDefaultWaitPolls (~2 s).
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int polls) {
+  for (int i = 0; i < polls; ++i) {
     if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
   }
   return false;
@@ -290,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool aborted = false;
   // Waits on `bar` in every thread; true (in every thread) if any thread gave up.
   auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-    const bool ok = wait_bar(bar, parity);
+    const bool ok = wait_bar(bar, parity, p.wait_polls);
     return __syncthreads_or(!ok) != 0;
   };
   auto mma_done = [&]() {
@@ -726,13 +728,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) report(p.status, OQ_DEV_TIMEOUT);
     // Let every issued MMA and copy land before TMEM and shared memory go away.
     if (tid == 0) umma_commit(&bars->drain);
-    wait_bar(&bars->drain, 0);
+    wait_bar(&bars->drain, 0, kDefaultWaitPolls);
     for (int s = 0; s < 2; ++s) {
-      while (kq_waited[s] < kq_issued[s]) wait_bar(&bars->kq[s], (kq_waited[s]++) & 1);
+      while (kq_waited[s] < kq_issued[s]) wait_bar(&bars->kq[s], (kq_waited[s]++) & 1, kDefaultWaitPolls);
     }
-    while (v_waited < v_issued) wait_bar(&bars->v, (v_waited++) & 1);
-    while (ab_waited < ab_issued) wait_bar(&bars->ab, (ab_waited++) & 1);
-    while (p_waited < p_issued) wait_bar(&bars->pp, (p_waited++) & 1);
+    while (v_waited < v_issued) wait_bar(&bars->v, (v_waited++) & 1, kDefaultWaitPolls);
+    while (ab_waited < ab_issued) wait_bar(&bars->ab, (ab_waited++) & 1, kDefaultWaitPolls);
+    while (p_waited < p_issued) wait_bar(&bars->pp, (p_waited++) & 1, kDefaultWaitPolls);
   } else if (p.s_out != nullptr) {
     tc_fence_after();
 #pragma unroll 1
@@ -832,7 +834,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   bool issued_mma = false;
-  bool ok = wait_bar(&bars->kq, 0);
+  bool ok = wait_bar(&bars->kq, 0, p.wait_polls);
   if (__syncthreads_or(!ok) == 0) {
     // G = [K; Q] K^T (M = 128: 64 keys then 64 queries; N = 64 keys; K = d)
     if (tid == 0) {
@@ -879,7 +881,7 @@ __global__ void __launch_bounds__(kThreads)
         tok(0, 7)[t] = tok(0, 2)[t] * expf(gc[e]) * dk;
       }
     }
-    ok = wait_bar(&bars->mma, 0);
+    ok = wait_bar(&bars->mma, 0, p.wait_polls);
     if (__syncthreads_or(!ok) == 0) {
       tc_fence_after();
       const float* s_gc = tok(0, 1);
@@ -1048,8 +1050,8 @@ __global__ void __launch_bounds__(kThreads)
   if (!ok) {
     if (tid == 0) report(p.status, OQ_DEV_TIMEOUT);
     // let the copy and the MMA land before shared and tensor memory go away
-    if (tid == 0) wait_bar(&bars->kq, 0);
-    if (issued_mma && tid == 0) wait_bar(&bars->mma, 0);
+    if (tid == 0) wait_bar(&bars->kq, 0, kDefaultWaitPolls);
+    if (issued_mma && tid == 0) wait_bar(&bars->mma, 0, kDefaultWaitPolls);
   }
   tc_fence_before();
   __syncthreads();
@@ -1163,6 +1165,7 @@ int gdn_chunk_impl(
   p.scale = scale;
   p.l2norm = use_qk_l2norm;
   p.status = device_status;
+  p.wait_polls = wait_polls();
   dim3 grid((unsigned)num_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (two_phase) {

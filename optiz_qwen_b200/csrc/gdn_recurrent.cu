@@ -61,6 +61,7 @@ struct GdnParams {
   float norm_eps;
   int* norm_counters;  // [B * H] zeroed; every launch leaves them zero
   int32_t* status_word;  // OQ_DEV_* bits of the shared-memory kernel's bounded wait (may be null)
+  int wait_polls;        // polls of that wait (wait_polls() at launch)
 };
 
 constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
@@ -297,12 +298,25 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
 constexpr int kSliceFloats = kDk * kCols;  // 16 KB
 constexpr size_t kSmemSlice = size_t(kSliceFloats) * 4 + 128;
 
-// Bounded wait on a copy's mbarrier (sleeping in try_wait, ~2 s in all); false if it ran out.
-__device__ __forceinline__ bool wait_bar_bounded(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < 100000; ++i) {
+// Bounded wait on a copy's mbarrier (sleeping in try_wait up to 20 us per poll; the default
+// kDefaultWaitPolls is ~2 s in all); false if it ran out.
+__device__ __forceinline__ bool wait_bar_bounded(uint64_t* bar, uint32_t parity, int polls) {
+  for (int i = 0; i < polls; ++i) {
     if (mbar_try_wait_suspend(bar, parity, 20000)) return true;
   }
   return false;
+}
+
+// The slice copy did not land within the caller's limit: report it, and let thread 0 wait for
+// the copy (at the default limit) so that the CTA, whose shared memory the copy writes, does
+// not end while it is in flight.  Nothing has been written to global memory yet, so the
+// state and the outputs of this slice are left as they were.  (This kernel has no fused norm,
+// so no norm counter is involved.)
+__device__ __forceinline__ void slice_timeout(const GdnParams& p, uint64_t* bar, int tid) {
+  if (tid == 0) {
+    report(p.status_word, OQ_DEV_TIMEOUT);
+    wait_bar_bounded(bar, 0, kDefaultWaitPolls);
+  }
 }
 
 // 10 CTAs per SM (48 registers, no spill): at B = 64 x 16 heads x 4 slices = 4096 CTAs the
@@ -371,10 +385,12 @@ __global__ void __launch_bounds__(kThreads, 10) gdn_smem_kernel(const __grid_con
     const float gt = load_as_float(p.g, p.g_dtype, gi);
     const float bt = load_as_float(p.beta, p.beta_dtype, gi);
     if (!landed) {
-      const bool ok = wait_bar_bounded(&full, 0);
+      // thread 0 initialised the barrier; every thread sees that before it polls it
+      __syncthreads();
+      const bool ok = wait_bar_bounded(&full, 0, p.wait_polls);
       if (__syncthreads_or(!ok)) {
-        if (tid == 0) report(p.status_word, OQ_DEV_TIMEOUT);
-        return;  // (a copy that has not landed in ~2 s will not; nothing else is in flight)
+        slice_timeout(p, &full, tid);
+        return;
       }
       landed = true;
     } else {
@@ -457,9 +473,10 @@ __global__ void __launch_bounds__(kThreads, 10) gdn_smem_kernel(const __grid_con
   }
   if (p.seq_len == 0) {
     // no token: the state passes through unchanged
-    const bool ok = wait_bar_bounded(&full, 0);
+    __syncthreads();  // (the barrier's initialisation, as above)
+    const bool ok = wait_bar_bounded(&full, 0, p.wait_polls);
     if (__syncthreads_or(!ok)) {
-      if (tid == 0) report(p.status_word, OQ_DEV_TIMEOUT);
+      slice_timeout(p, &full, tid);
       return;
     }
     if (p.s_out != nullptr) {
@@ -583,7 +600,7 @@ int gdn_recurrent_impl(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, void* stream) {
+    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, int32_t* device_status, void* stream) {
   if (int st = check_norm(norm, batch, num_heads, "gdn_recurrent"); st != OQ_OK) return st;
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
@@ -618,6 +635,8 @@ int gdn_recurrent_impl(
   p.scale = scale;
   p.l2norm = use_qk_l2norm;
   p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
+  p.status_word = device_status;
+  p.wait_polls = wait_polls();
   set_norm(p, norm);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (norm == nullptr && initial_state != nullptr && batch * num_heads * kDk < (int64_t(1) << 31)) {
@@ -700,11 +719,11 @@ extern "C" int oq_gdn_recurrent(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, int flags, void* stream) {
+    float scale, int use_qk_l2norm, int flags, int32_t* device_status, void* stream) {
   return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
                                 k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
                                 initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
-                                use_qk_l2norm, nullptr, flags, stream);
+                                use_qk_l2norm, nullptr, flags, device_status, stream);
 }
 
 extern "C" int oq_gdn_recurrent_norm(
@@ -724,7 +743,7 @@ extern "C" int oq_gdn_recurrent_norm(
   return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
                                 k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
                                 initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
-                                use_qk_l2norm, &norm, flags, stream);
+                                use_qk_l2norm, &norm, flags, nullptr, stream);
 }
 
 extern "C" int oq_gdn_conv_step(

@@ -1,4 +1,5 @@
 // Status strings and the per-thread error detail behind oq_last_error().
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -7,6 +8,7 @@
 
 namespace {
 thread_local char g_last_error[512] = "";
+std::atomic<int> g_wait_polls{oq::kDefaultWaitPolls};
 }
 
 namespace oq {
@@ -46,7 +48,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+int wait_polls() { return g_wait_polls.load(std::memory_order_relaxed); }
+
 }  // namespace oq
+
+extern "C" int oq_debug_set_wait_polls(int polls) {
+  return g_wait_polls.exchange(polls < 0 ? oq::kDefaultWaitPolls : polls);
+}
 
 extern "C" const char* oq_status_string(int status) {
   switch (status) {
@@ -62,4 +70,4 @@ extern "C" const char* oq_status_string(int status) {
 
 extern "C" const char* oq_last_error(void) { return g_last_error; }
 
-extern "C" int oq_abi_version(void) { return 2; }
+extern "C" int oq_abi_version(void) { return 3; }

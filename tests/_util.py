@@ -15,7 +15,15 @@ ATTN_RTOL = 1e-2
 GDN_RTOL = 1e-4
 
 
-def assert_attn_close(actual: np.ndarray, expected: np.ndarray) -> None:
+def attn_margin(actual: np.ndarray, expected: np.ndarray) -> float:
+    """Largest |err| / (ATTN_ATOL + ATTN_RTOL |ref|): the share of the tolerance used (<= 1 passes)."""
+    actual = np.asarray(actual, np.float64)
+    expected = np.asarray(expected, np.float64)
+    return float(np.max(np.abs(actual - expected) / (ATTN_ATOL + ATTN_RTOL * np.abs(expected))))
+
+
+def assert_attn_close(actual: np.ndarray, expected: np.ndarray) -> float:
+    """Asserts the attention tolerance; returns the share of it used (see :func:`attn_margin`)."""
     actual = np.asarray(actual, np.float32)
     expected = np.asarray(expected, np.float32)
     err = np.abs(actual - expected)
@@ -24,6 +32,52 @@ def assert_attn_close(actual: np.ndarray, expected: np.ndarray) -> None:
     worst = np.unravel_index(np.argmax(err - bound), err.shape)
     assert np.all(err <= bound), (
         f"attention mismatch: max |err| {err.max():.3e} at {worst}: {actual[worst]} vs {expected[worst]}")
+    return attn_margin(actual, expected)
+
+
+def random_paged_cache(rng: np.random.Generator, lengths, num_kv_heads: int, head_dim: int, page_size: int,
+                       seed_pages=None, *, k_scale=(0.30, 0.42), k_min=(-3.1, -2.3), v_scale=(0.30, 0.42),
+                       v_min=(-3.1, -2.3)) -> kq.PagedKvOracle:
+    """A populated INT4 ``PagedKvOracle`` without running the quantiser: codes uniform on [0, 15] and
+    fp16 scale / min uniform on the given ranges (the defaults are what per-token groups of 256
+    N(0,1) values give: min about -2.7, scale about 0.36).  Used for long contexts, where
+    quantising N(0,1) data in numpy would dominate the test's time; the attention oracle
+    dequantises the stored codes and fp16 values either way."""
+    lengths = [int(x) for x in lengths]
+    need = sum(-(-n // page_size) for n in lengths)
+    max_pages = max(1, max(-(-n // page_size) for n in lengths))
+    table = kq.build_block_table(lengths, page_size, need, max_pages, seed_pages)
+    cache = kq.PagedKvOracle(need, num_kv_heads, head_dim, page_size, table, lengths)
+    cache.kv_codes[...] = rng.integers(0, 256, cache.kv_codes.shape, dtype=np.uint8)
+    meta = np.empty(cache.kv_meta.shape, np.float32)
+    for idx, (lo, hi) in enumerate((k_scale, k_min, v_scale, v_min)):
+        meta[:, :, idx] = rng.uniform(lo, hi, meta[:, :, idx].shape)
+    cache.kv_meta[...] = meta.astype(np.float16)
+    return cache
+
+
+def oracle_from_device(pool, block_table: torch.Tensor, seq_lens: torch.Tensor, rows) -> kq.PagedKvOracle:
+    """The sequences ``rows`` of a device pool as a ``PagedKvOracle`` (their pages downloaded and
+    renumbered in order; row i of the result is sequence rows[i])."""
+    rows = [int(r) for r in rows]
+    table = block_table.cpu().numpy()
+    lens = seq_lens.cpu().numpy().astype(np.int64)
+    page = pool.page_size
+    pages = [table[r, : -(-int(lens[r]) // page)] for r in rows]
+    flat = np.concatenate(pages) if pages else np.zeros(0, np.int64)
+    idx = torch.from_numpy(flat.astype(np.int64)).to(pool.kv_codes.device)
+    max_pages = max(1, max(len(x) for x in pages))
+    new_table = np.full((len(rows), max_pages), -1, np.int32)
+    off = 0
+    for i, x in enumerate(pages):
+        new_table[i, : len(x)] = np.arange(off, off + len(x))
+        off += len(x)
+    cache = kq.PagedKvOracle(max(1, len(flat)), pool.num_kv_heads, pool.head_dim, page, new_table,
+                             [int(lens[r]) for r in rows], bits=pool.bits)
+    if len(flat):
+        cache.kv_codes[...] = pool.kv_codes.index_select(0, idx).cpu().numpy()
+        cache.kv_meta[...] = pool.kv_meta.index_select(0, idx).cpu().numpy()
+    return cache
 
 
 def assert_gdn_close(actual: np.ndarray, expected: np.ndarray, rtol: float = GDN_RTOL) -> None:

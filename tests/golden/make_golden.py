@@ -165,7 +165,8 @@ def make_epilogue(torch):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (its src/ holds the optiz_qwen package)")
     ap.add_argument("--only", choices=["quant", "attention", "gdn", "epilogue"], default=None,
                     help="regenerate one fixture file only")
     args = ap.parse_args()

@@ -63,6 +63,6 @@ def test_argument_validation_needs_no_gpu():
                                            1, 8, 2, 256, 1.0, None, 0, 0, None, None, None, 0, 0, None, None)
     assert status == _lib.OQ_ERR_UNSUPPORTED          # fp32 query
     status = lib.oq_gdn_recurrent(None, None, None, _lib.OQ_BF16, 0, 0, 0, 0, 0, 0, 0, 0, 0, None, 0, None, 0,
-                                  None, None, None, 1, 1, 1, 64, 64, 1.0, 0, 0, None)
+                                  None, None, None, 1, 1, 1, 64, 64, 1.0, 0, 0, None, None)
     assert status == _lib.OQ_ERR_UNSUPPORTED          # head dims other than 128
     assert b"128" in lib.oq_last_error()

@@ -1,8 +1,8 @@
 """Host-side behaviour of the drop-in API (mirrors the reference's tests/test_qserve_kv_cache.py:32-172).
 
-Everything here runs on CPU: config validation, chain building, dense-phase
-behaviour of the deferred layer, prefill delegation of the fused forward, the
-page allocator policy, and loud failure of the kernels on CPU tensors.
+Everything here runs on CPU: config validation, the cache builder, dense-phase
+behaviour of the deferred layer, the page allocator policy, and loud failure of the
+kernels on CPU tensors.
 """
 
 from __future__ import annotations
@@ -18,8 +18,6 @@ from optiz_qwen_b200.compression import (
     QServeKvConfig,
     build_qserve_deferred_split_fused_kv_cache,
 )
-from optiz_qwen_b200.kernels.qwen35_fused_attention import _qserve_fused_forward
-from optiz_qwen_b200.scheduling import build_kv_chain
 
 
 class MinimalQwenConfig:
@@ -67,21 +65,14 @@ def test_packing_cpu_tensors_fails_loudly():
         layer.update(torch.randn(1, 2, 1, 16), torch.randn(1, 2, 1, 16))
 
 
-def test_deferred_split_chain_reports_its_runtime_implementation():
-    cache, report = build_kv_chain(chain_name="qserve_deferred_split_fused_kv", model_config=MinimalQwenConfig(),
-                                   enabled=True, qserve_config=CFG16)
+def test_deferred_split_cache_builder_places_packed_layers_on_full_attention():
+    """What the reference's chain builder (scheduling/kv_chain.py) receives from the cache builder."""
+    cache = build_qserve_deferred_split_fused_kv_cache(MinimalQwenConfig(), CFG16)
     assert isinstance(cache, QServeDeferredSplitFusedKvCache)
-    assert report.implementation == "qserve_triton_int4_deferred_split_decode"
     assert cache.full_attention_layers == (1,)
     assert isinstance(cache.layers[1], QServeDeferredSplitFusedAttentionLayer)
     assert cache.kernel_calls == 0 and cache.fallback_calls == 0
     assert cache.packed_decode_active() is False
-
-
-def test_disabled_chain_builds_nothing():
-    cache, report = build_kv_chain(chain_name="QServe_Deferred_Split_Fused_KV", model_config=MinimalQwenConfig(),
-                                   enabled=False)
-    assert cache is None and report.enabled is False
 
 
 def test_qserve_config_rejects_unknown_attention_backend():
@@ -121,34 +112,11 @@ def test_8bit_layers_build_an_8bit_pool_and_dispatch_to_the_8bit_entry_points():
         cabi.PagedKvPool(2, 2, 256, 64, "cpu", bits=2)
 
 
-def test_removed_kv_chain_names_are_rejected():
-    with pytest.raises(ValueError, match="Only qserve_deferred_split_fused_kv is retained"):
-        build_kv_chain(chain_name="qserve_fused_kv", model_config=MinimalQwenConfig(), enabled=True)
-
-
 def test_builder_and_report():
     cache = build_qserve_deferred_split_fused_kv_cache(MinimalQwenConfig(), CFG16)
     rep = cache.report()
     assert rep.group_size == 16 and rep.attention_backend == "triton_int4_split_decode"
     assert "QServeDeferredSplitFusedKvCache" in repr(cache)
-
-
-def test_fused_attention_delegates_prefill_to_the_native_forward():
-    class Attention:
-        def __init__(self) -> None:
-            self._optiz_original_forward = self.native_forward
-            self.calls = 0
-
-        def native_forward(self, hidden_states, **kwargs):
-            self.calls += 1
-            return hidden_states, kwargs
-
-    attention = Attention()
-    hidden_states = torch.randn(1, 2, 16)
-    result = _qserve_fused_forward(attention, hidden_states, position_embeddings=(torch.empty(0), torch.empty(0)),
-                                   attention_mask=None)
-    assert attention.calls == 1
-    assert result[0] is hidden_states
 
 
 def test_page_allocator_policy_matches_the_oracle():
