@@ -63,8 +63,10 @@ def parse_args(argv=None):
                     help="hybrid/serving: include the layers' output epilogues (attention * sigmoid(gate), GDN "
                          "gated RMSNorm), fused into the kernels' stores; the CPU legs run them too")
     ap.add_argument("--small", action="store_true",
-                    help="prefill workload only: a reduced case (B=4, T=8192, 2 layers, 8 decode steps) for ncu captures")
+                    help="reduced case for ncu captures: prefill B=4, T=8192, 2 layers, 8 decode steps; hybrid B=8")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="hybrid workload: skip the serving and long-context sub-records")
     return ap.parse_args(argv)
 
 
@@ -189,18 +191,19 @@ def build_stack(args, world, rank, device):
     from optiz_qwen_b200.serving import shard_by_cost
 
     if args.workload == "hybrid":
-        shape = HybridShape(batch=64, context=4096)
+        bsz = 8 if args.small else 64   # (--small: the profiling case, B = 8)
+        shape = HybridShape(batch=bsz, context=4096)
         stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv,
                                   epilogues=args.epilogues, kv_bits=args.kv_bits)
         desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
                 "epilogues": EPILOGUES if args.epilogues else "none",
-                "workload": "hybrid decode step: B=64 per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
+                "workload": f"hybrid decode step: B={bsz} per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
                             f"INT{args.kv_bits} paged KV, page 64, permuted pages), 3:1 interleave, hidden 2048",
-                "batch_per_gpu": 64, "global_batch": 64 * world, "context": 4096, "layers": 24,
+                "batch_per_gpu": bsz, "global_batch": bsz * world, "context": 4096, "layers": 24,
                 "context_held": "each step appends the new token at slot 4096 and attends over 4097",
                 "l2": "no flush: ~2 GB per-step working set > 126 MB L2", "parallelism": f"dp{world} (sequences)"}
-        return stack, 64 * world, desc
+        return stack, bsz * world, desc
     lengths = serving_lengths()
     shards = shard_by_cost(lengths, world)
     mine = [lengths[i] for i in shards[rank]]
@@ -228,6 +231,154 @@ def time_graph(graph, reps, device):
     return s.elapsed_time(e) / reps
 
 
+def ranks_gather(value: float, dist, device) -> list[float]:
+    """Every rank's value, in rank order (one all-gather; a one-element list on one process)."""
+    if dist is None:
+        return [value]
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    out = torch.empty(dist.get_world_size(), dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(out, t)
+    return out.tolist()
+
+
+def time_host_step(stack, steps, device, dist):
+    """ms per call of the host-facing step (pinned inputs -> device, kernels, outputs -> host, the
+    caller waiting for the outputs every step), max over ranks."""
+    import torch
+
+    for _ in range(3):
+        stack.step()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(steps):
+        stack.step()
+        torch.cuda.current_stream(device).synchronize()   # the caller reads the step's outputs
+    e2.record()
+    torch.cuda.synchronize(device)
+    return max_over_ranks(s2.elapsed_time(e2) / steps, dist, device)
+
+
+def time_copies_only(stack, steps, device, dist):
+    """The host-facing step's transfers alone (same copies, streams and grouping, no kernels):
+    ms per step, max over ranks.  The floor e2e cannot go below on this host."""
+    import torch
+
+    graph = stack.capture_io(kinds=())
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(steps):
+        graph.replay()
+        torch.cuda.current_stream(device).synchronize()
+    e2.record()
+    torch.cuda.synchronize(device)
+    del graph
+    return max_over_ranks(s2.elapsed_time(e2) / steps, dist, device)
+
+
+def measure_serving(args, world, rank, device, dist, hbm_peak):
+    """Batched serving (B = 1024 ragged contexts, U[256, 8192], seed 3) sharded by byte cost over the
+    ranks (strong scaling): device-timed step, per-rank spread, e2e through the host-facing step."""
+    import torch
+
+    sub = argparse.Namespace(**{**vars(args), "workload": "serving"})
+    stack, global_batch, desc = build_stack(sub, world, rank, device)
+    stack.fill_inputs()
+    counts = stack.counts()
+    graph = stack.capture()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    barrier(dist, device)
+    steps = max(10, min(args.steps, 100))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    ms_local = s.elapsed_time(e) / steps
+    per_rank = ranks_gather(ms_local, dist, device)
+    ms = max(per_rank)
+    stack.graph = graph
+    e2e_ms = time_host_step(stack, max(10, steps // 4), device, dist)
+    step_bytes = counts.attn_bytes + counts.gdn_bytes + counts.append_bytes
+    out = {"workload": desc["workload"], "global_batch": global_batch, "batch_this_rank": stack.shape.batch,
+           "scaling": "strong", "steps": steps, "ms_per_step": round(ms, 4),
+           "tokens_per_s": round(global_batch * 1000.0 / ms, 1),
+           "rank_ms": {"min": round(min(per_rank), 4), "max": round(max(per_rank), 4)},
+           "hbm_frac_rank0": round(step_bytes / ms_local / 1e6 / hbm_peak, 4),
+           "e2e": {"tokens_per_s": round(global_batch * 1000.0 / e2e_ms, 1), "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step_per_rank": counts.h2d_bytes,
+                   "d2h_bytes_per_step_per_rank": counts.d2h_bytes}}
+    del graph, stack
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_longctx(args, world, rank, device, dist, hbm_peak):
+    """Long context (B = 1, context 131072, 6 attention layers, seed 2): the KV range split across the
+    ranks, per layer the partial attention and the exchange + LSE merge, the step in a CUDA graph."""
+    import torch
+
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
+
+    length, layers = 131072, 6
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2 * 1000 + rank)
+    decs = []
+    for _ in range(layers):
+        d = ContextParallelDecoder(2, 256, rank=rank, world=world, device=device)
+        d.prefill_random(length, generator=gen, capacity_tokens=0, page_seed=2)
+        decs.append(d)
+    q = torch.randn((1, 8, 256), generator=gen, device=device).to(torch.bfloat16)
+
+    def step():
+        for d in decs:
+            d.decode(q)
+
+    # one step, NCCL all-gathers included, captured in a CUDA graph after an eager warm-up
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(device).wait_stream(side)
+    barrier(dist, device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    barrier(dist, device)
+    steps = max(10, min(args.steps, 500))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    ms = max_over_ranks(start.elapsed_time(end) / steps, dist, device)
+    kv_bytes = length * 2 * 264 * layers
+    del graph                                  # (a graph holding NCCL calls goes before the group does)
+    torch.cuda.synchronize(device)
+    return {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
+                        "KV range split evenly across GPUs, per layer partial attention + exchange of fp32 "
+                        "(out, lse) + LSE merge (one GPU: the attention kernel writes the output), step in a "
+                        "CUDA graph",
+            "scaling": "strong", "steps": steps, "ms_per_step": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 1),
+            "kv_bytes_per_step_total": kv_bytes, "GB_s_per_gpu": round(kv_bytes / world / ms / 1e6, 1),
+            "hbm_frac_per_gpu": round(kv_bytes / world / ms / 1e6 / hbm_peak, 4)}
+
+
 def run_b200(args):
     import torch
 
@@ -245,6 +396,8 @@ def run_b200(args):
         graph.replay()
     barrier(dist, device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # clocks are sampled from here through the last loaded phase (the timed loop alone is too short
+    # for nvidia-smi's sampling at small step counts)
     clocks = ClockSampler(device.index if world == 1 else local).__enter__()
     start.record()
     for _ in range(args.steps):
@@ -279,35 +432,35 @@ def run_b200(args):
 
     # end to end through the host-facing call: pinned inputs -> device -> step -> host
     stack.graph = graph
-    for _ in range(3):
-        stack.step()
-    torch.cuda.synchronize(device)
-    barrier(dist, device)
     e_steps = max(10, args.steps // 4)
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(e_steps):
-        stack.step()
-        torch.cuda.current_stream(device).synchronize()   # the caller reads the step's outputs
-    e2.record()
-    torch.cuda.synchronize(device)
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e_steps, dist, device)
+    e2e_ms = time_host_step(stack, e_steps, device, dist)
+    copy_ms = time_copies_only(stack, e_steps, device, dist)
+    del graph, stack
+    torch.cuda.empty_cache()
+
+    extra = {}
+    if args.workload == "hybrid" and not args.no_sub_records:
+        extra["serving"] = measure_serving(args, world, rank, device, dist, hbm_peak)
+        extra["longctx"] = measure_longctx(args, world, rank, device, dist, hbm_peak)
     clocks.__exit__(None, None, None)
 
     step_bytes = counts.attn_bytes + counts.gdn_bytes + counts.append_bytes
     line = {
-        "metric": METRIC if stack.kv_bits == 4 else METRIC.replace("INT4", "INT8"), "value": round(value, 1),
+        "metric": METRIC if args.kv_bits == 4 else METRIC.replace("INT4", "INT8"), "value": round(value, 1),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak" if args.workload == "hybrid" else "strong", "vs_baseline": None,
-        "dtype": (f"int{stack.kv_bits} KV codes: q.k as u8 x s8 integer MMA (q in 15-bit fixed point per head), "
-                  "p.v as fp16 MMA (P' as fp16 + fp16 remainder, codes as exact fp16 subnormals), fp32 "
-                  "softmax / accumulate; GDN fp32 state, bf16 q/k/v"),
+        "dtype": (f"int{args.kv_bits} KV codes: q.k as u8 x s8 integer MMA (q in 21-bit fixed point per head, "
+                  "three 8-bit digits), p.v as fp16 MMA (P' as fp16 + fp16 remainder, codes as exact fp16 "
+                  "subnormals), fp32 softmax / accumulate; GDN fp32 state, bf16 q/k/v"),
         "data": "synthetic, seeded (config-0 distributions)", "config": desc,
         "clocks": clocks.summary(),
         "e2e": {"value": round(global_batch * 1000.0 / e2e_ms, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": counts.h2d_bytes, "d2h_bytes_per_step": counts.d2h_bytes,
-                "ms_per_step": round(e2e_ms, 4)},
+                "h2d_bytes_per_step": counts.h2d_bytes * world, "d2h_bytes_per_step": counts.d2h_bytes * world,
+                "ms_per_step": round(e2e_ms, 4),
+                # the same transfers with no kernels: what the host's copy bandwidth allows
+                "copies_only_ms_per_step": round(copy_ms, 4),
+                "host_GB_s_copies_only": round((counts.h2d_bytes + counts.d2h_bytes) * world / copy_ms / 1e6, 1)},
         "gpu_launches": counts.launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": dk["GB_s"], "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(dk["GB_s"] / hbm_peak, 4),
@@ -318,12 +471,16 @@ def run_b200(args):
         "kernels": kernels,
         "step_hbm": {"bytes_per_step_per_gpu": step_bytes, "GB_s": round(step_bytes / ms_local / 1e6, 1),
                      "frac": round(step_bytes / ms_local / 1e6 / hbm_peak, 4)},
+        **extra,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(stack.shape, args.cpu_seconds, args.epilogues, bits=stack.kv_bits)
+        from optiz_qwen_b200.hybrid import HybridShape
+
+        shape = HybridShape(batch=64, context=4096) if args.workload == "hybrid" else HybridShape(
+            batch=1024, context=serving_lengths())
+        line["cpu_baseline"] = cpu_baseline(shape, args.cpu_seconds, args.epilogues, bits=args.kv_bits)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, stack
     if dist is not None:
         dist.destroy_process_group()
 
@@ -332,7 +489,8 @@ def run_b200(args):
 class OracleStep:
     """The oracle (numpy restatement of the reference's CPU torch path) over a sample of sequences:
     per attention layer the reference quantiser on the new token, dequantisation of the whole
-    INT4 cache and fp32 attention; per GDN layer the recurrent gated delta rule."""
+    INT4 cache and fp32 attention; per GDN layer the decode branch's gate arithmetic and the
+    recurrent gated delta rule."""
 
     def __init__(self, shape, seqs: int, layer_fraction: float = 1.0, seed: int = 0, epilogues: bool = False,
                  bits: int = 4):
@@ -355,8 +513,10 @@ class OracleStep:
         self.knew = rng.standard_normal((1, hkv, 1, d)).astype(np.float32)
         self.state = (0.02 * rng.standard_normal((1, h, dk, dk))).astype(np.float32)
         self.gq = rng.standard_normal((1, 1, h, dk)).astype(np.float32)
-        self.gg = -np.logaddexp(0, rng.standard_normal((1, 1, h))).astype(np.float32)
-        self.gb = (1 / (1 + np.exp(-rng.standard_normal((1, 1, h))))).astype(np.float32)
+        # raw gate projections; A_log = dt_bias = 0 as in the GPU stack (g = -softplus(a))
+        self.ga = rng.standard_normal((1, 1, h)).astype(np.float32)
+        self.gbr = rng.standard_normal((1, 1, h)).astype(np.float32)
+        self.gparam = np.zeros(h, np.float32)
         self.gate = rng.standard_normal((1, shape.num_heads, d)).astype(np.float32)
         self.z = rng.standard_normal((1, 1, h, dk)).astype(np.float32)
         self.norm_w = (1.0 + 0.1 * rng.standard_normal(dk)).astype(np.float32)
@@ -377,7 +537,8 @@ class OracleStep:
             if self.epilogues:
                 ep.sigmoid_gate(o, self.gate, rnd=kq.round_bf16)
         for _ in range(self.n_gdn):
-            o, _ = ogdn.recurrent_gated_delta_rule(self.gq, self.gq, self.gq, self.gg, self.gb, self.state, True, True)
+            g, beta = ogdn.decay_gates(self.ga, self.gbr, self.gparam, self.gparam, rnd=kq.round_bf16)
+            o, _ = ogdn.recurrent_gated_delta_rule(self.gq, self.gq, self.gq, g, beta, self.state, True, True)
             if self.epilogues:
                 ep.rmsnorm_gated(kq.round_bf16(o), self.z, self.norm_w, 1e-6, rnd=kq.round_bf16)
 
@@ -451,71 +612,26 @@ def run_reference(args):
 
 
 def run_longctx(args):
-    """Config 2: one sequence at context 131072, 6 attention layers, KV range split across the ranks;
-    per layer: append on the tail rank, partial attention, NCCL all-gather of (out, lse), LSE merge."""
+    """Config 2 on its own (``--workload longctx``): one sequence at context 131072, 6 attention
+    layers, KV range split across the ranks."""
     import torch
-
-    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
 
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist = init_pg(world, local)
     hbm_peak, peak_src = peaks()
-    length, layers = 131072, 6
-    gen = torch.Generator(device=device)
-    gen.manual_seed(2 * 1000 + rank)
-    decs = []
-    for _ in range(layers):
-        d = ContextParallelDecoder(2, 256, rank=rank, world=world, device=device)
-        d.prefill_random(length, generator=gen, capacity_tokens=0, page_seed=2)
-        decs.append(d)
-    q = torch.randn((1, 8, 256), generator=gen, device=device).to(torch.bfloat16)
-
-    def step():
-        for d in decs:
-            d.decode(q)
-
-    # one step, NCCL all-gathers included, captured in a CUDA graph after an eager warm-up
-    side = torch.cuda.Stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(side):
-        for _ in range(2):
-            step()
-    torch.cuda.current_stream(device).wait_stream(side)
-    barrier(dist, device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=side):
-        step()
-    for _ in range(max(3, args.warmup)):
-        graph.replay()
-    barrier(dist, device)
-    steps = max(10, min(args.steps, 500))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        graph.replay()
-    end.record()
-    torch.cuda.synchronize(device)
-    barrier(dist, device)
-    ms = max_over_ranks(start.elapsed_time(end) / steps, dist, device)
-    kv_bytes = length * 2 * 264 * layers
-    line = {"metric": METRIC, "value": round(1000.0 / ms, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int4 KV codes: q.k as u8 x s8 integer MMA, p.v as fp16 MMA; fp32 "
-                                          "softmax / merge",
-            "data": "synthetic, seeded",
-            "config": {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
-                                   "KV range split evenly across GPUs, NCCL all-gather of fp32 (out, lse) partials "
-                                   "+ LSE merge per layer (one GPU: the attention kernel writes the output, no "
-                                   "exchange), step captured in a CUDA graph", "global_batch": 1},
-            "step_hbm": {"kv_bytes_per_step_total": kv_bytes,
-                         "GB_s_per_gpu": round(kv_bytes / world / ms / 1e6, 1),
-                         "frac_per_gpu": round(kv_bytes / world / ms / 1e6 / hbm_peak, 4), "peak_source": peak_src}}
+    rec = measure_longctx(args, world, rank, device, dist, hbm_peak)
+    line = {"metric": METRIC, "value": rec["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": rec["steps"], "warmup": args.warmup, "ms_per_step": rec["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 KV codes: q.k as u8 x s8 integer MMA, p.v as fp16 MMA; fp32 softmax / merge",
+            "data": "synthetic, seeded", "config": {"workload": rec["workload"], "global_batch": 1},
+            "step_hbm": {"kv_bytes_per_step_total": rec["kv_bytes_per_step_total"],
+                         "GB_s_per_gpu": rec["GB_s_per_gpu"], "frac_per_gpu": rec["hbm_frac_per_gpu"],
+                         "peak_source": peak_src}}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph                                  # release the graph holding NCCL calls first
-    torch.cuda.synchronize(device)
     if dist is not None:
         dist.destroy_process_group()
 

@@ -295,6 +295,24 @@ int oq_gdn_recurrent(
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
     float scale, int use_qk_l2norm, int flags, int32_t* device_status, void* stream);
 
+/* oq_gdn_recurrent with the layer's gate arithmetic fused in: instead of g and beta it
+ * takes the raw projections a, b [batch, seq_len, num_heads] (contiguous, ab_dtype) and the
+ * layer's A_log and dt_bias [num_heads] (their own dtypes), and computes per token, as the
+ * decode branch of Qwen3_5GatedDeltaNet.forward does before calling the hook (transformers
+ * models/qwen3_5/modeling_qwen3_5.py:492-493): beta = sigmoid(b) rounded to ab_dtype, and in
+ * fp32 g = -exp(A_log) * softplus(a + dt_bias) (softplus(x) = x for x > 20).  The rest of
+ * the contract is oq_gdn_recurrent's. */
+int oq_gdn_recurrent_gates(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* a, const void* b, int ab_dtype, const void* a_log, int a_log_dtype, const void* dt_bias,
+    int dt_bias_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, int32_t* device_status, void* stream);
+
 /* oq_gdn_recurrent with the GDN layer's output norm fused in:
  * out = Qwen3_5RMSNormGated(o, z) per head (transformers models/qwen3_5/modeling_qwen3_5.py:175-190,
  * applied at :527-529) = rnd(rnd(rnd(o * rsqrt(mean(o^2) + norm_eps)) * w) * silu(z)), with o

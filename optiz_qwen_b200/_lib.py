@@ -56,6 +56,9 @@ SIGNATURES = {
     "oq_gather_dequant_int8": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32, p, p]),
+    "oq_gdn_recurrent_gates": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                     p, p, i32, p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32, i32,
+                                     p, p]),
     "oq_debug_set_wait_polls": (i32, [i32]),
     "oq_gdn_recurrent_norm": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                     p, i32, p, i32, p, p, p, i64, i64, i64, i64, i64, f32, i32,

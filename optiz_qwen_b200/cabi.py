@@ -310,6 +310,45 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
     return out
 
 
+def gdn_recurrent_gates(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                        A_log: torch.Tensor, dt_bias: torch.Tensor, *, scale: float | None = None,
+                        initial_state: torch.Tensor | None = None, final_state: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None, use_qk_l2norm: bool = False, prefetch_state: bool = False,
+                        device_status: torch.Tensor | None = None) -> torch.Tensor:
+    """:func:`gdn_recurrent` with the layer's gate arithmetic in the kernel (``oq_gdn_recurrent_gates``):
+    from the raw projections ``a``, ``b`` ``[B, T, H]`` and the layer's ``A_log``, ``dt_bias`` ``[H]``
+    it computes ``beta = sigmoid(b)`` (in b's dtype) and ``g = -exp(A_log) * softplus(a + dt_bias)``
+    in fp32, as Qwen3_5GatedDeltaNet's decode branch does before calling the hook
+    (transformers models/qwen3_5/modeling_qwen3_5.py:492-493)."""
+    require_cuda(q, k, v, a, b, A_log, dt_bias, initial_state, final_state)
+    if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError("q, k must be [B, T, H, Dk] and v [B, T, H, Dv]")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    bsz, t, h, dk = q.shape
+    dv = v.shape[-1]
+    q, k, v = (x if x.stride(3) == 1 else x.contiguous() for x in (q, k, v))
+    a, b = a.contiguous(), b.contiguous()
+    if tuple(a.shape) != (bsz, t, h) or b.shape != a.shape or a.dtype != b.dtype:
+        raise ValueError("a and b must be [B, T, H] of one dtype")
+    A_log, dt_bias = A_log.contiguous(), dt_bias.contiguous()
+    if A_log.numel() != h or dt_bias.numel() != h:
+        raise ValueError("A_log and dt_bias must have one value per head")
+    for s in (initial_state, final_state):
+        if s is not None and (s.dtype != torch.float32 or tuple(s.shape) != (bsz, h, dk, dv) or not s.is_contiguous()):
+            raise ValueError("states must be contiguous fp32 [B, H, Dk, Dv]")
+    if out is None:
+        out = torch.empty((bsz, t, h, dv), dtype=q.dtype, device=q.device)
+    scale = dk ** -0.5 if scale is None else float(scale)
+    call("oq_gdn_recurrent_gates", ptr(q), ptr(k), ptr(v), dtype_code(q.dtype),
+         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+         v.stride(0), v.stride(1), v.stride(2),
+         ptr(a), ptr(b), dtype_code(a.dtype), ptr(A_log), dtype_code(A_log.dtype), ptr(dt_bias),
+         dtype_code(dt_bias.dtype), ptr(initial_state), ptr(final_state), ptr(out), bsz, t, h, dk, dv, float(scale),
+         int(use_qk_l2norm), GDN_STATE_PREFETCH if prefetch_state else 0, ptr(device_status), stream_ptr(q.device))
+    return out
+
+
 GDN_STATE_PREFETCH = 1
 CHUNK_SIZE = 64
 

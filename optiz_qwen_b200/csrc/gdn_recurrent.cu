@@ -62,7 +62,36 @@ struct GdnParams {
   int* norm_counters;  // [B * H] zeroed; every launch leaves them zero
   int32_t* status_word;  // OQ_DEV_* bits of the shared-memory kernel's bounded wait (may be null)
   int wait_polls;        // polls of that wait (wait_polls() at launch)
+  // raw gate inputs (oq_gdn_recurrent_gates; null: g and beta are given): a, b [B, T, H] in
+  // ab_dtype, A_log and dt_bias [H]
+  const void *gate_a, *gate_b, *a_log, *dt_bias;
+  int ab_dtype, a_log_dtype, dt_bias_dtype;
 };
+
+__device__ __forceinline__ float round_to(int dtype, float x) {
+  if (dtype == OQ_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  if (dtype == OQ_F16) return __half2float(__float2half_rn(x));
+  return x;
+}
+
+// The token's decay exponent g and write strength beta.  Given directly, or from the layer's
+// raw projections as Qwen3_5GatedDeltaNet.forward computes them (transformers
+// models/qwen3_5/modeling_qwen3_5.py:492-493): beta = sigmoid(b) in b's dtype, and in fp32
+// g = -exp(A_log) * softplus(a + dt_bias), softplus(x) = x above 20 (torch's threshold),
+// else log(1 + exp(x)).
+__device__ __forceinline__ void step_gates(const GdnParams& p, int64_t gi, int64_t h, float& g, float& beta) {
+  if (p.gate_a == nullptr) {
+    g = load_as_float(p.g, p.g_dtype, gi);
+    beta = load_as_float(p.beta, p.beta_dtype, gi);
+    return;
+  }
+  const float bv = load_as_float(p.gate_b, p.ab_dtype, gi);
+  const float x = load_as_float(p.gate_a, p.ab_dtype, gi) + load_as_float(p.dt_bias, p.dt_bias_dtype, h);
+  const float a_log = load_as_float(p.a_log, p.a_log_dtype, h);
+  beta = round_to(p.ab_dtype, 1.0f / (1.0f + expf(-bv)));
+  const float softplus = x > 20.0f ? x : log1pf(expf(x));
+  g = -expf(a_log) * softplus;
+}
 
 constexpr int kConvWidth = 4;  // state width = kernel size = 4 (Qwen3.5's conv_kernel_size)
 
@@ -176,8 +205,8 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(GdnParams p) {
       }
     }
     const int64_t gi = (b * p.seq_len + t) * H + h;
-    const float gt = load_as_float(p.g, p.g_dtype, gi);
-    const float bt = load_as_float(p.beta, p.beta_dtype, gi);
+    float gt, bt;
+    step_gates(p, gi, h, gt, bt);
     __syncthreads();
 
     float inv_q = 1.0f, inv_k = 1.0f;
@@ -382,8 +411,8 @@ __global__ void __launch_bounds__(kThreads, 10) gdn_smem_kernel(const __grid_con
       }
     }
     const int64_t gi = (b * p.seq_len + t) * H + h;
-    const float gt = load_as_float(p.g, p.g_dtype, gi);
-    const float bt = load_as_float(p.beta, p.beta_dtype, gi);
+    float gt, bt;
+    step_gates(p, gi, h, gt, bt);
     if (!landed) {
       // thread 0 initialised the barrier; every thread sees that before it polls it
       __syncthreads();
@@ -516,6 +545,16 @@ cudaError_t launch_gdn_cluster(void (*kernel)(GdnParams), dim3 grid, cudaStream_
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+// Raw gate inputs of oq_gdn_recurrent_gates (null: g and beta are given).
+struct RawGates {
+  const void *a, *b;
+  int ab_dtype;
+  const void* a_log;
+  int a_log_dtype;
+  const void* dt_bias;
+  int dt_bias_dtype;
+};
+
 // Gated RMSNorm epilogue arguments (null: plain output).
 struct NormArgs {
   const void* z;
@@ -600,8 +639,18 @@ int gdn_recurrent_impl(
     const void* g, int g_dtype, const void* beta, int beta_dtype,
     const float* initial_state, float* final_state, void* out,
     int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
-    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, int32_t* device_status, void* stream) {
+    float scale, int use_qk_l2norm, const NormArgs* norm, int flags, int32_t* device_status, void* stream,
+    const RawGates* raw = nullptr) {
   if (int st = check_norm(norm, batch, num_heads, "gdn_recurrent"); st != OQ_OK) return st;
+  if (raw) {
+    if (!valid_dtype(raw->ab_dtype) || !valid_dtype(raw->a_log_dtype) || !valid_dtype(raw->dt_bias_dtype)) {
+      return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent_gates: unknown dtype");
+    }
+    if (!raw->a || !raw->b || !raw->a_log || !raw->dt_bias) {
+      return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_recurrent_gates: null gate input");
+    }
+    g_dtype = beta_dtype = OQ_F32;  // (unused)
+  }
   if (!valid_dtype(qkv_dtype) || !valid_dtype(g_dtype) || !valid_dtype(beta_dtype)) {
     return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: unknown dtype");
   }
@@ -609,7 +658,7 @@ int gdn_recurrent_impl(
   if (batch < 0 || seq_len < 0 || num_heads <= 0) return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_recurrent: bad sizes");
   if (batch == 0) return ok();
   if (batch > 65535 || num_heads > 65535) return fail(OQ_ERR_UNSUPPORTED, "gdn_recurrent: grid too large");
-  if (!g || !beta || (seq_len > 0 && (!q || !k || !v || !out))) {
+  if ((!raw && (!g || !beta)) || (seq_len > 0 && (!q || !k || !v || !out))) {
     return fail(OQ_ERR_INVALID_ARGUMENT, "gdn_recurrent: null pointer");
   }
   if ((initial_state && reinterpret_cast<uintptr_t>(initial_state) % 16) ||
@@ -637,6 +686,15 @@ int gdn_recurrent_impl(
   p.prefetch_state = (flags & OQ_GDN_STATE_PREFETCH) != 0;
   p.status_word = device_status;
   p.wait_polls = wait_polls();
+  if (raw) {
+    p.gate_a = raw->a;
+    p.gate_b = raw->b;
+    p.ab_dtype = raw->ab_dtype;
+    p.a_log = raw->a_log;
+    p.a_log_dtype = raw->a_log_dtype;
+    p.dt_bias = raw->dt_bias;
+    p.dt_bias_dtype = raw->dt_bias_dtype;
+  }
   set_norm(p, norm);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (norm == nullptr && initial_state != nullptr && batch * num_heads * kDk < (int64_t(1) << 31)) {
@@ -724,6 +782,23 @@ extern "C" int oq_gdn_recurrent(
                                 k_stride_h, v_stride_b, v_stride_t, v_stride_h, g, g_dtype, beta, beta_dtype,
                                 initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
                                 use_qk_l2norm, nullptr, flags, device_status, stream);
+}
+
+extern "C" int oq_gdn_recurrent_gates(
+    const void* q, const void* k, const void* v, int qkv_dtype,
+    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+    const void* a, const void* b, int ab_dtype, const void* a_log, int a_log_dtype, const void* dt_bias,
+    int dt_bias_dtype,
+    const float* initial_state, float* final_state, void* out,
+    int64_t batch, int64_t seq_len, int64_t num_heads, int64_t k_dim, int64_t v_dim,
+    float scale, int use_qk_l2norm, int flags, int32_t* device_status, void* stream) {
+  const oq::RawGates raw = {a, b, ab_dtype, a_log, a_log_dtype, dt_bias, dt_bias_dtype};
+  return oq::gdn_recurrent_impl(q, k, v, qkv_dtype, q_stride_b, q_stride_t, q_stride_h, k_stride_b, k_stride_t,
+                                k_stride_h, v_stride_b, v_stride_t, v_stride_h, nullptr, OQ_F32, nullptr, OQ_F32,
+                                initial_state, final_state, out, batch, seq_len, num_heads, k_dim, v_dim, scale,
+                                use_qk_l2norm, nullptr, flags, device_status, stream, &raw);
 }
 
 extern "C" int oq_gdn_recurrent_norm(

@@ -74,8 +74,12 @@ class _GdnLayer:
     q: torch.Tensor = None           # ... or q / k / v after the conv
     k: torch.Tensor = None
     v: torch.Tensor = None
-    g: torch.Tensor = None
-    beta: torch.Tensor = None
+    g: torch.Tensor = None           # fp32 [B, 1, H] decay exponent ...
+    beta: torch.Tensor = None        # ... and write strength, precomputed (conv variants), or
+    a: torch.Tensor = None           # the raw projections [B, 1, H] the step turns into g and beta
+    b: torch.Tensor = None
+    A_log: torch.Tensor = None       # [H] layer parameters of that gate arithmetic
+    dt_bias: torch.Tensor = None
     z: torch.Tensor = None           # [B, 1, H, Dv] gate of the output norm (with epilogues)
     norm_w: torch.Tensor = None      # [Dv] weight of the output norm
     out: torch.Tensor = None
@@ -105,6 +109,10 @@ class HybridDecodeStack:
     ``"fused"`` the single-launch ``oq_gdn_conv_step`` (slower on B200, measured: the four
     column-slice CTAs of a head each convolve q/k and synchronise as a cluster).  With
     ``conv=None`` q/k/v are given post-conv.
+    Without a conv mode each GDN layer takes its raw gate projections ``a``, ``b`` and computes
+    ``g = -exp(A_log) softplus(a + dt_bias)``, ``beta = sigmoid(b)`` inside the step kernel
+    (``oq_gdn_recurrent_gates``), as the decode branch does ahead of the hook; the conv modes
+    take g and beta precomputed.
     ``epilogues=True`` adds the layers' output epilogues: the attention output gate
     ``* sigmoid(gate)`` (q_proj's second half), fused into the attention kernel's store, and
     the GDN output norm ``Qwen3_5RMSNormGated(o, z)`` (z = the z projection) as the
@@ -149,6 +157,9 @@ class HybridDecodeStack:
                 state = torch.randn((b, shape.gdn_heads, shape.gdn_dim, shape.gdn_dim), generator=self.gen,
                                     device=self.device, dtype=torch.float32).mul_(0.02)
                 layer = _GdnLayer(state=state)
+                if not conv:  # A = exp(A_log) = 1 and dt_bias = 0: g = -softplus(a), a ~ N(0, 1)
+                    layer.A_log = torch.zeros(shape.gdn_heads, dtype=dtype, device=self.device)
+                    layer.dt_bias = torch.zeros(shape.gdn_heads, dtype=dtype, device=self.device)
                 if epilogues:
                     layer.norm_w = (1.0 + 0.1 * torch.randn(shape.gdn_dim, generator=self.gen,
                                                             device=self.device)).to(dtype)
@@ -227,10 +238,13 @@ class HybridDecodeStack:
                                                           device=self.device))
                 else:
                     in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp)]
-                in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
-                # g stays fp32 (the module computes it in fp32): its bits take two 16-bit slots
-                # per value inside the layer's input range, so the layer's inputs are one copy
-                in_specs += [(("gdn", i, "g_bits"), (b * s.gdn_heads * 4 // self._esize,))]
+                if self.conv:
+                    in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
+                    # g stays fp32 (the module computes it in fp32): its bits take two 16-bit slots
+                    # per value inside the layer's input range, so the layer's inputs are one copy
+                    in_specs += [(("gdn", i, "g_bits"), (b * s.gdn_heads * 4 // self._esize,))]
+                else:
+                    in_specs += [(("gdn", i, "a"), (b, 1, s.gdn_heads)), (("gdn", i, "b"), (b, 1, s.gdn_heads))]
                 if self.epilogues:
                     in_specs += [(("gdn", i, "z"), shp)]
                 out_specs += [(("gdn", i, "out"), shp)]
@@ -276,7 +290,8 @@ class HybridDecodeStack:
             gh.copy_(-torch.nn.functional.softplus(torch.randn(gh.shape, generator=gen)))
         self.in_dev.copy_(self.in_host)
         for layer in self.gdn:
-            layer.beta.copy_(torch.sigmoid(layer.beta.float()).to(self.dtype))
+            if layer.beta is not None:
+                layer.beta.copy_(torch.sigmoid(layer.beta.float()).to(self.dtype))
         self.in_host.copy_(self.in_dev)
 
     # ------------------------------------------------------------------ the step
@@ -321,9 +336,9 @@ class HybridDecodeStack:
                     cabi.gdn_recurrent(q, k, v, layer.g, layer.beta, initial_state=layer.state,
                                        final_state=layer.state, out=layer.out, use_qk_l2norm=True)
                 else:
-                    cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
-                                       final_state=layer.state, out=layer.out, use_qk_l2norm=True,
-                                       prefetch_state=chained)
+                    cabi.gdn_recurrent_gates(layer.q, layer.k, layer.v, layer.a, layer.b, layer.A_log,
+                                             layer.dt_bias, initial_state=layer.state, final_state=layer.state,
+                                             out=layer.out, use_qk_l2norm=True, prefetch_state=chained)
                 if layer.z is not None:
                     cabi.rmsnorm_gated(layer.out, layer.z, layer.norm_w, 1e-6, out=layer.out)
                 prev = ("gdn", i)
@@ -341,7 +356,7 @@ class HybridDecodeStack:
             self.step_device(kinds)
         return graph
 
-    def capture_io(self) -> torch.cuda.CUDAGraph:
+    def capture_io(self, kinds=("attn", "gdn", "append")) -> torch.cuda.CUDAGraph:
         """The host-facing step as one graph with its transfers: a copy stream brings the
         inputs (and g) from the pinned host buffers in layer order, in groups of 1, 2, 4, 8,
         ... layers (one copy per group; a layer's launches wait for its group), and a second
@@ -350,11 +365,12 @@ class HybridDecodeStack:
         later layers run under the kernels of earlier ones.  (Measured at B = 64: host-to-
         device copies slow to about a third of their idle rate while the step's kernels load
         HBM, so the compute can catch up with them; growing groups beat one copy per layer,
-        and splitting the copies over more streams is slower.)"""
+        and splitting the copies over more streams is slower.)  ``kinds=()`` keeps the transfers
+        and drops the kernels (a measure of what the host's copies alone cost)."""
         dev = self.device
         self.stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.stream):  # eager warm-up of the launches
-            self.step_device()
+            self.step_device(kinds)
         torch.cuda.current_stream(dev).wait_stream(self.stream)
         copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         graph = torch.cuda.CUDAGraph()
@@ -401,7 +417,7 @@ class HybridDecodeStack:
                     self.out_host[lo:hi].copy_(self.out_dev[lo:hi], non_blocking=True)
                 pending.clear()
 
-            self.step_device(before=before, after=after)
+            self.step_device(kinds, before=before, after=after)
             main.wait_stream(copy_in)
             main.wait_stream(copy_out)
         return graph

@@ -27,6 +27,25 @@ def l2norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
     return (x * inv).astype(np.float32)
 
 
+def decay_gates(a, b, a_log, dt_bias, rnd=None):
+    """The decode branch's gate arithmetic (modeling_qwen3_5.py:492-493), ahead of the hook call.
+
+    ``beta = b.sigmoid()`` in b's dtype (``rnd`` rounds to it; None: fp32) and, in fp32,
+    ``g = -exp(A_log) * softplus(a + dt_bias)`` with torch's softplus (threshold 20: the
+    identity above it).  ``a``, ``b`` ``[B, T, H]``; ``a_log``, ``dt_bias`` ``[H]``.
+    Returns ``(g, beta)`` as float32.
+    """
+    a, b, a_log, dt_bias = (np.asarray(x, np.float32) for x in (a, b, a_log, dt_bias))
+    beta = (np.float32(1.0) / (np.float32(1.0) + np.exp(-b))).astype(np.float32)
+    if rnd is not None:
+        beta = rnd(beta)
+    x = (a + dt_bias).astype(np.float32)
+    with np.errstate(over="ignore"):
+        softplus = np.where(x > np.float32(20.0), x, np.log1p(np.exp(x))).astype(np.float32)
+    g = (-np.exp(a_log) * softplus).astype(np.float32)
+    return g, beta
+
+
 def recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None, output_final_state=True,
                                use_qk_l2norm_in_kernel=False, scale=None):
     """modeling_qwen3_5.py:314-353 in fp32.

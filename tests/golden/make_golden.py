@@ -163,11 +163,31 @@ def make_epilogue(torch):
     np.savez_compressed(HERE / "epilogue_golden.npz", **out)
 
 
+def make_gates(torch):
+    """The GDN decode branch's gate arithmetic ahead of the hook (transformers
+    modeling_qwen3_5.py:492-493), on bf16 projections and bf16 parameters as a bf16 model
+    holds them: ``beta = b.sigmoid()``, ``g = -A_log.float().exp() * F.softplus(a.float() + dt_bias)``."""
+    import torch.nn.functional as F
+
+    rng = np.random.default_rng(6)
+    bsz, t, h = 4, 3, 16
+    a = torch.from_numpy(3.0 * rng.standard_normal((bsz, t, h), dtype=np.float32)).to(torch.bfloat16)
+    b = torch.from_numpy(3.0 * rng.standard_normal((bsz, t, h), dtype=np.float32)).to(torch.bfloat16)
+    a[0, 0, :4] = torch.tensor([25.0, -30.0, 19.5, 0.0])          # softplus threshold and tails
+    A_log = torch.log(torch.from_numpy(rng.uniform(1.0, 16.0, h).astype(np.float32))).to(torch.bfloat16)
+    dt_bias = torch.ones(h, dtype=torch.bfloat16) + 0.1 * torch.from_numpy(
+        rng.standard_normal(h, dtype=np.float32)).to(torch.bfloat16)
+    beta = b.sigmoid()
+    g = -A_log.float().exp() * F.softplus(a.float() + dt_bias)
+    np.savez_compressed(HERE / "gates_golden.npz", a=_bf16_bits(a), b=_bf16_bits(b), A_log=_bf16_bits(A_log),
+                        dt_bias=_bf16_bits(dt_bias), beta=_bf16_bits(beta), g=g.numpy().astype(np.float32))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True,
                     help="checkout of the reference project (its src/ holds the optiz_qwen package)")
-    ap.add_argument("--only", choices=["quant", "attention", "gdn", "epilogue"], default=None,
+    ap.add_argument("--only", choices=["quant", "attention", "gdn", "epilogue", "gates"], default=None,
                     help="regenerate one fixture file only")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
@@ -184,6 +204,8 @@ def main() -> None:
         make_gdn(torch)
     if args.only in (None, "epilogue"):
         make_epilogue(torch)
+    if args.only in (None, "gates"):
+        make_gates(torch)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

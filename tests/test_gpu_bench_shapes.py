@@ -26,6 +26,16 @@ from tests._util import (assert_attn_close, assert_gdn_close, oracle_attention, 
 
 pytestmark = pytest.mark.gpu
 
+
+def _gates(layer):
+    """g and beta of a GDN layer of the stack: given, or (raw-gate layers) the oracle of the
+    decode branch's gate arithmetic on the layer's a, b, A_log and dt_bias."""
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    if layer.g is not None:
+        return f(layer.g), f(layer.beta)
+    return ogdn.decay_gates(f(layer.a), f(layer.b), f(layer.A_log), f(layer.dt_bias), rnd=kq.round_bf16)
+
+
 SCALING = 256 ** -0.5
 
 
@@ -57,7 +67,7 @@ def test_hybrid_step_b64_ctx4096_sampled():
     for i in gdn_layers:
         layer = stack.gdn[i]
         ro, rs = ogdn.recurrent_gated_delta_rule(f(layer.q)[rows], f(layer.k)[rows], f(layer.v)[rows],
-                                                 f(layer.g)[rows], f(layer.beta)[rows], states0[i], True, True)
+                                                 *(x[rows] for x in _gates(layer)), states0[i], True, True)
         assert_gdn_close(layer.state[rows].cpu().numpy(), rs)
         got = f(layer.out)[rows]
         assert np.all(np.abs(got - ro) <= 2.0 ** -8 * np.abs(ro) + 1e-4 * np.abs(ro).max())

@@ -109,3 +109,32 @@ def test_strided_qkv_views():
     torch.cuda.synchronize()
     assert_gdn_close(out.cpu().numpy(), ref_o)
     assert_gdn_close(s.cpu().numpy(), ref_s)
+
+
+def test_fused_gates_match_transformers_gate_arithmetic():
+    """oq_gdn_recurrent_gates: g and beta from the raw projections inside the kernel, against the
+    oracle of transformers' gate lines (golden-pinned) followed by the recurrence."""
+    from optiz_qwen_b200.cabi import gdn_recurrent, gdn_recurrent_gates
+
+    gold = np.load(GOLD.replace("gdn_golden", "gates_golden"))
+    f = kq.bf16_bits_to_f32
+    a, b, a_log, dt_bias = (f(gold[k]) for k in ("a", "b", "A_log", "dt_bias"))
+    bsz, t, h = a.shape
+    rng = np.random.default_rng(8)
+    q, k, v, _, _, s0 = _config0_inputs(rng, b=bsz, t=t, h=h)
+    g_ref, beta_ref = gdn.decay_gates(a, b, a_log, dt_bias, rnd=kq.round_bf16)
+    ro, rs = gdn.recurrent_gated_delta_rule(q, k, v, g_ref, beta_ref, s0, True, True)
+    bf = lambda x: _t(x, torch.bfloat16)  # noqa: E731
+    s = _t(s0)
+    out = gdn_recurrent_gates(_t(q), _t(k), _t(v), bf(a), bf(b), bf(a_log), bf(dt_bias), initial_state=s,
+                              final_state=s, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), ro)
+    assert_gdn_close(s.cpu().numpy(), rs)
+    # the same step with g / beta precomputed by the oracle agrees to fp32 rounding of the gates
+    s2 = _t(s0)
+    out2 = gdn_recurrent(_t(q), _t(k), _t(v), _t(g_ref), _t(beta_ref), initial_state=s2, final_state=s2,
+                         use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_gdn_close(out.cpu().numpy(), out2.cpu().numpy(), rtol=1e-5)
+    assert_gdn_close(s.cpu().numpy(), s2.cpu().numpy(), rtol=1e-5)

@@ -19,6 +19,15 @@ from tests._util import assert_attn_close, assert_gdn_close, oracle_attention
 pytestmark = pytest.mark.gpu
 
 
+def _gates(layer):
+    """g and beta of a GDN layer of the stack: given, or (raw-gate layers) the oracle of the
+    decode branch's gate arithmetic on the layer's a, b, A_log and dt_bias."""
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    if layer.g is not None:
+        return f(layer.g), f(layer.beta)
+    return ogdn.decay_gates(f(layer.a), f(layer.b), f(layer.A_log), f(layer.dt_bias), rnd=kq.round_bf16)
+
+
 def test_graph_step_matches_oracle():
     from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
 
@@ -35,7 +44,7 @@ def test_graph_step_matches_oracle():
 
     f = lambda t: t.float().cpu().numpy()  # noqa: E731
     for layer, s0 in zip(stack.gdn, states0):
-        ro, rs = ogdn.recurrent_gated_delta_rule(f(layer.q), f(layer.k), f(layer.v), f(layer.g), f(layer.beta), s0,
+        ro, rs = ogdn.recurrent_gated_delta_rule(f(layer.q), f(layer.k), f(layer.v), *_gates(layer), s0,
                                                  True, True)
         assert_gdn_close(layer.state.cpu().numpy(), rs)
         got = f(layer.out)
@@ -86,7 +95,7 @@ def test_graph_step_with_conv_matches_conv_then_recurrence(conv):
                                                        silu=True)[:, :, 0])
         b = conv.shape[0]
         q, k, v = (conv[:, i * h * d:(i + 1) * h * d].reshape(b, 1, h, d) for i in range(3))
-        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, f(layer.g), f(layer.beta), s0, True, True)
+        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, *_gates(layer), s0, True, True)
         assert np.array_equal(f(layer.conv_state), cst)
         assert_gdn_close(layer.state.cpu().numpy(), rs)
         got = f(layer.out)
@@ -124,7 +133,7 @@ def test_graph_step_with_epilogues(conv):
             q, k, v = (y[:, i * h * d:(i + 1) * h * d].reshape(b, 1, h, d) for i in range(3))
         else:
             q, k, v = f(layer.q), f(layer.k), f(layer.v)
-        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, f(layer.g), f(layer.beta), s0, True, True)
+        ro, rs = ogdn.recurrent_gated_delta_rule(q, k, v, *_gates(layer), s0, True, True)
         assert_gdn_close(layer.state.cpu().numpy(), rs)
         ref = ep.rmsnorm_gated(kq.round_bf16(ro), f(layer.z), f(layer.norm_w), 1e-6, rnd=kq.round_bf16)
         got = f(layer.out)

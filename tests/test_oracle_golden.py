@@ -171,3 +171,13 @@ def test_int8_token_format_matches_the_reference_quantiser(quant):
     assert cache.kv_codes.shape[-1] == 256
     k, v = cache.gather(0)
     assert k.shape == (2, 70, 256) and v.shape == (2, 70, 256)
+
+
+def test_decay_gates_match_transformers():
+    """The decode branch's g / beta (transformers modeling_qwen3_5.py:492-493) on bf16 inputs:
+    beta bit-exact in bf16 (torch rounds sigmoid to b's dtype), g within a few fp32 ulps."""
+    gold = np.load(GOLD / "gates_golden.npz")
+    f = kq.bf16_bits_to_f32
+    g, beta = ogdn.decay_gates(f(gold["a"]), f(gold["b"]), f(gold["A_log"]), f(gold["dt_bias"]), rnd=kq.round_bf16)
+    assert np.array_equal(kq.f32_to_bf16_bits(beta), gold["beta"])
+    np.testing.assert_allclose(g, gold["g"], rtol=1e-6, atol=0)
