@@ -44,6 +44,8 @@ METRIC = "decode tokens/s (hybrid 24-layer hot path: GDN step + INT4 paged atten
 
 
 EPILOGUES = "attention * sigmoid(gate) and GDN gated RMSNorm, fused into the kernels' stores"
+GATES_DESC = {"given": "g and beta given (the hook's arguments)",
+              "fused": "g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) computed in the GDN kernel"}
 
 
 def parse_args(argv=None):
@@ -65,6 +67,9 @@ def parse_args(argv=None):
     ap.add_argument("--small", action="store_true",
                     help="reduced case for ncu captures: prefill B=4, T=8192, 2 layers, 8 decode steps; hybrid B=8")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
+    ap.add_argument("--gates", choices=["given", "fused"], default="given",
+                    help="hybrid/serving: GDN steps take g and beta (the hook's arguments), or the raw gate "
+                         "projections with the gate arithmetic in the kernel")
     ap.add_argument("--no-sub-records", action="store_true",
                     help="hybrid workload: skip the serving and long-context sub-records")
     return ap.parse_args(argv)
@@ -194,8 +199,9 @@ def build_stack(args, world, rank, device):
         bsz = 8 if args.small else 64   # (--small: the profiling case, B = 8)
         shape = HybridShape(batch=bsz, context=4096)
         stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv,
-                                  epilogues=args.epilogues, kv_bits=args.kv_bits)
+                                  epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates)
         desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+                "gdn_gates": GATES_DESC[args.gates],
                 "epilogues": EPILOGUES if args.epilogues else "none",
                 "workload": f"hybrid decode step: B={bsz} per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
@@ -209,8 +215,9 @@ def build_stack(args, world, rank, device):
     mine = [lengths[i] for i in shards[rank]]
     shape = HybridShape(batch=len(mine), context=mine)
     stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv,
-                              epilogues=args.epilogues, kv_bits=args.kv_bits)
+                              epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates)
     desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
+            "gdn_gates": GATES_DESC[args.gates],
             "epilogues": EPILOGUES if args.epilogues else "none",
             "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
                         f"cost across GPUs, 24-layer hybrid hot path, INT{args.kv_bits} paged KV", "global_batch": 1024,

@@ -79,8 +79,9 @@ __device__ __forceinline__ float round_to(int dtype, float x) {
 // models/qwen3_5/modeling_qwen3_5.py:492-493): beta = sigmoid(b) in b's dtype, and in fp32
 // g = -exp(A_log) * softplus(a + dt_bias), softplus(x) = x above 20 (torch's threshold),
 // else log(1 + exp(x)).
+template <int kRaw = -1>  // 1: raw projections, 0: g and beta given, -1: decided from p at run time
 __device__ __forceinline__ void step_gates(const GdnParams& p, int64_t gi, int64_t h, float& g, float& beta) {
-  if (p.gate_a == nullptr) {
+  if (kRaw == 0 || (kRaw < 0 && p.gate_a == nullptr)) {
     g = load_as_float(p.g, p.g_dtype, gi);
     beta = load_as_float(p.beta, p.beta_dtype, gi);
     return;
@@ -351,7 +352,7 @@ __device__ __forceinline__ void slice_timeout(const GdnParams& p, uint64_t* bar,
 // 10 CTAs per SM (48 registers, no spill): at B = 64 x 16 heads x 4 slices = 4096 CTAs the
 // grid is 2.77 waves of 1480 slots, where 9 per SM (55 registers) left a last wave of 100
 // CTAs that cannot keep HBM busy; 11 per SM (2.52 waves) measured slower than 10.
-template <typename T>
+template <typename T, bool kRaw>
 __global__ void __launch_bounds__(kThreads, 10) gdn_smem_kernel(const __grid_constant__ CUtensorMap tmap, GdnParams p) {
   extern __shared__ uint8_t slice_raw[];
   float* sl = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(slice_raw) + 127) & ~uintptr_t(127));
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 10) gdn_smem_kernel(const __grid_con
     }
     const int64_t gi = (b * p.seq_len + t) * H + h;
     float gt, bt;
-    step_gates(p, gi, h, gt, bt);
+    step_gates<kRaw ? 1 : 0>(p, gi, h, gt, bt);
     if (!landed) {
       // thread 0 initialised the barrier; every thread sees that before it polls it
       __syncthreads();
@@ -617,18 +618,24 @@ int encode_state_map(CUtensorMap* map, const float* state, int64_t rows) {
   return OQ_OK;
 }
 
-template <typename T>
-int launch_smem(const GdnParams& p, int64_t batch, cudaStream_t s) {
+template <typename T, bool kRaw>
+int launch_smem_as(const GdnParams& p, int64_t batch, cudaStream_t s) {
   CUtensorMap tmap;
   if (int st = encode_state_map(&tmap, p.s_in, batch * p.num_heads * kDk); st != OQ_OK) return st;
-  cudaFuncSetAttribute(gdn_smem_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemSlice));
+  cudaFuncSetAttribute(gdn_smem_kernel<T, kRaw>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemSlice));
   const dim3 grid(unsigned(kDv / kCols), unsigned(p.num_heads), unsigned(batch));
   if (p.prefetch_state) {
-    launch_pdl(gdn_smem_kernel<T>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
+    launch_pdl(gdn_smem_kernel<T, kRaw>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
   } else {
-    launch_plain(gdn_smem_kernel<T>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
+    launch_plain(gdn_smem_kernel<T, kRaw>, grid, dim3(kThreads), kSmemSlice, s, tmap, p);
   }
   return OQ_OK;
+}
+
+// (the raw-gate form is a separate instance: the given-gates step keeps no branch for it)
+template <typename T>
+int launch_smem(const GdnParams& p, int64_t batch, cudaStream_t s) {
+  return p.gate_a != nullptr ? launch_smem_as<T, true>(p, batch, s) : launch_smem_as<T, false>(p, batch, s);
 }
 
 int gdn_recurrent_impl(

@@ -109,10 +109,10 @@ class HybridDecodeStack:
     ``"fused"`` the single-launch ``oq_gdn_conv_step`` (slower on B200, measured: the four
     column-slice CTAs of a head each convolve q/k and synchronise as a cluster).  With
     ``conv=None`` q/k/v are given post-conv.
-    Without a conv mode each GDN layer takes its raw gate projections ``a``, ``b`` and computes
-    ``g = -exp(A_log) softplus(a + dt_bias)``, ``beta = sigmoid(b)`` inside the step kernel
-    (``oq_gdn_recurrent_gates``), as the decode branch does ahead of the hook; the conv modes
-    take g and beta precomputed.
+    ``gates="given"`` feeds every GDN step its g and beta, the hook's own arguments;
+    ``gates="fused"`` (no conv mode) gives it the raw gate projections ``a``, ``b`` instead and
+    computes ``g = -exp(A_log) softplus(a + dt_bias)``, ``beta = sigmoid(b)`` inside the step
+    kernel (``oq_gdn_recurrent_gates``), as the decode branch does ahead of the hook.
     ``epilogues=True`` adds the layers' output epilogues: the attention output gate
     ``* sigmoid(gate)`` (q_proj's second half), fused into the attention kernel's store, and
     the GDN output norm ``Qwen3_5RMSNormGated(o, z)`` (z = the z projection) as the
@@ -127,9 +127,12 @@ class HybridDecodeStack:
 
     def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
                  hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16,
-                 conv: str | None = None, epilogues: bool = False, kv_bits: int = 4):
+                 conv: str | None = None, epilogues: bool = False, kv_bits: int = 4, gates: str = "given"):
         if conv not in (None, "separate", "fused"):
             raise ValueError("conv must be None, 'separate' or 'fused'")
+        if gates not in ("given", "fused") or (gates == "fused" and conv):
+            raise ValueError("gates must be 'given' or 'fused' (the latter without a conv mode)")
+        self.fused_gates = gates == "fused"
         if kv_bits not in (4, 8):
             raise ValueError("kv_bits must be 4 or 8")
         self.kv_bits = kv_bits
@@ -157,7 +160,7 @@ class HybridDecodeStack:
                 state = torch.randn((b, shape.gdn_heads, shape.gdn_dim, shape.gdn_dim), generator=self.gen,
                                     device=self.device, dtype=torch.float32).mul_(0.02)
                 layer = _GdnLayer(state=state)
-                if not conv:  # A = exp(A_log) = 1 and dt_bias = 0: g = -softplus(a), a ~ N(0, 1)
+                if self.fused_gates:  # A = exp(A_log) = 1 and dt_bias = 0: g = -softplus(a), a ~ N(0, 1)
                     layer.A_log = torch.zeros(shape.gdn_heads, dtype=dtype, device=self.device)
                     layer.dt_bias = torch.zeros(shape.gdn_heads, dtype=dtype, device=self.device)
                 if epilogues:
@@ -238,7 +241,7 @@ class HybridDecodeStack:
                                                           device=self.device))
                 else:
                     in_specs += [(("gdn", i, "q"), shp), (("gdn", i, "k"), shp), (("gdn", i, "v"), shp)]
-                if self.conv:
+                if not self.fused_gates:
                     in_specs += [(("gdn", i, "beta"), (b, 1, s.gdn_heads))]
                     # g stays fp32 (the module computes it in fp32): its bits take two 16-bit slots
                     # per value inside the layer's input range, so the layer's inputs are one copy
@@ -335,10 +338,14 @@ class HybridDecodeStack:
                     q, k, v = (y[:, j * hd:(j + 1) * hd, 0].view(s.batch, 1, s.gdn_heads, s.gdn_dim) for j in range(3))
                     cabi.gdn_recurrent(q, k, v, layer.g, layer.beta, initial_state=layer.state,
                                        final_state=layer.state, out=layer.out, use_qk_l2norm=True)
-                else:
+                elif self.fused_gates:
                     cabi.gdn_recurrent_gates(layer.q, layer.k, layer.v, layer.a, layer.b, layer.A_log,
                                              layer.dt_bias, initial_state=layer.state, final_state=layer.state,
                                              out=layer.out, use_qk_l2norm=True, prefetch_state=chained)
+                else:
+                    cabi.gdn_recurrent(layer.q, layer.k, layer.v, layer.g, layer.beta, initial_state=layer.state,
+                                       final_state=layer.state, out=layer.out, use_qk_l2norm=True,
+                                       prefetch_state=chained)
                 if layer.z is not None:
                     cabi.rmsnorm_gated(layer.out, layer.z, layer.norm_w, 1e-6, out=layer.out)
                 prev = ("gdn", i)

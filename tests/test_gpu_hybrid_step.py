@@ -28,11 +28,12 @@ def _gates(layer):
     return ogdn.decay_gates(f(layer.a), f(layer.b), f(layer.A_log), f(layer.dt_bias), rnd=kq.round_bf16)
 
 
-def test_graph_step_matches_oracle():
+@pytest.mark.parametrize("gates", ["given", "fused"])
+def test_graph_step_matches_oracle(gates):
     from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
 
     shape = HybridShape(batch=3, context=[70, 130, 5], num_layers=8)
-    stack = HybridDecodeStack(shape, device="cuda", seed=3)
+    stack = HybridDecodeStack(shape, device="cuda", seed=3, gates=gates)
     stack.fill_inputs()
     states0 = [layer.state.cpu().numpy().copy() for layer in stack.gdn]
     graph = stack.capture()          # (the capture runs one eager step first)
