@@ -70,9 +70,11 @@ struct PageFormat {
 // exact integer dot products of the codes with each digit, combined in fp32.  With
 // 21 bits every bf16 (fp16) element within 2^-13 (2^-10) of the head's largest is
 // represented exactly, so q.k is as exact as fp32 arithmetic on the codes.  With at
-// most 4 query heads per KV head two MMAs per 32 dims cover every head ("packed":
-// set 0 = d2 of heads 0-3 | d1 of heads 0-3, set 1 = d0 of heads 0-3 | zeros); with
-// 5-8 heads each digit takes one MMA ("dual": sets d2, d1, d0).  The fragments live in
+// most 4 query heads per KV head two MMAs per 32 dims cover every head ("packed"): the
+// columns of set 0 are (d2, d1) of heads 0, 1, 2, 3 in turn and those of set 1 (d0, 0),
+// so the lane holding columns 2h, 2h+1 of both sets has all three digit products of head
+// h and assembles its dot products without exchanging anything.  With 5-8 heads each
+// digit takes one MMA ("dual": sets d2, d1, d0; columns = heads).  The fragments live in
 // shared memory and are read per k-step.
 //
 // Code unpacking needs no shifts: w & 0x0F0F0F0F gives the even dims' codes as
@@ -175,10 +177,10 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   auto page_at = [&](int i) { return cta_begin + wg + kWG * i; };  // sequence page of this group's page i
   const int32_t* bt_row = p.block_table + b * p.bt_stride;
   const bool pre_ok = warp == 0 && lane < kSt && int64_t(page_at(lane)) < p.max_pages;
-  // This lane feeds q.k MMA column r: head (packed) r & 3, digit hi for r < 4 and lo for
-  // r >= 4; (dual) head r, both digits.  It holds dims 64c .. 64c+63 of that head, so the
+  // This lane feeds q.k MMA column r: (packed) head r >> 1, digits d2 / d0 for even r and d1
+  // for odd r; (dual) head r, every digit.  It holds dims 64c .. 64c+63 of that head, so the
   // four lanes (r, 0..3) hold the whole head.
-  const int f_head = kDual ? r : (r & 3);
+  const int f_head = kDual ? r : (r >> 1);
   const bool f_has = f_head < G;
   pdl_wait();  // (one long wave: the successor is allowed to launch only after the page loop)
   const int32_t len_raw = p.seq_lens[b];
@@ -309,38 +311,39 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
           dst[4 * k + half] = wa[k];
           dst[4 * k + 2 + half] = wb[k];
         }
-      } else {  // column r: set 0 = d2 (r < 4) | d1 (r >= 4) of head r & 3; set 1 = d0 (r < 4) | 0
-        dst[half] = r < 4 ? wa[0] : wa[1];
-        dst[2 + half] = r < 4 ? wb[0] : wb[1];
-        dst[4 + half] = r < 4 ? wa[2] : 0u;
-        dst[6 + half] = r < 4 ? wb[2] : 0u;
+      } else {  // column r of head r >> 1: set 0 = d2 (even r) | d1 (odd r); set 1 = d0 (even r) | 0
+        const bool odd = r & 1;
+        dst[half] = odd ? wa[1] : wa[0];
+        dst[2 + half] = odd ? wb[1] : wb[0];
+        dst[4 + half] = odd ? 0u : wa[2];
+        dst[6 + half] = odd ? 0u : wb[2];
       }
     }
   }
   named_bar_sync(bar_wg, kThreads);  // fragments written; the stage barriers are initialised
-  // sum(q) and 2^-e of the two heads (2c, 2c+1) whose scores this lane holds: lanes
-  // 8c (r = 2c) and 8c + 4 (r = 2c + 1) hold them
-  const float qs_a = __shfl_sync(0xffffffffu, qsum, 8 * c), qs_b = __shfl_sync(0xffffffffu, qsum, 8 * c + 4);
-  const float qx_a = __shfl_sync(0xffffffffu, q_scale, 8 * c), qx_b = __shfl_sync(0xffffffffu, q_scale, 8 * c + 4);
-  // Packed (<= 4 heads): lanes c and c + 2 both compute heads 2 (c & 1), 2 (c & 1) + 1; lanes
-  // c < 2 feed P' rounded to fp16 to MMA columns 0-3, lanes c >= 2 its fp16 remainder to
-  // columns 4-7, so p.v sees P' to ~22 bits at no extra MMA.  Dual: lane c has heads 2c, 2c+1.
-  const int hc = kDual ? c : (c & 1);
-  const bool ha_ok = 2 * hc < G;
-  const bool hb_ok = 2 * hc + 1 < G;
-  const bool lo_lane = !kDual && c >= 2;
-  // Per-set dot products -> the four q.k values of this lane.  Dual: sets d2, d1, d0 of heads
-  // 2c, 2c+1.  Packed: lane c < 2 holds d2 (set 0) and d0 (set 1) of heads 2c, 2c+1, lane c + 2
-  // the same heads' d1 (set 0); both assemble the full products.
-  auto digit_dots = [&](const int (&tot)[kSets][4], float (&dot)[4]) {
+  // Heads of this lane's scores: (packed) head c, from columns 2c (d2 / d0) and 2c+1 (d1);
+  // (dual) heads 2c and 2c+1.  Lane 8c (r = 2c) holds sum(q) and 2^-e of head c (packed) or
+  // 2c (dual), lane 8c + 4 those of head 2c + 1 (dual).
+  constexpr int kNH = kDual ? 2 : 1;
+  const int h0 = kDual ? 2 * c : c;
+  float qs[kNH], qx[kNH];
+  bool h_ok[kNH];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+  for (int e = 0; e < kNH; ++e) {
+    qs[e] = __shfl_sync(0xffffffffu, qsum, 8 * c + 4 * e);
+    qx[e] = __shfl_sync(0xffffffffu, q_scale, 8 * c + 4 * e);
+    h_ok[e] = h0 + e < G;
+  }
+  // The digit products of this lane's accumulators -> its q_int . codes, dot[tok][e] for tokens
+  // r, r + 8 (accumulator rows) and heads h0 + e.
+  auto digit_dots = [&](const int (&tot)[kSets][4], float (&dot)[2][kNH]) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
       if constexpr (kDual) {
-        dot[j] = combine_digits(tot[0][j], tot[1][j], tot[kSets - 1][j]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) dot[t][e] = combine_digits(tot[0][2 * t + e], tot[1][2 * t + e], tot[2][2 * t + e]);
       } else {
-        const int x0 = __shfl_xor_sync(0xffffffffu, tot[0][j], 2);
-        const int x1 = __shfl_xor_sync(0xffffffffu, tot[kSets - 1][j], 2);
-        dot[j] = lo_lane ? combine_digits(x0, tot[0][j], x1) : combine_digits(tot[0][j], x0, tot[kSets - 1][j]);
+        dot[t][0] = combine_digits(tot[0][2 * t], tot[0][2 * t + 1], tot[1][2 * t]);
       }
     }
   };
@@ -348,9 +351,13 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   float acc[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-  float m_a = -INFINITY, m_b = -INFINITY;  // reference max (log2 units) of heads 2c, 2c+1
-  float l_a = 0.0f, l_b = 0.0f;            // this lane's share of sum(p)
-  float mp_a = 0.0f, mp_b = 0.0f;          // ... of sum(p * v_min)
+  float m[kNH], l[kNH], mp[kNH];  // per head: reference max (log2 units); this lane's sum(p), sum(p v_min)
+#pragma unroll
+  for (int e = 0; e < kNH; ++e) {
+    m[e] = -INFINITY;
+    l[e] = 0.0f;
+    mp[e] = 0.0f;
+  }
 
   const int tok0 = warp * 16 + r;  // token rows of this lane in the page (A rows r and r+8)
   const int tok1 = tok0 + 8;
@@ -420,7 +427,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
       const __half* meta = reinterpret_cast<const __half*>(metas + s * kStageMetaBytes);
 
       // ---------------- integer q.k: A = K codes (16 tokens x 32 dims, u8), B = q digits (s8)
-      float dot[4];  // q_int . codes of (token r, head a), (r, b), (r+8, a), (r+8, b)
+      float dot[2][kNH];  // q_int . codes of (token r / r + 8, head h0 + e)
       if constexpr (kBits == 8) {
         // lane c holds dims 64c .. 64c + 63 of both token rows (16 words each); MMA "lo" of
         // step s takes words 4s (b0 dims) and 4s + 2, MMA "hi" words 4s + 1 and 4s + 3,
@@ -484,60 +491,79 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
         }
         digit_dots(tot, dot);
       }
-      const bool v0 = tok0 < page_tokens, v1 = tok1 < page_tokens;
-      const float ks0 = __half2float(meta[tok0]), km0 = __half2float(meta[kPage + tok0]);
-      const float ks1 = __half2float(meta[tok1]), km1 = __half2float(meta[kPage + tok1]);
-      const float vs0 = __half2float(meta[2 * kPage + tok0]), vm0 = __half2float(meta[3 * kPage + tok0]);
-      const float vs1 = __half2float(meta[2 * kPage + tok1]), vm1 = __half2float(meta[3 * kPage + tok1]);
-      // q.k = scale * 2^-e * sum(code * q_int) + min * sum(q), in log2 units
-      const bool ok0a = v0 && ha_ok, ok0b = v0 && hb_ok, ok1a = v1 && ha_ok, ok1b = v1 && hb_ok;
-      const float s0a = ok0a ? fmaf(ks0 * qx_a, dot[0], km0 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s0b = ok0b ? fmaf(ks0 * qx_b, dot[1], km0 * qs_b) * p.scale_log2 : -INFINITY;
-      const float s1a = ok1a ? fmaf(ks1 * qx_a, dot[2], km1 * qs_a) * p.scale_log2 : -INFINITY;
-      const float s1b = ok1b ? fmaf(ks1 * qx_b, dot[3], km1 * qs_b) * p.scale_log2 : -INFINITY;
-
-      // ---------------- online softmax with a lazily moved reference max
-      float tm_a = fmaxf(s0a, s1a), tm_b = fmaxf(s0b, s1b);
+      const bool tv[2] = {tok0 < page_tokens, tok1 < page_tokens};
+      const int tk[2] = {tok0, tok1};
+      float vs[2], vm[2], sc[2][kNH];
 #pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        tm_a = fmaxf(tm_a, __shfl_xor_sync(0xffffffffu, tm_a, o));
-        tm_b = fmaxf(tm_b, __shfl_xor_sync(0xffffffffu, tm_b, o));
-      }
-      if (__any_sync(0xffffffffu, tm_a > m_a + kTau || tm_b > m_b + kTau)) {
-        const float nm_a = fmaxf(m_a, tm_a), nm_b = fmaxf(m_b, tm_b);
-        const float corr_a = nm_a == -INFINITY ? 1.0f : exp2f(m_a - nm_a);
-        const float corr_b = nm_b == -INFINITY ? 1.0f : exp2f(m_b - nm_b);
-        m_a = nm_a;
-        m_b = nm_b;
-        l_a *= corr_a;
-        l_b *= corr_b;
-        mp_a *= corr_a;
-        mp_b *= corr_b;
+      for (int t = 0; t < 2; ++t) {
+        const float ks = __half2float(meta[tk[t]]), km = __half2float(meta[kPage + tk[t]]);
+        vs[t] = __half2float(meta[2 * kPage + tk[t]]);
+        vm[t] = __half2float(meta[3 * kPage + tk[t]]);
+        // q.k = scale * 2^-e * sum(code * q_int) + min * sum(q), in log2 units
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          acc[j][0] *= corr_a;
-          acc[j][2] *= corr_a;
-          acc[j][1] *= corr_b;
-          acc[j][3] *= corr_b;
+        for (int e = 0; e < kNH; ++e) {
+          sc[t][e] = tv[t] && h_ok[e] ? fmaf(ks * qx[e], dot[t][e], km * qs[e]) * p.scale_log2 : -INFINITY;
         }
       }
-      const float p0a = ok0a ? exp2f(s0a - m_a) : 0.0f, p0b = ok0b ? exp2f(s0b - m_b) : 0.0f;
-      const float p1a = ok1a ? exp2f(s1a - m_a) : 0.0f, p1b = ok1b ? exp2f(s1b - m_b) : 0.0f;
-      l_a += p0a + p1a;
-      l_b += p0b + p1b;
-      mp_a += (v0 ? p0a * vm0 : 0.0f) + (v1 ? p1a * vm1 : 0.0f);
-      mp_b += (v0 ? p0b * vm0 : 0.0f) + (v1 ? p1b * vm1 : 0.0f);
-      // P' = p * v_scale * 2^-kTau in fp16, rows = tokens, cols = heads (packed: the fp16
-      // remainder P' - fp16(P') in the lo lanes' columns)
-      const float ps0 = v0 ? vs0 * kPScale : 0.0f, ps1 = v1 ? vs1 * kPScale : 0.0f;
-      uint32_t blk0 = pack_half2(p0a * ps0, p0b * ps0);
-      uint32_t blk1 = pack_half2(p1a * ps1, p1b * ps1);
-      if (lo_lane) {
-        const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&blk0));
-        const float2 r1 = __half22float2(*reinterpret_cast<const __half2*>(&blk1));
-        blk0 = pack_half2(fmaf(p0a, ps0, -r0.x), fmaf(p0b, ps0, -r0.y));
-        blk1 = pack_half2(fmaf(p1a, ps1, -r1.x), fmaf(p1b, ps1, -r1.y));
+
+      // ---------------- online softmax with a lazily moved reference max
+      float tm[kNH];
+      bool move = false;
+#pragma unroll
+      for (int e = 0; e < kNH; ++e) {
+        tm[e] = fmaxf(sc[0][e], sc[1][e]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) tm[e] = fmaxf(tm[e], __shfl_xor_sync(0xffffffffu, tm[e], o));
+        move = move || tm[e] > m[e] + kTau;
       }
+      if (__any_sync(0xffffffffu, move)) {
+        float corr[kNH];
+#pragma unroll
+        for (int e = 0; e < kNH; ++e) {
+          const float nm = fmaxf(m[e], tm[e]);
+          corr[e] = nm == -INFINITY ? 1.0f : exp2f(m[e] - nm);
+          m[e] = nm;
+          l[e] *= corr[e];
+          mp[e] *= corr[e];
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if constexpr (kDual) {  // columns 2c, 2c+1 = heads h0, h0 + 1
+            acc[j][0] *= corr[0];
+            acc[j][2] *= corr[0];
+            acc[j][1] *= corr[kNH - 1];
+            acc[j][3] *= corr[kNH - 1];
+          } else {  // columns 2c, 2c+1 = the fp16 part and the remainder of head c
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) acc[j][q4] *= corr[0];
+          }
+        }
+      }
+      float pp[2][kNH];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+#pragma unroll
+        for (int e = 0; e < kNH; ++e) {
+          pp[t][e] = tv[t] && h_ok[e] ? exp2f(sc[t][e] - m[e]) : 0.0f;
+          l[e] += pp[t][e];
+          mp[e] = fmaf(pp[t][e], tv[t] ? vm[t] : 0.0f, mp[e]);
+        }
+      }
+      // P' = p * v_scale * 2^-kTau, rows = tokens.  Packed: columns 2c, 2c+1 = P' rounded to fp16
+      // and its fp16 remainder (P' to ~22 bits); dual: columns = heads 2c, 2c+1 in fp16.
+      uint32_t blk[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const float ps = tv[t] ? vs[t] * kPScale : 0.0f;
+        if constexpr (kDual) {
+          blk[t] = pack_half2(pp[t][0] * ps, pp[t][kNH - 1] * ps);
+        } else {
+          const float x = pp[t][0] * ps;
+          const float hi = __half2float(__float2half_rn(x));
+          blk[t] = pack_half2(hi, x - hi);
+        }
+      }
+      const uint32_t blk0 = blk[0], blk1 = blk[1];
       // transpose into the B operand of p.v
       pv_page(st, movmatrix_trans(blk0), movmatrix_trans(blk1));
     }
@@ -578,16 +604,20 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   // ---- reduce this warp's per-lane sums over the 8 token rows
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
-    mp_a += __shfl_xor_sync(0xffffffffu, mp_a, o);
-    mp_b += __shfl_xor_sync(0xffffffffu, mp_b, o);
+#pragma unroll
+    for (int e = 0; e < kNH; ++e) {
+      l[e] += __shfl_xor_sync(0xffffffffu, l[e], o);
+      mp[e] += __shfl_xor_sync(0xffffffffu, mp[e], o);
+    }
   }
   if (r == 0) {
-    tail->warp_m[warp][2 * c] = m_a;
-    tail->warp_m[warp][2 * c + 1] = m_b;
-    tail->warp_l[warp][2 * c] = l_a;
-    tail->warp_l[warp][2 * c + 1] = l_b;
+#pragma unroll
+    for (int e = 0; e < kNH; ++e) {
+      if (h_ok[e]) {
+        tail->warp_m[warp][h0 + e] = m[e];
+        tail->warp_l[warp][h0 + e] = l[e];
+      }
+    }
   }
   const int outputs = G * kHeadDim;
   const bool single = nsplit_b == 1;
@@ -620,17 +650,9 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   //      numerator = 2^kTau * 2^24 * acc / (1 or 16) + sum(p * v_min)
   float* red = reinterpret_cast<float*>(codes);  // this group's kWarps * kMaxGroup rows of kRedStride floats
   {
-    if constexpr (!kDual) {
-      // packed: add the remainder columns (lanes c + 2) to the fp16 P' columns (lanes c)
+    float f[kNH];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], 2);
-      }
-    }
-    const int ha = 2 * c, hb = 2 * c + 1;
-    const float fa = ha < G ? tail->warp_f[warp][ha] : 0.0f;
-    const float fb = hb < G ? tail->warp_f[warp][hb] : 0.0f;
+    for (int e = 0; e < kNH; ++e) f[e] = h_ok[e] ? tail->warp_f[warp][h0 + e] : 0.0f;
     // INT4: row r = even dim 32r + 2j (codes x 1), row r + 8 = odd dim (codes x 16);
     // INT8: MMA j = 8 hf + k, row r = dim 128 hf + 16r + 2k, row r + 8 = the next dim (x 1)
     constexpr float kEvenUnscale = kPUnscale * kVCodeUnscale;
@@ -638,13 +660,24 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int d0 = kBits == 8 ? 128 * (j >> 3) + 16 * r + 2 * (j & 7) : 32 * r + 2 * j;
-      if (ha < G) {
-        red[red_index(warp, ha, d0)] = fmaf(acc[j][0], kEvenUnscale, mp_a) * fa;
-        red[red_index(warp, ha, d0 + 1)] = fmaf(acc[j][2], kOddUnscale, mp_a) * fa;
+      // per head of this lane: the even-row (d0) and odd-row (d0 + 1) sums; packed: the fp16
+      // part (column 2c) plus the remainder (column 2c + 1) of head c
+      float ev[kNH], od[kNH];
+      if constexpr (kDual) {
+        ev[0] = acc[j][0];
+        od[0] = acc[j][2];
+        ev[kNH - 1] = acc[j][1];
+        od[kNH - 1] = acc[j][3];
+      } else {
+        ev[0] = acc[j][0] + acc[j][1];
+        od[0] = acc[j][2] + acc[j][3];
       }
-      if (hb < G) {
-        red[red_index(warp, hb, d0)] = fmaf(acc[j][1], kEvenUnscale, mp_b) * fb;
-        red[red_index(warp, hb, d0 + 1)] = fmaf(acc[j][3], kOddUnscale, mp_b) * fb;
+#pragma unroll
+      for (int e = 0; e < kNH; ++e) {
+        if (h_ok[e]) {
+          red[red_index(warp, h0 + e, d0)] = fmaf(ev[e], kEvenUnscale, mp[e]) * f[e];
+          red[red_index(warp, h0 + e, d0 + 1)] = fmaf(od[e], kOddUnscale, mp[e]) * f[e];
+        }
       }
     }
   }
