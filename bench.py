@@ -55,6 +55,9 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["hybrid", "serving", "longctx", "prefill"], default="hybrid")
+    ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
+                    help="long-context exchange of the partials across GPUs: the NVLink exchange kernel "
+                         "(peer stores, one launch per layer) or NCCL all-gather + merge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kv-bits", type=int, choices=[4, 8], default=4,
                     help="hybrid/serving: width of the paged KV cache codes (8: the reference's k_bits=8 preset)")
@@ -335,14 +338,17 @@ def measure_longctx(args, world, rank, device, dist, hbm_peak):
     ranks, per layer the partial attention and the exchange + LSE merge, the step in a CUDA graph."""
     import torch
 
-    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder, PeerExchange
 
     length, layers = 131072, 6
     gen = torch.Generator(device=device)
     gen.manual_seed(2 * 1000 + rank)
+    # NVLink exchange kernel (one call site per layer) or the NCCL all-gather + merge
+    exchange = (PeerExchange(8, 256, rank=rank, world=world, device=device, sites=layers)
+                if world > 1 and args.exchange == "nvlink" else None)
     decs = []
-    for _ in range(layers):
-        d = ContextParallelDecoder(2, 256, rank=rank, world=world, device=device)
+    for layer in range(layers):
+        d = ContextParallelDecoder(2, 256, rank=rank, world=world, device=device, exchange=exchange, site=layer)
         d.prefill_random(length, generator=gen, capacity_tokens=0, page_seed=2)
         decs.append(d)
     q = torch.randn((1, 8, 256), generator=gen, device=device).to(torch.bfloat16)
@@ -377,10 +383,15 @@ def measure_longctx(args, world, rank, device, dist, hbm_peak):
     kv_bytes = length * 2 * 264 * layers
     del graph                                  # (a graph holding NCCL calls goes before the group does)
     torch.cuda.synchronize(device)
+    if exchange is not None:
+        exchange.close()
+    how = ("NVLink exchange kernel: peer stores + flag + LSE merge in one launch" if exchange is not None
+           else "NCCL all-gather of the partials + LSE merge kernel")
     return {"workload": "long context: B=1, context 131072, 6 full-attention layers (Hq 8 / Hkv 2 / D 256), "
                         "KV range split evenly across GPUs, per layer partial attention + exchange of fp32 "
-                        "(out, lse) + LSE merge (one GPU: the attention kernel writes the output), step in a "
+                        f"(out, lse) ({how}) (one GPU: the attention kernel writes the output), step in a "
                         "CUDA graph",
+            "exchange": "none (one GPU)" if world == 1 else args.exchange,
             "scaling": "strong", "steps": steps, "ms_per_step": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 1),
             "kv_bytes_per_step_total": kv_bytes, "GB_s_per_gpu": round(kv_bytes / world / ms / 1e6, 1),
             "hbm_frac_per_gpu": round(kv_bytes / world / ms / 1e6 / hbm_peak, 4)}

@@ -220,6 +220,61 @@ def lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, dtype: torch.dtype
     return out
 
 
+def xrank_buffer_bytes(rows: int, head_dim: int, world: int) -> int:
+    """Bytes of one call site's NVLink receive buffer (``oq_xrank_buffer_bytes``)."""
+    n = int(_lib.load().oq_xrank_buffer_bytes(rows, head_dim, world))
+    if n == 0:
+        raise ValueError(f"bad exchange sizes: rows={rows}, head_dim={head_dim}, world={world}")
+    return n
+
+
+def ipc_export(buf: torch.Tensor) -> tuple[bytes, int]:
+    """IPC handle of the device allocation holding ``buf`` and ``buf``'s byte offset in it."""
+    require_cuda(buf)
+    import ctypes
+
+    handle = ctypes.create_string_buffer(int(_lib.load().oq_ipc_handle_bytes()))
+    off = ctypes.c_int64(0)
+    call("oq_ipc_export", ptr(buf), ctypes.addressof(handle), ctypes.addressof(off))
+    return handle.raw, off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Map a peer's allocation into this process; returns the device address at ``offset``."""
+    import ctypes
+
+    out = ctypes.c_void_p(0)
+    call("oq_ipc_import", handle, int(offset), ctypes.addressof(out))
+    return int(out.value)
+
+
+def ipc_close(address: int, offset: int) -> None:
+    call("oq_ipc_close", int(address), int(offset))
+
+
+def xrank_lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, peer_table: torch.Tensor, rank: int,
+                    world: int, epoch: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                    out: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
+                    device_status: torch.Tensor | None = None) -> torch.Tensor:
+    """Exchange this rank's partial ``part_out`` ``[R, D]`` / ``part_lse`` ``[R]`` over NVLink and merge
+    every rank's into ``[R, D]`` (``oq_xrank_lse_merge``).  ``peer_table``: int64 device tensor of
+    the ``world`` buffer addresses of this call site; ``epoch``: its int32 device counter."""
+    require_cuda(part_out, part_lse, peer_table, epoch)
+    if part_out.dtype != torch.float32 or part_lse.dtype != torch.float32:
+        raise ValueError("partials must be fp32")
+    if peer_table.dtype != torch.int64 or peer_table.numel() != world or epoch.dtype != torch.int32:
+        raise ValueError("peer_table must be int64 [world] and epoch int32")
+    part_out, part_lse = part_out.contiguous(), part_lse.contiguous()
+    rows, d = part_out.shape
+    if tuple(part_lse.shape) != (rows,):
+        raise ValueError("part_lse must be [rows]")
+    if out is None:
+        out = torch.empty((rows, d), dtype=dtype, device=part_out.device)
+    call("oq_xrank_lse_merge", ptr(part_out), ptr(part_lse), rows, d, ptr(peer_table), int(rank), int(world),
+         ptr(epoch), ptr(out), dtype_code(out.dtype), ptr(out_lse), ptr(device_status), stream_ptr(part_out.device))
+    return out
+
+
 def gather_dequant(pool: PagedKvPool, block_table: torch.Tensor, seq_lens: torch.Tensor, max_len: int,
                    dtype: torch.dtype, *, device_status: torch.Tensor | None = None, _bits: int | None = None):
     """Dequantised ``(keys, values)`` ``[B, Hkv, max_len, D]`` (rows past a sequence's length are 0)."""

@@ -13,8 +13,14 @@ combines them with ``oq_lse_merge``:
 
 New decode tokens are appended to the last rank's range (the tail of the
 sequence).  The reference decodes on one GPU; this module has no counterpart
-there.  The exchange goes through torch.distributed (NCCL); no kernel here
-reads another GPU's memory.
+there.
+
+Two exchanges give the same bits.  The NCCL path packs the partial, all-gathers
+it through torch.distributed and merges with ``oq_lse_merge``.  The NVLink path
+(``PeerExchange``) is one kernel per layer, ``oq_xrank_lse_merge``: it stores the
+partial into every rank's receive buffer with plain stores over NVLink (CUDA IPC
+mappings, no multicast), raises a per-call flag, waits (bounded) for every rank's
+flag and merges in the same order as ``oq_lse_merge``.
 """
 
 from __future__ import annotations
@@ -62,12 +68,15 @@ class PartialFns:
     # optional, one rank: q -> out [B, Hq, D] straight from the attention kernel.  The merge of a
     # single partial is the identity, so the fp32 partial, its packing and the merge are skipped.
     single: Callable[[torch.Tensor], torch.Tensor] | None = None
+    # optional, several ranks: (out_f32 [B, Hq, D], lse [B, Hq]) -> out [B * Hq, D] merged over every
+    # rank by the NVLink exchange kernel, in place of pack + all-gather + unpack + merge.
+    exchange: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] | None = None
 
 
 def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> torch.Tensor:
     """Attention of ``q`` ``[B, Hq, D]`` over the KV ranges of every rank of ``group``; returns ``[B, Hq, D]``.
 
-    Every rank takes the same collective step (one all-gather) per call.
+    Every rank takes the same exchange step (one all-gather, or one NVLink exchange kernel) per call.
     """
     import torch.distributed as dist
 
@@ -75,6 +84,8 @@ def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> 
     if world == 1 and fns.single is not None:
         return fns.single(q).reshape(q.shape)
     out_f32, lse = fns.partial(q)
+    if world > 1 and fns.exchange is not None:
+        return fns.exchange(out_f32, lse).reshape(q.shape)
     msg = pack_partial(out_f32, lse)
     if world == 1:
         part_out, part_lse = unpack_partials(msg.view(1, *msg.shape), q.shape[-1])
@@ -83,6 +94,70 @@ def context_parallel_attention(q: torch.Tensor, fns: PartialFns, group=None) -> 
     dist.all_gather_into_tensor(gathered, msg, group=group)
     part_out, part_lse = unpack_partials(gathered.view(world, *msg.shape), q.shape[-1])
     return fns.merge(part_out, part_lse).reshape(q.shape)
+
+
+class PeerExchange:
+    """NVLink receive buffers for ``sites`` call sites (e.g. one per attention layer) of ``rows`` x
+    ``head_dim`` partials, mapped into every rank of ``group``.
+
+    Construction is collective: each rank allocates one zeroed buffer for all sites, exports its
+    CUDA IPC handle, all-gathers the handles over ``group`` and maps every peer's buffer.  Each
+    site keeps its own epoch counter on the device, so calls of one site may be captured in a
+    CUDA graph and replayed.  ``close()`` is collective too: it waits for every rank's last merge,
+    then unmaps the peers' buffers.
+    """
+
+    def __init__(self, rows: int, head_dim: int, *, rank: int, world: int, device, group=None, sites: int = 1):
+        from . import cabi
+
+        self.cabi = cabi
+        self.rows, self.head_dim, self.rank, self.world, self.sites = int(rows), int(head_dim), rank, world, sites
+        self.device = torch.device(device)
+        self.site_bytes = cabi.xrank_buffer_bytes(rows, head_dim, world)
+        self.buf = torch.zeros(self.site_bytes * sites, dtype=torch.uint8, device=self.device)
+        self._imported: list[tuple[int, int]] = []
+        bases = [0] * world
+        bases[rank] = self.buf.data_ptr()
+        if world > 1:
+            import torch.distributed as dist
+
+            handle, off = cabi.ipc_export(self.buf)
+            nh = len(handle)
+            msg = torch.zeros(nh + 8, dtype=torch.uint8)
+            msg[:nh] = torch.frombuffer(bytearray(handle), dtype=torch.uint8)
+            msg[nh:] = torch.tensor([off], dtype=torch.int64).view(torch.uint8)
+            gathered = torch.empty(world * msg.numel(), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(gathered, msg.to(self.device), group=group)
+            g = gathered.cpu().view(world, nh + 8)
+            for r in range(world):
+                if r == rank:
+                    continue
+                peer_off = int(g[r, nh:].clone().view(torch.int64)[0])
+                addr = cabi.ipc_import(bytes(g[r, :nh].tolist()), peer_off)
+                self._imported.append((addr, peer_off))
+                bases[r] = addr
+            dist.barrier(group=group)        # every buffer is zeroed and mapped before any rank's first store
+        self.group = group
+        self.peer_tables = torch.tensor([[b + s * self.site_bytes for b in bases] for s in range(sites)],
+                                        dtype=torch.int64, device=self.device)
+        self.epochs = torch.zeros(sites, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def merge(self, site: int, part_out: torch.Tensor, part_lse: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+        """This rank's partial ``[R, D]`` / ``[R]`` in, every rank's merged output ``[R, D]`` out."""
+        return self.cabi.xrank_lse_merge(part_out.reshape(self.rows, self.head_dim), part_lse.reshape(self.rows),
+                                         self.peer_tables[site], self.rank, self.world,
+                                         self.epochs[site:site + 1], dtype=dtype, device_status=self.status)
+
+    def close(self) -> None:
+        if self._imported:
+            import torch.distributed as dist
+
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)   # no rank still stores into a buffer that is about to go
+            for addr, off in self._imported:
+                self.cabi.ipc_close(addr, off)
+            self._imported = []
 
 
 class ContextParallelDecoder:
@@ -95,7 +170,8 @@ class ContextParallelDecoder:
     """
 
     def __init__(self, num_kv_heads: int, head_dim: int, *, rank: int, world: int, device, group=None,
-                 page_size: int = 64, out_dtype=torch.bfloat16):
+                 page_size: int = 64, out_dtype=torch.bfloat16, exchange: PeerExchange | None = None,
+                 site: int = 0):
         from . import cabi
 
         self.cabi = cabi
@@ -106,6 +182,8 @@ class ContextParallelDecoder:
         self.paged = None
         self.range = (0, 0)
         self._ws = None
+        # the NVLink exchange (call site `site` of it) in place of the NCCL all-gather, when given
+        self.exchange, self.site = exchange, site
 
     def prefill(self, keys: torch.Tensor, values: torch.Tensor, *, capacity_tokens: int | None = None,
                 page_seed: int | None = None) -> None:
@@ -173,7 +251,11 @@ class ContextParallelDecoder:
     def _merge(self, part_out: torch.Tensor, part_lse: torch.Tensor) -> torch.Tensor:
         return self.cabi.lse_merge(part_out, part_lse, dtype=self.out_dtype)
 
+    def _exchange(self, out_f32: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
+        return self.exchange.merge(self.site, out_f32, lse, dtype=self.out_dtype)
+
     def decode(self, q: torch.Tensor) -> torch.Tensor:
         # one rank with the output in the query's dtype: the kernel writes the output itself
         single = self._single if q.dtype == self.out_dtype else None
-        return context_parallel_attention(q, PartialFns(self._partial, self._merge, single), self.group)
+        exchange = self._exchange if self.exchange is not None else None
+        return context_parallel_attention(q, PartialFns(self._partial, self._merge, single, exchange), self.group)

@@ -1,7 +1,10 @@
-"""Long-context decode split across 2 GPUs (NCCL), against one GPU and the oracle.
+"""Long-context decode split across 2 GPUs, against one GPU and the oracle.
 
-Runs as two spawned ranks, one per GPU; skipped when fewer than 2 GPUs are
-visible.  NVLS is disabled for the test's NCCL communicator.
+Both exchanges of the partials run on the same ranks: the NCCL all-gather + merge
+and the NVLink exchange kernel (plain peer stores through CUDA IPC mappings, no
+multicast); their outputs must be bit-identical.  Runs as two spawned ranks, one
+per GPU; skipped when fewer than 2 GPUs are visible.  NVLS is disabled for the
+test's NCCL communicator.  The one-rank tests of the exchange kernel run on one GPU.
 """
 
 from __future__ import annotations
@@ -40,7 +43,7 @@ def _inputs():
 def _rank(rank, world, port, outdir):
     import torch.distributed as dist
 
-    from optiz_qwen_b200.context_parallel import ContextParallelDecoder
+    from optiz_qwen_b200.context_parallel import ContextParallelDecoder, PeerExchange
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -50,13 +53,26 @@ def _rank(rank, world, port, outdir):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
     k, v, q, kn = _inputs()
-    dec = ContextParallelDecoder(2, 256, rank=rank, world=world, device=dev)
+    ex = PeerExchange(8, 256, rank=rank, world=world, device=dev, sites=1)
+    dec = ContextParallelDecoder(2, 256, rank=rank, world=world, device=dev, exchange=ex)
     dec.prefill(torch.from_numpy(k).to(torch.bfloat16), torch.from_numpy(v).to(torch.bfloat16), capacity_tokens=16)
-    outs = [dec.decode(torch.from_numpy(q[0]).to(dev, torch.bfloat16)).float().cpu().numpy()]
+
+    def both(qs):
+        dec.exchange = None                                   # NCCL all-gather + oq_lse_merge
+        a = dec.decode(qs).float().cpu().numpy()
+        dec.exchange = ex                                     # NVLink exchange kernel
+        b = dec.decode(qs).float().cpu().numpy()
+        c = dec.decode(qs).float().cpu().numpy()              # second call: the other slot parity
+        return np.stack([a, b, c])
+
+    outs = [both(torch.from_numpy(q[0]).to(dev, torch.bfloat16))]
     knt = torch.from_numpy(kn).to(dev, torch.bfloat16)
     dec.append(knt, knt)
-    outs.append(dec.decode(torch.from_numpy(q[1]).to(dev, torch.bfloat16)).float().cpu().numpy())
+    outs.append(both(torch.from_numpy(q[1]).to(dev, torch.bfloat16)))
+    status = int(ex.status.item())
+    ex.close()
     np.save(os.path.join(outdir, f"out{rank}.npy"), np.stack(outs))
+    np.save(os.path.join(outdir, f"status{rank}.npy"), np.array([status]))
     dist.destroy_process_group()
 
 
@@ -73,6 +89,8 @@ def test_long_context_split_over_two_gpus_matches_one_gpu_and_oracle():
     with tempfile.TemporaryDirectory() as d:
         mp.spawn(_rank, args=(2, _free_port(), d), nprocs=2, join=True)
         outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(2)]
+        statuses = [int(np.load(os.path.join(d, f"status{r}.npy"))[0]) for r in range(2)]
+    assert statuses == [0, 0]
     k, v, q, kn = _inputs()
     # one GPU, whole cache
     pool = cabi.PagedKvPool(64, 2, 256, 64, "cuda")
@@ -85,10 +103,13 @@ def test_long_context_split_over_two_gpus_matches_one_gpu_and_oracle():
     vd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([v, kn], axis=2)))[0]
     ref0, _ = decode_attention(q[0], [kd[:, :LENGTH]], [vd[:, :LENGTH]], 1 / 16)
     ref1, _ = decode_attention(q[1], [kd], [vd], 1 / 16)
-    for out in outs:
-        assert_attn_close(out[0], ref0)
-        assert_attn_close(out[1], ref1)
-        assert_attn_close(out[0], single0)
+    for out in outs:                               # out [step, exchange (nccl, nvlink, nvlink), B, Hq, D]
+        for x in range(3):
+            assert_attn_close(out[0, x], ref0)
+            assert_attn_close(out[1, x], ref1)
+            assert_attn_close(out[0, x], single0)
+        assert np.array_equal(out[:, 0], out[:, 1])   # NVLink exchange == NCCL path, bit for bit
+        assert np.array_equal(out[:, 1], out[:, 2])
     assert np.array_equal(outs[0], outs[1])        # every rank holds the same merged output
 
 
@@ -118,3 +139,33 @@ def test_one_rank_path_matches_partial_and_merge_and_oracle():
         assert_attn_close(fast.float().cpu().numpy(), refs[step])
         assert_attn_close(general.float().cpu().numpy(), refs[step])
         assert_attn_close(fast.float().cpu().numpy(), general.float().cpu().numpy())
+
+
+def test_exchange_kernel_one_rank_matches_lse_merge_in_graph_replays():
+    """The exchange kernel with one rank: the merge of a single partial, bit-identical to
+    oq_lse_merge, over eager calls and CUDA graph replays (the epoch advances on the device)."""
+    from optiz_qwen_b200 import cabi
+    from optiz_qwen_b200.context_parallel import PeerExchange
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    rows, d = 16, 256
+    ex = PeerExchange(rows, d, rank=0, world=1, device="cuda", sites=2)
+    part = torch.randn((rows, d), generator=gen, device="cuda")
+    lse = torch.randn((rows,), generator=gen, device="cuda") * 4
+    ref = cabi.lse_merge(part.view(1, rows, d), lse.view(1, rows), dtype=torch.bfloat16)
+    for site in (0, 1, 0):
+        out = ex.merge(site, part, lse)
+        assert torch.equal(out, ref)
+    out = torch.empty_like(ref)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        out.copy_(ex.merge(1, part, lse))
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert ex.epochs.tolist() == [2, 4]        # site 0: 2 eager calls; site 1: 1 eager call + 3 replays
+    assert int(ex.status.item()) == 0

@@ -144,3 +144,26 @@ def test_chunked_gdn_timeout_then_clean_run(two_phase):
     _, rs = gdn.chunk_gated_delta_rule(q, k, v, g, beta, 64, s0, True, True)
     assert_gdn_close(sf.cpu().numpy(), rs)
     assert np.isfinite(out.float().cpu().numpy()).all()
+
+
+def test_exchange_wait_timeout_reports_and_next_call_is_clean():
+    """The NVLink exchange's flag wait (one rank: its own flag, raised before it polls) given no
+    polls reports OQ_DEV_TIMEOUT, still merges and advances the epoch; the next call is clean."""
+    from optiz_qwen_b200 import _lib, cabi
+    from optiz_qwen_b200.context_parallel import PeerExchange
+
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    ex = PeerExchange(8, 256, rank=0, world=1, device="cuda")
+    part = torch.randn((8, 256), generator=gen, device="cuda")
+    lse = torch.randn((8,), generator=gen, device="cuda")
+    ref = cabi.lse_merge(part.view(1, 8, 256), lse.view(1, 8), dtype=torch.bfloat16)
+    with wait_polls(0):
+        out = ex.merge(0, part, lse)
+        torch.cuda.synchronize()
+    assert int(ex.status.item()) & _lib.OQ_DEV_TIMEOUT
+    assert torch.equal(out, ref)
+    ex.status.zero_()
+    out = ex.merge(0, part, lse)
+    torch.cuda.synchronize()
+    assert int(ex.status.item()) == 0 and torch.equal(out, ref)
+    assert ex.epochs.tolist() == [2]
