@@ -244,37 +244,52 @@ int oq_lse_merge(const float* part_out, const float* part_lse,
 
 /* ------------------------------------------------------------------ exchange over NVLink
  * The long-context exchange of (out, lse) partials without NCCL: each rank stores its
- * partial straight into every other rank's receive buffer over NVLink (plain stores,
- * CUDA IPC mappings, no multicast object), raises a per-call flag there, waits (bounded)
+ * merged rows straight into every other rank's receive buffer over NVLink (plain stores,
+ * CUDA IPC mappings, no multicast object), raises a per-row flag there, waits (bounded)
  * for every rank's flag in its own buffer and merges with the arithmetic of oq_lse_merge,
  * in the same order, so the result is bit-identical to the all-gather + oq_lse_merge path.
  * No reference counterpart (the reference runs on one GPU).
  *
  * Set-up, once per rank and buffer:
  *   oq_xrank_buffer_bytes(rows, head_dim, world): bytes of one call site's receive buffer
- *     (0 for bad sizes).  Allocate one per call site (e.g. per attention layer), zeroed.
+ *     (0 for bad sizes).  Allocate one per call site (e.g. per attention layer), zeroed; it
+ *     also holds this rank's per-row call counters, so a CUDA graph replay works.
  *   oq_ipc_export(ptr, handle, &offset): writes oq_ipc_handle_bytes() bytes of IPC handle
  *     for the device allocation holding ptr, and ptr's offset in it.  Exchange handles and
  *     offsets between the ranks by any host channel.
  *   oq_ipc_import(handle, offset, &ptr): maps a peer's allocation into this process.
- *   oq_ipc_close(ptr, offset): unmaps it (after every rank's last merge).
- * Per call:
- *   oq_xrank_lse_merge: part_out [rows, head_dim] fp32 (16-byte aligned, head_dim % 4 == 0),
- *   part_lse [rows] fp32; peer_buffers: device array [world] of every rank's buffer for
- *   this call site (this rank's own at [rank]); epoch: this call site's uint32 counter in
- *   device memory, zero before the first call and advanced by the kernel itself (so a CUDA
- *   graph replay works); out [rows, head_dim] in `dtype`, out_lse [rows] or NULL.  Every
- *   rank calls each call site the same number of times, in the same order; a rank whose
- *   peers do not arrive within ~2 s sets OQ_DEV_TIMEOUT in device_status and merges what
- *   it has.  Calls at one call site must be ordered on one stream. */
+ *   oq_ipc_close(ptr, offset): unmaps it (after every rank's last exchange).
+ * Per call (peer_buffers: device array [world] of every rank's buffer for this call site,
+ * this rank's own at [rank]; every rank calls each call site the same number of times, in
+ * the same order, and calls at one call site are ordered on one stream; a rank whose peers
+ * do not arrive within ~2 s sets OQ_DEV_TIMEOUT in device_status and merges what it has):
+ *   oq_xrank_lse_merge: part_out [rows, head_dim] fp32, part_lse [rows] fp32 (an earlier
+ *     kernel's partial) -> out [rows, head_dim] in `dtype`, out_lse [rows] or NULL.
+ *   oq_decode_attn_int4_paged_xrank: oq_decode_attn_int4_paged over this rank's KV range
+ *     whose split merge exchanges every merged row in the same launch (no fp32 partial round
+ *     trip, no separate exchange kernel); `out` / out_f32 / out_lse receive the merge over
+ *     all ranks (rows = batch x num_heads).  The workspace is required (its size for
+ *     `num_splits` as for oq_decode_attn_int4_paged, at least one split). */
 size_t oq_xrank_buffer_bytes(int64_t rows, int64_t head_dim, int64_t world);
 size_t oq_ipc_handle_bytes(void);
 int oq_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int oq_ipc_import(const void* handle, int64_t offset, void** ptr);
 int oq_ipc_close(void* ptr, int64_t offset);
 int oq_xrank_lse_merge(const float* part_out, const float* part_lse, int64_t rows, int64_t head_dim,
-                       float* const* peer_buffers, int rank, int world, uint32_t* epoch,
+                       float* const* peer_buffers, int rank, int world,
                        void* out, int dtype, float* out_lse, int32_t* device_status, void* stream);
+int oq_decode_attn_int4_paged_xrank(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    float* const* peer_buffers, int rank, int world,
+    int32_t* device_status, void* stream);
 
 /* ------------------------------------------------------------------ paged gather
  * Replaces QServeAttentionLayer.materialize / _dequantize_groupwise / _unpack_uint4

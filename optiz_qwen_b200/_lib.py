@@ -57,7 +57,10 @@ SIGNATURES = {
     "oq_ipc_export": (i32, [p, p, p]),
     "oq_ipc_import": (i32, [p, i64, p]),
     "oq_ipc_close": (i32, [p, i64]),
-    "oq_xrank_lse_merge": (i32, [p, p, i64, i64, p, i32, i32, p, p, i32, p, p, p]),
+    "oq_xrank_lse_merge": (i32, [p, p, i64, i64, p, i32, i32, p, i32, p, p, p]),
+    "oq_decode_attn_int4_paged_xrank": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
+                                              i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, i32, i32,
+                                              p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gather_dequant_int8": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,

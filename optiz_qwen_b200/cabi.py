@@ -142,14 +142,18 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
                      out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
                      workspace: torch.Tensor | None = None, num_splits: int = 0,
                      device_status: torch.Tensor | None = None, want_out: bool = True,
-                     gate: torch.Tensor | None = None, _bits: int | None = None):
+                     gate: torch.Tensor | None = None, exchange: tuple | None = None, _bits: int | None = None):
     """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache (4- or 8-bit codes,
     as the pool holds: ``oq_decode_attn_int{4,8}_paged``).
 
     Returns ``out`` (query dtype, ``[B, Hq, D]``) unless ``want_out`` is False.  With
     ``gate`` ``[B, Hq, D]`` (query dtype, unit stride along D) the output is gated in the
     kernel: ``out = attn * sigmoid(gate)`` (``oq_decode_attn_int{4,8}_paged_gated``); fp32 /
-    lse outputs are not available then.
+    lse outputs are not available then.  With ``exchange = (peer_table, rank, world)`` (4-bit
+    pools; ``peer_table``: int64 device tensor of the ``world`` NVLink receive buffers of this
+    call site) this rank's KV range is attended and the split merge exchanges every merged row
+    with the other ranks in the same launch: the outputs are the merge over all ranks
+    (``oq_decode_attn_int4_paged_xrank``).
     """
     require_cuda(query, block_table, seq_lens)
     entry = _bits_entry("decode_attn", pool, _bits) + "_paged"
@@ -182,6 +186,21 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
              b, hq, pool.num_kv_heads, d, float(scaling), ptr(gate), gate.stride(0), gate.stride(1),
              ptr(out), out.stride(0), out.stride(1), ptr(workspace), workspace.numel(), int(num_splits),
              ptr(device_status), stream_ptr(query.device))
+        return out
+    if exchange is not None:
+        peer_table, rank, world = exchange
+        require_cuda(peer_table)
+        if entry != "oq_decode_attn_int4_paged":
+            raise ValueError("the cross-GPU exchange needs the 4-bit cache")
+        if peer_table.dtype != torch.int64 or peer_table.numel() != world:
+            raise ValueError("peer_table must be int64 [world]")
+        call(entry + "_xrank", ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
+             ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+             ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
+             b, hq, pool.num_kv_heads, d, float(scaling),
+             ptr(out), out.stride(0) if out is not None else 0, out.stride(1) if out is not None else 0,
+             ptr(out_f32), ptr(out_lse), ptr(workspace), workspace.numel(), int(num_splits),
+             ptr(peer_table), int(rank), int(world), ptr(device_status), stream_ptr(query.device))
         return out
     call(entry, ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
          ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
@@ -253,17 +272,17 @@ def ipc_close(address: int, offset: int) -> None:
 
 
 def xrank_lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, peer_table: torch.Tensor, rank: int,
-                    world: int, epoch: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                    world: int, *, dtype: torch.dtype = torch.bfloat16,
                     out: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
                     device_status: torch.Tensor | None = None) -> torch.Tensor:
     """Exchange this rank's partial ``part_out`` ``[R, D]`` / ``part_lse`` ``[R]`` over NVLink and merge
     every rank's into ``[R, D]`` (``oq_xrank_lse_merge``).  ``peer_table``: int64 device tensor of
-    the ``world`` buffer addresses of this call site; ``epoch``: its int32 device counter."""
-    require_cuda(part_out, part_lse, peer_table, epoch)
+    the ``world`` buffer addresses of this call site."""
+    require_cuda(part_out, part_lse, peer_table)
     if part_out.dtype != torch.float32 or part_lse.dtype != torch.float32:
         raise ValueError("partials must be fp32")
-    if peer_table.dtype != torch.int64 or peer_table.numel() != world or epoch.dtype != torch.int32:
-        raise ValueError("peer_table must be int64 [world] and epoch int32")
+    if peer_table.dtype != torch.int64 or peer_table.numel() != world:
+        raise ValueError("peer_table must be int64 [world]")
     part_out, part_lse = part_out.contiguous(), part_lse.contiguous()
     rows, d = part_out.shape
     if tuple(part_lse.shape) != (rows,):
@@ -271,7 +290,7 @@ def xrank_lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, peer_table: 
     if out is None:
         out = torch.empty((rows, d), dtype=dtype, device=part_out.device)
     call("oq_xrank_lse_merge", ptr(part_out), ptr(part_lse), rows, d, ptr(peer_table), int(rank), int(world),
-         ptr(epoch), ptr(out), dtype_code(out.dtype), ptr(out_lse), ptr(device_status), stream_ptr(part_out.device))
+         ptr(out), dtype_code(out.dtype), ptr(out_lse), ptr(device_status), stream_ptr(part_out.device))
     return out
 
 

@@ -102,9 +102,11 @@ class PeerExchange:
 
     Construction is collective: each rank allocates one zeroed buffer for all sites, exports its
     CUDA IPC handle, all-gathers the handles over ``group`` and maps every peer's buffer.  Each
-    site keeps its own epoch counter on the device, so calls of one site may be captured in a
-    CUDA graph and replayed.  ``close()`` is collective too: it waits for every rank's last merge,
-    then unmaps the peers' buffers.
+    site's buffer keeps its own per-row call counters on the device, so calls of one site may be
+    captured in a CUDA graph and replayed.  A site serves either the standalone exchange
+    (``merge``) or the attention launch that exchanges in its split merge (``table``), with the
+    same rows.  ``close()`` is collective too: it waits for every rank's last exchange, then
+    unmaps the peers' buffers.
     """
 
     def __init__(self, rows: int, head_dim: int, *, rank: int, world: int, device, group=None, sites: int = 1):
@@ -140,14 +142,17 @@ class PeerExchange:
         self.group = group
         self.peer_tables = torch.tensor([[b + s * self.site_bytes for b in bases] for s in range(sites)],
                                         dtype=torch.int64, device=self.device)
-        self.epochs = torch.zeros(sites, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def table(self, site: int) -> tuple[torch.Tensor, int, int]:
+        """``(peer_table, rank, world)`` of ``site``: the ``exchange`` argument of ``cabi.decode_attention``."""
+        return self.peer_tables[site], self.rank, self.world
 
     def merge(self, site: int, part_out: torch.Tensor, part_lse: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
         """This rank's partial ``[R, D]`` / ``[R]`` in, every rank's merged output ``[R, D]`` out."""
         return self.cabi.xrank_lse_merge(part_out.reshape(self.rows, self.head_dim), part_lse.reshape(self.rows),
-                                         self.peer_tables[site], self.rank, self.world,
-                                         self.epochs[site:site + 1], dtype=dtype, device_status=self.status)
+                                         self.peer_tables[site], self.rank, self.world, dtype=dtype,
+                                         device_status=self.status)
 
     def close(self) -> None:
         if self._imported:
@@ -182,8 +187,10 @@ class ContextParallelDecoder:
         self.paged = None
         self.range = (0, 0)
         self._ws = None
-        # the NVLink exchange (call site `site` of it) in place of the NCCL all-gather, when given
+        # the NVLink exchange (call site `site` of it) in place of the NCCL all-gather, when given:
+        # inside the attention's split merge (fused_exchange) or as its own kernel after it
         self.exchange, self.site = exchange, site
+        self.fused_exchange = True
 
     def prefill(self, keys: torch.Tensor, values: torch.Tensor, *, capacity_tokens: int | None = None,
                 page_seed: int | None = None) -> None:
@@ -254,7 +261,16 @@ class ContextParallelDecoder:
     def _exchange(self, out_f32: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
         return self.exchange.merge(self.site, out_f32, lse, dtype=self.out_dtype)
 
+    def _fused(self, q: torch.Tensor) -> torch.Tensor:
+        """Partial attention whose split merge exchanges the rows over NVLink: one launch pair."""
+        return self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
+                                               self.head_dim ** -0.5, workspace=self._workspace(q),
+                                               exchange=self.exchange.table(self.site),
+                                               device_status=self.exchange.status)
+
     def decode(self, q: torch.Tensor) -> torch.Tensor:
+        if self.exchange is not None and self.world > 1 and q.dtype == self.out_dtype and self.fused_exchange:
+            return self._fused(q).reshape(q.shape)
         # one rank with the output in the query's dtype: the kernel writes the output itself
         single = self._single if q.dtype == self.out_dtype else None
         exchange = self._exchange if self.exchange is not None else None

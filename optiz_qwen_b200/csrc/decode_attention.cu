@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
     }
   }
   const int outputs = G * kHeadDim;
-  const bool single = nsplit_b == 1;
+  const bool single = nsplit_b == 1 && p.xr.world == 0;  // (an exchange always goes through the merge kernel)
   __syncthreads();
 
   // per head, over every warp of every group: M = the largest reference max, L = the sums at
@@ -744,12 +744,15 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
   const int G = p.group;
   const int64_t b = unit / p.num_kv_heads;
   const int kvh = int(unit - b * p.num_kv_heads);
+  // the exchange's epoch of this CTA's row: written by this call site's previous merge launch,
+  // which is at least two launches back (the attention kernel of this call runs in between)
+  const uint32_t e = p.xr.world > 0 ? xrank_epoch(p.xl, p.xr, int(unit) * G + h) : 0u;
   pdl_wait();
   pdl_allow_next();
   const int len = max(p.seq_lens[b], 0);
   const int npages_b = int(min(int64_t((len + kPage - 1) / kPage), p.max_pages));
   const int nsplit = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
-  if (nsplit == 1) return;  // the attention kernel wrote this unit's output itself
+  if (nsplit == 1 && p.xr.world == 0) return;  // the attention kernel wrote this unit's output itself
   const int tid = threadIdx.x;
   const int rec_floats = G * (kHeadDim + 2);
   const int outputs = G * kHeadDim;
@@ -792,7 +795,21 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
   }
   for (; s < nsplit; ++s) n0 = fmaf(sm_w[s], col[s * rec_floats], n0);
   const float num = (n0 + n1) + (n2 + n3);
-  store_out<T>(p, b, int64_t(kvh) * G + h, d, L > 0.0f ? num / L : 0.0f, M, L);
+  const int64_t hq = int64_t(kvh) * G + h;
+  if (p.xr.world == 0) {
+    store_out<T>(p, b, hq, d, L > 0.0f ? num / L : 0.0f, M, L);
+    return;
+  }
+  // ---- exchange this rank's merged row with every rank's over NVLink, then merge them: the
+  // values are those store_out would write to out_f32 / out_lse, merged as oq_lse_merge does
+  const int row = int(b * p.num_kv_heads * G + hq);
+  xrank_put(p.xl, p.xr, row, e, d, L > 0.0f ? num / L : 0.0f);
+  if (tid == 0) xrank_put(p.xl, p.xr, row, e, kHeadDim, lse_nat(M, L));
+  float lse_all;
+  const float y = xrank_merge(p.xl, p.xr, row, e, d, p.status, &lse_all);
+  if (p.out) static_cast<T*>(p.out)[b * p.o_sb + hq * p.o_sh + d] = from_float<T>(y);
+  if (p.out_f32) p.out_f32[(b * p.num_kv_heads * G + hq) * kHeadDim + d] = y;
+  if (p.out_lse && d == 0) p.out_lse[b * p.num_kv_heads * G + hq] = lse_all;
 }
 
 // ---------------------------------------------------------------- host side
@@ -910,7 +927,7 @@ int decode_attn_impl(
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
     const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
-    int32_t* device_status, void* stream) {
+    int32_t* device_status, void* stream, const XrankArgs* xr = nullptr) {
   const char* name = bits == 8 ? "decode_attn_int8_paged" : "decode_attn_int4_paged";
   if (gate && !out) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: a gate needs the model-dtype output", name);
   if (dtype != OQ_BF16 && dtype != OQ_F16) {
@@ -945,10 +962,18 @@ int decode_attn_impl(
   const int64_t units = batch * num_kv_heads;
   int pps = 0;
   int splits = decode_attn_plan(bits, dtype, group, batch, num_kv_heads, max_pages_per_seq, num_splits, &pps);
+  if (xr) {
+    if (gate) return fail(OQ_ERR_UNSUPPORTED, "%s: no gate with the cross-GPU exchange", name);
+    if (!xr->peers || xr->world <= 0 || xr->rank < 0 || xr->rank >= xr->world || xr->world > kXrankMaxWorld) {
+      return fail(OQ_ERR_INVALID_ARGUMENT, "%s: bad exchange rank / world / buffers", name);
+    }
+    if (batch * num_heads > (1 << 20)) return fail(OQ_ERR_UNSUPPORTED, "%s: too many rows to exchange", name);
+    if (!workspace) return fail(OQ_ERR_WORKSPACE, "%s: the exchange needs the split workspace", name);
+  }
 
-  if (splits > 1 || workspace) {
+  if (splits > 1 || workspace || xr) {
     const size_t need = oq_decode_attn_workspace_bytes(batch, num_heads, num_kv_heads, head_dim, splits);
-    if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
+    if ((splits > 1 || xr) && (workspace == nullptr || workspace_bytes < need)) {
       return fail(OQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed for %d splits", name, need,
                   splits);
     }
@@ -985,12 +1010,14 @@ int decode_attn_impl(
   p.max_splits = int(std::min<int64_t>(max_splits_ws, 1 << 20));
   p.pages_per_split = pps;
   // few splits: the last CTA of each (sequence, KV head) merges in-launch; many: a merge kernel
-  p.defer_merge = splits > kInLaunchMergeSplits ? 1 : 0;
+  p.defer_merge = (splits > kInLaunchMergeSplits || xr) ? 1 : 0;
   p.status = device_status;
   p.gate = gate;
   p.g_sb = gate_stride_b;
   p.g_sh = gate_stride_h;
   p.wait_polls = wait_polls();
+  p.xr = xr ? *xr : XrankArgs{nullptr, 0, 0, 0};
+  p.xl = XrankLayout{int(batch * num_heads), int(head_dim), xr ? xr->world : 0};
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1082,4 +1109,24 @@ extern "C" int oq_decode_attn_int8_paged_gated(
                               num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, nullptr,
                               nullptr, workspace, workspace_bytes, num_splits, gate, gate_stride_b, gate_stride_h,
                               device_status, stream);
+}
+
+extern "C" int oq_decode_attn_int4_paged_xrank(
+    const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits,
+    float* const* peer_buffers, int rank, int world,
+    int32_t* device_status, void* stream) {
+  const oq::XrankArgs xr{peer_buffers, rank, world, oq::xrank_polls()};
+  return oq::decode_attn_impl(4, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32,
+                              out_lse, workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream,
+                              &xr);
 }

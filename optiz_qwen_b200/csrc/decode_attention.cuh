@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "xrank.cuh"
 
 namespace oq {
 
@@ -44,6 +45,10 @@ struct AttnParams {
   const void* gate;
   int64_t g_sb, g_sh;
   int wait_polls;  // polls of a bounded wait on a page copy (wait_polls() at launch)
+  // optional cross-GPU exchange (xr.world > 0): the split merge publishes each merged row to
+  // every rank over NVLink, waits for theirs and writes the merge of all ranks (xrank.cuh)
+  XrankArgs xr;
+  XrankLayout xl;
 };
 
 // The partition a decode-attention launch uses (host side): the number of KV ranges per

@@ -57,20 +57,26 @@ def _rank(rank, world, port, outdir):
     dec = ContextParallelDecoder(2, 256, rank=rank, world=world, device=dev, exchange=ex)
     dec.prefill(torch.from_numpy(k).to(torch.bfloat16), torch.from_numpy(v).to(torch.bfloat16), capacity_tokens=16)
 
+    ex2 = PeerExchange(8, 256, rank=rank, world=world, device=dev, sites=1)
+
     def both(qs):
         dec.exchange = None                                   # NCCL all-gather + oq_lse_merge
         a = dec.decode(qs).float().cpu().numpy()
-        dec.exchange = ex                                     # NVLink exchange kernel
+        dec.exchange, dec.fused_exchange = ex, False          # standalone NVLink exchange kernel
         b = dec.decode(qs).float().cpu().numpy()
         c = dec.decode(qs).float().cpu().numpy()              # second call: the other slot parity
-        return np.stack([a, b, c])
+        dec.exchange, dec.fused_exchange = ex2, True          # exchange inside the split merge
+        d = dec.decode(qs).float().cpu().numpy()
+        e = dec.decode(qs).float().cpu().numpy()
+        return np.stack([a, b, c, d, e])
 
     outs = [both(torch.from_numpy(q[0]).to(dev, torch.bfloat16))]
     knt = torch.from_numpy(kn).to(dev, torch.bfloat16)
     dec.append(knt, knt)
     outs.append(both(torch.from_numpy(q[1]).to(dev, torch.bfloat16)))
-    status = int(ex.status.item())
+    status = int(ex.status.item()) | int(ex2.status.item())
     ex.close()
+    ex2.close()
     np.save(os.path.join(outdir, f"out{rank}.npy"), np.stack(outs))
     np.save(os.path.join(outdir, f"status{rank}.npy"), np.array([status]))
     dist.destroy_process_group()
@@ -103,13 +109,18 @@ def test_long_context_split_over_two_gpus_matches_one_gpu_and_oracle():
     vd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(np.concatenate([v, kn], axis=2)))[0]
     ref0, _ = decode_attention(q[0], [kd[:, :LENGTH]], [vd[:, :LENGTH]], 1 / 16)
     ref1, _ = decode_attention(q[1], [kd], [vd], 1 / 16)
-    for out in outs:                               # out [step, exchange (nccl, nvlink, nvlink), B, Hq, D]
-        for x in range(3):
+    for out in outs:           # out [step, exchange (nccl, standalone x2, in-merge x2), B, Hq, D]
+        for x in range(5):
             assert_attn_close(out[0, x], ref0)
             assert_attn_close(out[1, x], ref1)
             assert_attn_close(out[0, x], single0)
-        assert np.array_equal(out[:, 0], out[:, 1])   # NVLink exchange == NCCL path, bit for bit
-        assert np.array_equal(out[:, 1], out[:, 2])
+        # the standalone exchange merges the same partials as the NCCL path: bit for bit
+        for x in (1, 2):
+            assert np.array_equal(out[:, 0], out[:, x]), f"standalone exchange call {x} differs from NCCL"
+        # the in-merge exchange takes its partial from the split-merge kernel (another order of the
+        # local split sums than the in-launch merge): repeatable, and within fp32 rounding of NCCL
+        assert np.array_equal(out[:, 3], out[:, 4])
+        np.testing.assert_allclose(out[:, 3], out[:, 0], rtol=2 ** -7, atol=1e-5)
     assert np.array_equal(outs[0], outs[1])        # every rank holds the same merged output
 
 
@@ -143,7 +154,8 @@ def test_one_rank_path_matches_partial_and_merge_and_oracle():
 
 def test_exchange_kernel_one_rank_matches_lse_merge_in_graph_replays():
     """The exchange kernel with one rank: the merge of a single partial, bit-identical to
-    oq_lse_merge, over eager calls and CUDA graph replays (the epoch advances on the device)."""
+    oq_lse_merge, over eager calls and CUDA graph replays (the per-row call counters advance on
+    the device)."""
     from optiz_qwen_b200 import cabi
     from optiz_qwen_b200.context_parallel import PeerExchange
 
@@ -167,5 +179,52 @@ def test_exchange_kernel_one_rank_matches_lse_merge_in_graph_replays():
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, ref)
-    assert ex.epochs.tolist() == [2, 4]        # site 0: 2 eager calls; site 1: 1 eager call + 3 replays
     assert int(ex.status.item()) == 0
+
+
+@pytest.mark.parametrize("length", [3000, 40000])
+def test_attention_with_exchange_one_rank_matches_oracle(length):
+    """The attention launch whose split merge exchanges the rows (one rank): against the oracle
+    and the plain launch, over eager calls and CUDA graph replays (both slot parities)."""
+    from oracle import kv_quant as kq
+    from oracle.attention import decode_attention
+    from optiz_qwen_b200 import cabi
+    from optiz_qwen_b200.compression.paged_kv import PagedKvState
+    from optiz_qwen_b200.context_parallel import PeerExchange
+    from tests._util import assert_attn_close
+
+    rng = np.random.default_rng(length)
+    k = kq.round_bf16(rng.standard_normal((1, 2, length, 256), dtype=np.float32))
+    v = kq.round_bf16(rng.standard_normal((1, 2, length, 256), dtype=np.float32))
+    q = kq.round_bf16(rng.standard_normal((1, 8, 256), dtype=np.float32))
+    pages = -(-length // 64)
+    pool = cabi.PagedKvPool(pages + 1, 2, 256, 64, "cuda")
+    paged = PagedKvState(pool, 1, max_pages=pages)
+    paged.append(torch.from_numpy(k).cuda().to(torch.bfloat16), torch.from_numpy(v).cuda().to(torch.bfloat16))
+    kd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(k))[0]
+    vd = kq.dequantize_tokens_int4(*kq.quantize_tokens_int4(v))[0]
+    ref, _ = decode_attention(q, [kd], [vd], 1 / 16)
+    qt = torch.from_numpy(q).cuda().to(torch.bfloat16)
+    ws = cabi.new_decode_workspace(1, 8, 2, pages, "cuda")
+    ex = PeerExchange(8, 256, rank=0, world=1, device="cuda")
+    plain = cabi.decode_attention_int4(qt, pool, paged.block_table, paged.seq_lens, 1 / 16, workspace=ws)
+
+    def fused():
+        return cabi.decode_attention_int4(qt, pool, paged.block_table, paged.seq_lens, 1 / 16, workspace=ws,
+                                          exchange=ex.table(0), device_status=ex.status)
+
+    outs = [fused(), fused()]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        g_out = fused()
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        outs.append(g_out.clone())
+    assert int(ex.status.item()) == 0
+    for o in outs:
+        assert torch.equal(o, outs[0])
+        assert_attn_close(o.float().cpu().numpy(), ref)
+        assert_attn_close(o.float().cpu().numpy(), plain.float().cpu().numpy())
