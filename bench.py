@@ -460,6 +460,12 @@ def run_b200(args):
     if args.workload == "hybrid" and not args.no_sub_records:
         extra["serving"] = measure_serving(args, world, rank, device, dist, hbm_peak)
         extra["longctx"] = measure_longctx(args, world, rank, device, dist, hbm_peak)
+        pre = measure_prefill(args, world, rank, device, dist, hbm_peak, peak_src, 3)
+        rf = pre["roofline"]
+        extra["prefill"] = {"workload": pre["config"]["workload"], "scaling": "weak", "steps": pre["steps"],
+                            "ms_per_step": pre["ms_per_step"], "tokens_per_s": pre["value"],
+                            "us_per_layer": rf["us_per_launch"], "GB_s": rf["achieved"], "hbm_frac": rf["frac"],
+                            "tensor": rf["tensor"], "decode_tail": pre["decode_tail"], "e2e": pre["e2e"]}
     clocks.__exit__(None, None, None)
 
     step_bytes = counts.attn_bytes + counts.gdn_bytes + counts.append_bytes
@@ -698,19 +704,32 @@ def prefill_cpu_baseline(budget_s: float, t: int = 512):
 
 
 def run_prefill(args):
-    """Config 4: chunked GDN prefill (B=8, T=8192, H=16, d=128, 18 layers) on the tensor cores, then
-    256 recurrent decode steps from the prefill's final states.  Weak scaling: every rank runs its own
-    batch of 8 sequences, with no data-path collective."""
+    """Config 4 on its own (``--workload prefill``): see ``measure_prefill``."""
     import torch
-
-    from optiz_qwen_b200 import cabi
-    from optiz_qwen_b200.gdn.gated_delta_rule import chunk_gated_delta_rule
 
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist = init_pg(world, local)
     hbm_peak, peak_src = peaks()
+    line = measure_prefill(args, world, rank, device, dist, hbm_peak, peak_src, max(3, min(args.steps, 40)))
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = prefill_cpu_baseline(min(args.cpu_seconds, 15.0))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def measure_prefill(args, world, rank, device, dist, hbm_peak, peak_src, steps: int) -> dict:
+    """Config 4: chunked GDN prefill (B=8, T=8192, H=16, d=128, 18 layers) on the tensor cores, then
+    256 recurrent decode steps from the prefill's final states.  Weak scaling: every rank runs its own
+    batch of 8 sequences, with no data-path collective.  Returns the bench line (no CPU baseline)."""
+    import torch
+
+    from optiz_qwen_b200 import cabi
+    from optiz_qwen_b200.gdn.gated_delta_rule import chunk_gated_delta_rule
+
     tflops_peak = None
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -754,7 +773,6 @@ def run_prefill(args):
         graphs["prefill"].replay()
         graphs["decode"].replay()
     barrier(dist, device)
-    steps = max(3, min(args.steps, 40))
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     with ClockSampler(device.index if world == 1 else local) as clocks:
         ev[0].record()
@@ -823,13 +841,9 @@ def run_prefill(args):
                                 "frac": round(tflops / tflops_peak, 4) if tflops_peak else None,
                                 "algorithmic_flops_per_launch": flops_layer}},
     }
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = prefill_cpu_baseline(min(args.cpu_seconds, 15.0))
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     del graphs
-    if dist is not None:
-        dist.destroy_process_group()
+    torch.cuda.synchronize(device)
+    return line
 
 
 def main(argv=None):
