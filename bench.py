@@ -61,6 +61,10 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kv-bits", type=int, choices=[4, 8], default=4,
                     help="hybrid/serving: width of the paged KV cache codes (8: the reference's k_bits=8 preset)")
+    ap.add_argument("--append", choices=["fused", "separate"], default="fused",
+                    help="the new token's append-quantize: inside the attention launch, or its own launch")
+    ap.add_argument("--no-early-attn", action="store_true",
+                    help="launch attention only after the GDN layer ahead of it has finished")
     ap.add_argument("--conv", choices=["separate", "fused"], default=None,
                     help="hybrid/serving: feed each GDN layer its raw projection output and run its causal conv1d "
                          "update (separate kernel, or fused into the GDN step)")
@@ -194,6 +198,10 @@ def serving_lengths(batch=1024, lo=256, hi=8192, seed=3):
     return np.random.default_rng(seed).integers(lo, hi + 1, size=batch).tolist()
 
 
+APPEND_DESC = {"fused": "the new token quantised into the cache by the attention launch itself",
+               "separate": "the new token quantised into the cache by its own append launch"}
+
+
 def build_stack(args, world, rank, device):
     from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
     from optiz_qwen_b200.serving import shard_by_cost
@@ -202,9 +210,10 @@ def build_stack(args, world, rank, device):
         bsz = 8 if args.small else 64   # (--small: the profiling case, B = 8)
         shape = HybridShape(batch=bsz, context=4096)
         stack = HybridDecodeStack(shape, device=device, seed=1 + rank, page_seed=1, conv=args.conv,
-                                  epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates)
+                                  epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates,
+                                  fused_append=args.append == "fused", early_attention=not args.no_early_attn)
         desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
-                "gdn_gates": GATES_DESC[args.gates],
+                "gdn_gates": GATES_DESC[args.gates], "append": APPEND_DESC[args.append],
                 "epilogues": EPILOGUES if args.epilogues else "none",
                 "workload": f"hybrid decode step: B={bsz} per GPU at context 4096, 24 layers = 18 Gated-DeltaNet "
                             "(16 heads x 128, fp32 state) + 6 full attention (Hq 8 / Hkv 2 / head_dim 256, "
@@ -218,9 +227,10 @@ def build_stack(args, world, rank, device):
     mine = [lengths[i] for i in shards[rank]]
     shape = HybridShape(batch=len(mine), context=mine)
     stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv,
-                              epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates)
+                              epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates,
+                              fused_append=args.append == "fused", early_attention=not args.no_early_attn)
     desc = {"gdn_conv": f"causal conv1d update ({args.conv})" if args.conv else "q/k/v given post-conv",
-            "gdn_gates": GATES_DESC[args.gates],
+            "gdn_gates": GATES_DESC[args.gates], "append": APPEND_DESC[args.append],
             "epilogues": EPILOGUES if args.epilogues else "none",
             "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
                         f"cost across GPUs, 24-layer hybrid hot path, INT{args.kv_bits} paged KV", "global_batch": 1024,
@@ -430,9 +440,11 @@ def run_b200(args):
     # per-kernel device time: graphs holding only one kernel kind, same shapes and state
     kernels = {}
     reps = max(20, min(200, args.steps // 5))
-    for kind, name, launches in (("gdn", "gdn_recurrent", len(stack.gdn)),
-                                 ("attn", f"decode_attn_int{stack.kv_bits}_paged", len(stack.attn)),
-                                 ("append", f"append_quant_int{stack.kv_bits}", len(stack.attn))):
+    kinds = [("gdn", "gdn_recurrent", len(stack.gdn)),
+             ("attn", f"decode_attn_int{stack.kv_bits}_paged", len(stack.attn))]
+    if not stack.fused_append:
+        kinds.append(("append", f"append_quant_int{stack.kv_bits}", len(stack.attn)))
+    for kind, name, launches in kinds:
         g = stack.capture((kind,))
         for _ in range(3):
             g.replay()

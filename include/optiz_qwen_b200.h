@@ -62,6 +62,16 @@ enum oq_gdn_flags {
   OQ_GDN_STATE_PREFETCH = 1
 };
 
+/* Flags of oq_decode_attn_paged_append and oq_decode_attn_int4_paged_xrank. */
+enum oq_attn_flags {
+  /* Launch with programmatic stream serialisation and read seq_lens, the block table and the
+   * cached pages (all but the page that receives an appended token) before the kernel ahead
+   * in the stream has finished: set only when that kernel writes none of them (in a decode
+   * step: the previous layer's kernels).  The query, the appended key / value and the gate
+   * are always read after it finishes, and every write comes after that too. */
+  OQ_ATTN_EARLY = 1
+};
+
 /* Static description of an oq_status value. */
 const char* oq_status_string(int status);
 /* Detail of the last failing call on this host thread ("" when none). */
@@ -206,6 +216,31 @@ int oq_decode_attn_int8_paged_gated(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream);
 
+/* Append + attend in one launch (no reference counterpart as one call: it fuses the cache
+ * layer's update -- QServeAttentionLayer._append_decode_token / _quantize_groupwise,
+ * qserve_kv_cache.py:200-232, 313-335 -- with the decode attention that follows it,
+ * qserve_int4_attention.py:520-545, 576-620).  The token new_key / new_value [batch,
+ * num_kv_heads, head_dim] (query dtype, last dim contiguous, rows 16-byte aligned) is
+ * quantised into the `bits`-bit cache (4 or 8) at position seq_lens[b], with the same codes
+ * and fp16 scale / min as oq_append_quant_int4 / _int8, and the query attends over the
+ * seq_lens[b] + 1 tokens.  seq_lens is not modified (advance it with oq_advance_seq_lens, or
+ * keep it to hold the context).  gate may be NULL (else as oq_decode_attn_int4_paged_gated:
+ * out only); other arguments as oq_decode_attn_int4_paged; flags: OQ_ATTN_EARLY or 0. */
+int oq_decode_attn_paged_append(
+    int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
+    const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits, int flags,
+    int32_t* device_status, void* stream);
+
 /* Same attention, for callers that cannot allocate device memory (no counterpart
  * in the reference, which only runs inside PyTorch's allocator).  A decode loop
  * embedded in a host runtime whose arena owns all device memory, or a
@@ -288,7 +323,7 @@ int oq_decode_attn_int4_paged_xrank(
     void* out, int64_t out_stride_b, int64_t out_stride_h,
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
-    float* const* peer_buffers, int rank, int world,
+    float* const* peer_buffers, int rank, int world, int flags,
     int32_t* device_status, void* stream);
 
 /* ------------------------------------------------------------------ paged gather

@@ -23,6 +23,7 @@ OQ_ERR_CUDA = 5
 
 OQ_F32, OQ_F16, OQ_BF16 = 0, 1, 2
 OQ_DEV_BAD_PAGE, OQ_DEV_OVERFLOW, OQ_DEV_TIMEOUT = 1, 2, 4
+OQ_ATTN_EARLY = 1
 
 _DTYPES = {torch.float32: OQ_F32, torch.float16: OQ_F16, torch.bfloat16: OQ_BF16}
 
@@ -60,7 +61,10 @@ SIGNATURES = {
     "oq_xrank_lse_merge": (i32, [p, p, i64, i64, p, i32, i32, p, i32, p, p, p]),
     "oq_decode_attn_int4_paged_xrank": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                               i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, i32, i32,
-                                              p, p]),
+                                              i32, p, p]),
+    "oq_decode_attn_paged_append": (i32, [i32, p, i32, i64, i64, p, i64, i64, p, i64, i64, p, p, i64, i64,
+                                          p, i64, i64, p, i64, i64, i64, i64, f32, p, i64, i64, p, i64, i64,
+                                          p, p, p, sz, i32, i32, p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gather_dequant_int8": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),
     "oq_gdn_recurrent": (i32, [p, p, p, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,

@@ -142,7 +142,9 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
                      out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
                      workspace: torch.Tensor | None = None, num_splits: int = 0,
                      device_status: torch.Tensor | None = None, want_out: bool = True,
-                     gate: torch.Tensor | None = None, exchange: tuple | None = None, _bits: int | None = None):
+                     gate: torch.Tensor | None = None, exchange: tuple | None = None,
+                     new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
+                     early: bool = False, _bits: int | None = None):
     """One-token attention of ``query`` ``[B, Hq, D]`` over the paged cache (4- or 8-bit codes,
     as the pool holds: ``oq_decode_attn_int{4,8}_paged``).
 
@@ -153,7 +155,12 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
     pools; ``peer_table``: int64 device tensor of the ``world`` NVLink receive buffers of this
     call site) this rank's KV range is attended and the split merge exchanges every merged row
     with the other ranks in the same launch: the outputs are the merge over all ranks
-    (``oq_decode_attn_int4_paged_xrank``).
+    (``oq_decode_attn_int4_paged_xrank``).  With ``new_key`` / ``new_value`` ``[B, Hkv, D]`` (query
+    dtype) the launch first quantises that token into the cache at position ``seq_lens[b]`` and
+    attends over ``seq_lens[b] + 1`` tokens; ``seq_lens`` is left as it is
+    (``oq_decode_attn_paged_append``).  ``early``: launch before the kernel ahead in the stream
+    has finished and read the lengths, the block table and the cached pages meanwhile; only
+    when that kernel writes none of them (``OQ_ATTN_EARLY``).
     """
     require_cuda(query, block_table, seq_lens)
     entry = _bits_entry("decode_attn", pool, _bits) + "_paged"
@@ -174,12 +181,32 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
     for t, shape in ((out_f32, (b, hq, d)), (out_lse, (b, hq))):
         if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous()):
             raise ValueError("out_f32 / out_lse must be contiguous fp32 of shape [B, Hq, D] / [B, Hq]")
+    flags = _lib.OQ_ATTN_EARLY if early else 0
     if gate is not None:
         require_cuda(gate)
         if gate.dtype != query.dtype or tuple(gate.shape) != (b, hq, d) or gate.stride(2) != 1:
             raise ValueError("gate must be [B, Hq, D] in the query dtype with unit stride along D")
         if out is None or out_f32 is not None or out_lse is not None:
             raise ValueError("a gated call writes the query-dtype output only")
+    if new_key is not None or new_value is not None:
+        if exchange is not None:
+            raise ValueError("an appended token with the cross-GPU exchange is not supported")
+        require_cuda(new_key, new_value)
+        hkv = pool.num_kv_heads
+        for t in (new_key, new_value):
+            if t is None or t.dtype != query.dtype or t.dim() != 3 or tuple(t.shape) != (b, hkv, d) or t.stride(2) != 1:
+                raise ValueError("new_key / new_value must be [B, Hkv, D] in the query dtype with unit stride along D")
+        call("oq_decode_attn_paged_append", pool.bits, ptr(query), dtype_code(query.dtype), query.stride(0),
+             query.stride(1), ptr(new_key), new_key.stride(0), new_key.stride(1), ptr(new_value), new_value.stride(0),
+             new_value.stride(1), ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+             ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
+             b, hq, hkv, d, float(scaling), ptr(gate), gate.stride(0) if gate is not None else 0,
+             gate.stride(1) if gate is not None else 0,
+             ptr(out), out.stride(0) if out is not None else 0, out.stride(1) if out is not None else 0,
+             ptr(out_f32), ptr(out_lse), ptr(workspace), workspace.numel(), int(num_splits), flags,
+             ptr(device_status), stream_ptr(query.device))
+        return out
+    if gate is not None:
         call(entry + "_gated", ptr(query), dtype_code(query.dtype), query.stride(0),
              query.stride(1), ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
              ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
@@ -200,7 +227,7 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
              b, hq, pool.num_kv_heads, d, float(scaling),
              ptr(out), out.stride(0) if out is not None else 0, out.stride(1) if out is not None else 0,
              ptr(out_f32), ptr(out_lse), ptr(workspace), workspace.numel(), int(num_splits),
-             ptr(peer_table), int(rank), int(world), ptr(device_status), stream_ptr(query.device))
+             ptr(peer_table), int(rank), int(world), flags, ptr(device_status), stream_ptr(query.device))
         return out
     call(entry, ptr(query), dtype_code(query.dtype), query.stride(0), query.stride(1),
          ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,

@@ -10,7 +10,7 @@
 // (the reference's bits=8 path: 255 levels, one code per byte) shares the kernel.
 #include <algorithm>
 
-#include "common.cuh"
+#include "quant_row.cuh"
 
 namespace oq {
 namespace {
@@ -32,25 +32,6 @@ struct AppendParams {
   int32_t* status;
 };
 
-template <typename T, int EPL, bool VEC>
-__device__ __forceinline__ void load_row(const T* row, int lane, float (&x)[EPL]) {
-  const T* p = row + lane * EPL;
-  if constexpr (VEC && (EPL * sizeof(T)) % 16 == 0) {
-    constexpr int kVecs = EPL * sizeof(T) / 16;
-    constexpr int kPer = 16 / sizeof(T);
-#pragma unroll
-    for (int v = 0; v < kVecs; ++v) {
-      uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + v);
-      const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) x[v * kPer + i] = to_float<T>(e[i]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) x[i] = to_float<T>(p[i]);
-  }
-}
-
 // One (token, head, K|V) row per warp; head_dim = 32 * EPL; codes of kBits bits.
 template <typename T, int EPL, bool VEC, int kBits>
 __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams p) {
@@ -63,8 +44,6 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
   const int64_t jobs = p.num_kv_heads * p.num_new * 2;
   constexpr int kHeadDim = EPL * 32;
   constexpr int kRowBytes = kHeadDim * kBits / 8;
-  constexpr float kLevels = float((1 << kBits) - 1);
-  constexpr int kLaneBytes = EPL * kBits / 8;
 
   for (int64_t job = int64_t(blockIdx.x) * kWarps + warp; job < jobs; job += int64_t(gridDim.x) * kWarps) {
     const int kv = int(job & 1);
@@ -86,49 +65,10 @@ __global__ void __launch_bounds__(kWarps * 32) append_quant_kernel(AppendParams 
 
     const T* src = static_cast<const T*>(kv ? p.value : p.key) + b * p.stride[kv][0] + h * p.stride[kv][1] +
                    t * p.stride[kv][2];
-    float x[EPL];
-    load_row<T, EPL, VEC>(src, lane, x);
-
-    float mn = x[0], mx = x[0];
-#pragma unroll
-    for (int i = 1; i < EPL; ++i) {
-      mn = fminf(mn, x[i]);
-      mx = fmaxf(mx, x[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    }
-    // scale = (max - min) / levels in fp32; 1 where it is not positive (qserve_kv_cache.py:326-328)
-    float scale = __fdiv_rn(__fsub_rn(mx, mn), kLevels);
-    if (!(scale > 0.0f)) scale = 1.0f;
-
-    constexpr int kWords = kLaneBytes / 4 > 0 ? kLaneBytes / 4 : 1;
-    constexpr int kPerWord = 32 / kBits;
-    uint32_t packed[kWords] = {};
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      float c = rintf(__fdiv_rn(__fsub_rn(x[i], mn), scale));
-      c = fminf(fmaxf(c, 0.0f), kLevels);
-      packed[i / kPerWord] |= static_cast<uint32_t>(c) << (kBits * (i % kPerWord));
-    }
-
     const int64_t block = (page * p.num_kv_heads + h) * 2 + kv;
-    uint8_t* row = p.kv_codes + (block * p.page_size + slot) * kRowBytes + lane * kLaneBytes;
-    if constexpr (kLaneBytes >= 4) {
-#pragma unroll
-      for (int w = 0; w < kLaneBytes / 4; ++w) reinterpret_cast<uint32_t*>(row)[w] = packed[w];
-    } else if constexpr (kLaneBytes == 2) {
-      *reinterpret_cast<uint16_t*>(row) = static_cast<uint16_t>(packed[0]);
-    } else {
-      *row = static_cast<uint8_t>(packed[0]);
-    }
-    if (lane == 0) {
-      uint16_t* meta = p.kv_meta + ((page * p.num_kv_heads + h) * 4 + kv * 2) * p.page_size + slot;
-      meta[0] = __half_as_ushort(__float2half_rn(scale));
-      meta[p.page_size] = __half_as_ushort(__float2half_rn(mn));
-    }
+    quantize_row<T, EPL, VEC, kBits>(src, lane, p.kv_codes + (block * p.page_size + slot) * kRowBytes,
+                                     p.kv_meta + ((page * p.num_kv_heads + h) * 4 + kv * 2) * p.page_size + slot,
+                                     p.page_size);
   }
   if (p.advance) {
     __syncthreads();  // every warp has read seq_lens[b]

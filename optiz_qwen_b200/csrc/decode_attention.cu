@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "decode_attention.cuh"
+#include "quant_row.cuh"
 
 namespace oq {
 namespace {
@@ -182,22 +183,34 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   // four lanes (r, 0..3) hold the whole head.
   const int f_head = kDual ? r : (r >> 1);
   const bool f_has = f_head < G;
-  pdl_wait();  // (one long wave: the successor is allowed to launch only after the page loop)
-  const int32_t len_raw = p.seq_lens[b];
-  const int first_pre = pre_ok ? bt_row[page_at(lane)] : -1;
   uint4 qv[8];
-  {
+  auto load_q = [&]() {
     const T* qrow = static_cast<const T*>(p.query) + b * p.q_sb + int64_t(kvh * G + (f_has ? f_head : 0)) * p.q_sh +
                     64 * c;
 #pragma unroll
     for (int i = 0; i < 8; ++i) qv[i] = f_has ? __ldg(reinterpret_cast<const uint4*>(qrow + 8 * i)) : make_uint4(0, 0, 0, 0);
+  };
+  // Early launch (p.early): this CTA may run while the kernel ahead of it in the stream still
+  // does, which by the caller's contract writes neither the cache, the block table nor
+  // seq_lens.  Everything up to the first page copies then happens before the dependency wait;
+  // the query, the appended token and every write come after it.  A plain launch waits first
+  // (a no-op) and loads the query with the lengths.  (One long wave: the successor is allowed
+  // to launch only after the page loop.)
+  if (!p.early) {
+    pdl_wait();
+    load_q();
   }
+  const int32_t len_raw = p.seq_lens[b];
+  const int first_pre = pre_ok ? bt_row[page_at(lane)] : -1;
   if (tid == 0) {
     for (int s2 = 0; s2 < kSt; ++s2) mbar_init(&tail->full[s2], 1);
     fence_mbar_init();
   }
 
-  const int len = max(len_raw, 0);
+  // With an appended token (p.append) the sequence holds len_raw + 1 tokens: the new one, at
+  // position len_raw of logical page lp_new, is quantised into the cache by this launch (warps 0
+  // and 1 of the group that owns that page) before any copy of that page is issued.
+  const int len = max(len_raw, 0) + (p.append ? 1 : 0);
   const int len_pages = (len + kPage - 1) / kPage;
   const int npages_b = int(min(int64_t(len_pages), p.max_pages));
   const int nsplit_b = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
@@ -205,11 +218,17 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
     pdl_allow_next();
     return;
   }
-  if (len_pages > p.max_pages && ctid == 0 && split == 0) report(p.status, OQ_DEV_OVERFLOW);
+  const bool overflow = len_pages > p.max_pages;
   const int cta_n = max(0, min(npages_b, cta_begin + p.pages_per_split) - cta_begin);
   // this group's share of the CTA's pages (an empty share is fine: m = -inf, l = 0)
   const int n = cta_n > wg ? (cta_n - wg + kWG - 1) / kWG : 0;
-  const int first_page = (warp == 0 && lane < min(n, kSt)) ? first_pre : -1;
+  const int lp_new = p.append ? (len - 1) / kPage : -1;
+  const int rel_new = lp_new - cta_begin;
+  // this group's index of the appended token's page, or -1
+  const int i_new = (p.append && lp_new < npages_b && rel_new >= 0 && rel_new < cta_n && rel_new % kWG == wg)
+                        ? rel_new / kWG : -1;
+  const int pid_new = (i_new >= 0 && warp < 2) ? bt_row[lp_new] : -1;
+  const int first_page = (warp == 0 && lane < min(n, kSt) && lane != i_new) ? first_pre : -1;
   // thread 0 loads the page id of the page it issues next one loop iteration ahead
   int next_pid = (tid == 0 && kSt < n) ? bt_row[page_at(kSt)] : 0;
 
@@ -237,9 +256,29 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
 #pragma unroll
     for (int i = 0; i < kSt; ++i) {
       const int page = __shfl_sync(0xffffffffu, first_page, i);
-      if (lane == 0 && i < n) issue(i, i, page);
+      if (lane == 0 && i < n && i != i_new) issue(i, i, page);  // (the appended token's page: below)
     }
     issued = min(n, kSt);
+  }
+  if (p.early) {
+    pdl_wait();
+    load_q();
+  }
+  if (overflow && ctid == 0 && split == 0) report(p.status, OQ_DEV_OVERFLOW);
+  if (i_new >= 0 && warp < 2) {
+    // the appended token: warp 0 quantises its K row, warp 1 its V row, into page pid_new
+    if (pid_new < 0 || pid_new >= p.num_pages) {
+      if (lane == 0) report(p.status, OQ_DEV_BAD_PAGE);
+    } else {
+      const int slot = (len - 1) - lp_new * kPage;
+      const int64_t blk = int64_t(pid_new) * p.num_kv_heads + kvh;
+      const T* src = static_cast<const T*>(warp == 0 ? p.new_k : p.new_v) + b * (warp == 0 ? p.nk_sb : p.nv_sb) +
+                     int64_t(kvh) * (warp == 0 ? p.nk_sh : p.nv_sh);
+      quantize_row<T, kHeadDim / 32, true, kBits>(src, lane, p.kv_codes + ((blk * 2 + warp) * kPage + slot) *
+                                                                               (kHeadDim * kBits / 8),
+                                                  p.kv_meta_w + (blk * 4 + 2 * warp) * kPage + slot, kPage);
+      asm volatile("fence.proxy.async.global;\n" ::: "memory");  // the page copy below reads these bytes
+    }
   }
 
   // ---- query digits (B operand of q.k).
@@ -321,6 +360,8 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
     }
   }
   named_bar_sync(bar_wg, kThreads);  // fragments written; the stage barriers are initialised
+  // the appended token's page, now that warps 0 and 1 have written its new row
+  if (tid == 0 && i_new >= 0 && i_new < kSt) issue(i_new, i_new, pid_new);
   // Heads of this lane's scores: (packed) head c, from columns 2c (d2 / d0) and 2c+1 (d1);
   // (dual) heads 2c and 2c+1.  Lane 8c (r = 2c) holds sum(q) and 2^-e of head c (packed) or
   // 2c (dual), lane 8c + 4 those of head 2c + 1 (dual).
@@ -749,7 +790,7 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
   const uint32_t e = p.xr.world > 0 ? xrank_epoch(p.xl, p.xr, int(unit) * G + h) : 0u;
   pdl_wait();
   pdl_allow_next();
-  const int len = max(p.seq_lens[b], 0);
+  const int len = max(p.seq_lens[b], 0) + (p.append ? 1 : 0);  // (the attention kernel's length)
   const int npages_b = int(min(int64_t((len + kPage - 1) / kPage), p.max_pages));
   const int nsplit = max(1, (npages_b + p.pages_per_split - 1) / p.pages_per_split);
   if (nsplit == 1 && p.xr.world == 0) return;  // the attention kernel wrote this unit's output itself
@@ -916,6 +957,14 @@ extern "C" size_t oq_decode_attn_workspace_bytes(int64_t batch, int64_t num_head
 namespace oq {
 namespace {
 
+// Options of the extended entry points: an appended token and launch flags.
+struct AttnExtras {
+  const void* new_k;
+  const void* new_v;
+  int64_t nk_sb, nk_sh, nv_sb, nv_sh;
+  int flags;
+};
+
 int decode_attn_impl(
     int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const uint8_t* kv_codes, const uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
@@ -927,8 +976,15 @@ int decode_attn_impl(
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
     const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
-    int32_t* device_status, void* stream, const XrankArgs* xr = nullptr) {
+    int32_t* device_status, void* stream, const XrankArgs* xr = nullptr, const AttnExtras* ex = nullptr) {
   const char* name = bits == 8 ? "decode_attn_int8_paged" : "decode_attn_int4_paged";
+  if (ex && ex->new_k) {
+    if (!ex->new_v) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: an appended token needs both key and value", name);
+    if (reinterpret_cast<uintptr_t>(ex->new_k) % 16 || reinterpret_cast<uintptr_t>(ex->new_v) % 16 ||
+        (ex->nk_sb * 2) % 16 || (ex->nk_sh * 2) % 16 || (ex->nv_sb * 2) % 16 || (ex->nv_sh * 2) % 16) {
+      return fail(OQ_ERR_MISALIGNED, "%s: appended key / value rows need 16-byte alignment", name);
+    }
+  }
   if (gate && !out) return fail(OQ_ERR_INVALID_ARGUMENT, "%s: a gate needs the model-dtype output", name);
   if (dtype != OQ_BF16 && dtype != OQ_F16) {
     return fail(OQ_ERR_UNSUPPORTED, "%s: query dtype must be bf16 or fp16", name);
@@ -1016,12 +1072,26 @@ int decode_attn_impl(
   p.g_sb = gate_stride_b;
   p.g_sh = gate_stride_h;
   p.wait_polls = wait_polls();
+  p.append = (ex && ex->new_k) ? 1 : 0;
+  p.new_k = ex ? ex->new_k : nullptr;
+  p.new_v = ex ? ex->new_v : nullptr;
+  p.nk_sb = ex ? ex->nk_sb : 0;
+  p.nk_sh = ex ? ex->nk_sh : 0;
+  p.nv_sb = ex ? ex->nv_sb : 0;
+  p.nv_sh = ex ? ex->nv_sh : 0;
+  p.kv_codes = const_cast<uint8_t*>(kv_codes);
+  p.kv_meta_w = const_cast<uint16_t*>(kv_meta);
+  p.early = (ex && (ex->flags & OQ_ATTN_EARLY)) ? 1 : 0;
   p.xr = xr ? *xr : XrankArgs{nullptr, 0, 0, 0};
   p.xl = XrankLayout{int(batch * num_heads), int(head_dim), xr ? xr->world : 0};
 
   dim3 grid((unsigned)splits, (unsigned)num_kv_heads, (unsigned)batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  launch_plain(kernel, grid, dim3(threads), smem_bytes, s, tmap, p);
+  if (p.early) {
+    launch_pdl(kernel, grid, dim3(threads), smem_bytes, s, tmap, p);
+  } else {
+    launch_plain(kernel, grid, dim3(threads), smem_bytes, s, tmap, p);
+  }
   if (p.defer_merge) {
     // early launch: the merge waits (griddepcontrol.wait) for the whole attention grid before
     // it reads a partial, and its launch gap overlaps the attention's epilogue
@@ -1121,12 +1191,40 @@ extern "C" int oq_decode_attn_int4_paged_xrank(
     void* out, int64_t out_stride_b, int64_t out_stride_h,
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits,
-    float* const* peer_buffers, int rank, int world,
+    float* const* peer_buffers, int rank, int world, int flags,
     int32_t* device_status, void* stream) {
   const oq::XrankArgs xr{peer_buffers, rank, world, oq::xrank_polls()};
+  const oq::AttnExtras ex{nullptr, nullptr, 0, 0, 0, 0, flags};
   return oq::decode_attn_impl(4, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
                               page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
                               num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32,
                               out_lse, workspace, workspace_bytes, num_splits, nullptr, 0, 0, device_status, stream,
-                              &xr);
+                              &xr, &ex);
+}
+
+extern "C" int oq_decode_attn_paged_append(
+    int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
+    const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
+    const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
+    uint8_t* kv_codes, uint16_t* kv_meta, int64_t num_pages, int64_t page_size,
+    const int32_t* block_table, int64_t block_table_stride, int64_t max_pages_per_seq,
+    const int32_t* seq_lens,
+    int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+    float scaling,
+    const void* gate, int64_t gate_stride_b, int64_t gate_stride_h,
+    void* out, int64_t out_stride_b, int64_t out_stride_h,
+    float* out_f32, float* out_lse,
+    void* workspace, size_t workspace_bytes, int num_splits, int flags,
+    int32_t* device_status, void* stream) {
+  if (bits != 4 && bits != 8) return oq::fail(OQ_ERR_UNSUPPORTED, "decode_attn_paged_append: bits must be 4 or 8");
+  if (!new_key || !new_value) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_append: null key / value");
+  if (gate && (out_f32 || out_lse)) {
+    return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_append: a gated call writes the query-dtype output only");
+  }
+  const oq::AttnExtras ex{new_key, new_value, key_stride_b, key_stride_h, value_stride_b, value_stride_h, flags};
+  return oq::decode_attn_impl(bits, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,
+                              page_size, block_table, block_table_stride, max_pages_per_seq, seq_lens, batch,
+                              num_heads, num_kv_heads, head_dim, scaling, out, out_stride_b, out_stride_h, out_f32,
+                              out_lse, workspace, workspace_bytes, num_splits, gate, gate_stride_b, gate_stride_h,
+                              device_status, stream, nullptr, &ex);
 }

@@ -45,6 +45,15 @@ struct AttnParams {
   const void* gate;
   int64_t g_sb, g_sh;
   int wait_polls;  // polls of a bounded wait on a page copy (wait_polls() at launch)
+  // optional appended token (append = 1): new_k / new_v [B, Hkv, 256] in the query dtype, written
+  // at position seq_lens[b] and attended with the seq_lens[b] cached tokens (see the kernel)
+  int append;
+  const void* new_k;
+  const void* new_v;
+  int64_t nk_sb, nk_sh, nv_sb, nv_sh;
+  uint8_t* kv_codes;     // the cache, for the appended token's writes
+  uint16_t* kv_meta_w;
+  int early;             // 1: launched early (programmatic stream serialisation), see the kernel
   // optional cross-GPU exchange (xr.world > 0): the split merge publishes each merged row to
   // every rank over NVLink, waits for theirs and writes the merge of all ranks (xrank.cuh)
   XrankArgs xr;

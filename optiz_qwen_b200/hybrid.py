@@ -127,7 +127,14 @@ class HybridDecodeStack:
 
     def __init__(self, shape: HybridShape, *, device="cuda", seed: int = 1, page_seed: int | None = 1,
                  hold_context: bool = True, extra_tokens: int = 0, dtype=torch.bfloat16,
-                 conv: str | None = None, epilogues: bool = False, kv_bits: int = 4, gates: str = "given"):
+                 conv: str | None = None, epilogues: bool = False, kv_bits: int = 4, gates: str = "given",
+                 fused_append: bool = True, early_attention: bool = True):
+        # fused_append: each attention layer's launch quantises the step's new token into the
+        # cache itself (oq_decode_attn_paged_append) instead of a separate append launch;
+        # early_attention: an attention launch right after a GDN layer starts early and loads
+        # its cached pages during that layer's tail (OQ_ATTN_EARLY: GDN launches write no cache data)
+        self.fused_append = fused_append
+        self.early_attention = early_attention
         if conv not in (None, "separate", "fused"):
             raise ValueError("conv must be None, 'separate' or 'fused'")
         if gates not in ("given", "fused") or (gates == "fused" and conv):
@@ -310,14 +317,25 @@ class HybridDecodeStack:
             if kind == "attn":
                 layer = self.attn[i]
                 p = layer.paged
-                if "append" in kinds:
-                    cabi.append_quant(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
-                                           advance=not self.hold_context)
-                    prev = ("append", i)
-                if "attn" in kinds:
-                    cabi.decode_attention(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
-                                               out=layer.out, workspace=layer.workspace, gate=layer.gate)
-                    prev = ("attn", i)
+                if self.fused_append:
+                    # one launch: the new token into the cache at write_pos, then attention over it
+                    if "attn" in kinds:
+                        early = self.early_attention and prev is not None and prev[0] == "gdn"
+                        cabi.decode_attention(layer.q, p.pool, p.block_table, layer.write_pos, scaling,
+                                              out=layer.out, workspace=layer.workspace, gate=layer.gate,
+                                              new_key=layer.k[:, :, 0], new_value=layer.v[:, :, 0], early=early)
+                        if not self.hold_context:
+                            cabi.advance_seq_lens(p.seq_lens)
+                        prev = ("attn", i)
+                else:
+                    if "append" in kinds:
+                        cabi.append_quant(layer.k, layer.v, p.pool, p.block_table, layer.write_pos,
+                                          advance=not self.hold_context)
+                        prev = ("append", i)
+                    if "attn" in kinds:
+                        cabi.decode_attention(layer.q, p.pool, p.block_table, layer.attend_lens, scaling,
+                                              out=layer.out, workspace=layer.workspace, gate=layer.gate)
+                        prev = ("attn", i)
             elif "gdn" in kinds:
                 layer = self.gdn[i]
                 # A layer's state is written only by its own launch one step earlier, so when the
@@ -456,13 +474,20 @@ class HybridDecodeStack:
         append_bytes_layer = s.batch * s.num_kv_heads * (2 * s.head_dim * 2 + self.kv_bytes_per_token_head)
         n_attn, n_gdn = len(self.attn), len(self.gdn)
         esize = self.in_dev.element_size()
+        attn_launches = (1 + (0 if self.hold_context else 1)) if self.fused_append else 2
+        per_kernel = {"gdn_recurrent": gdn_bytes_layer}
+        if self.fused_append:  # the attention launch also reads the new token and writes its codes
+            per_kernel[f"decode_attn_int{self.kv_bits}_paged"] = attn_bytes_layer + append_bytes_layer
+        else:
+            per_kernel[f"decode_attn_int{self.kv_bits}_paged"] = attn_bytes_layer
+            per_kernel[f"append_quant_int{self.kv_bits}"] = append_bytes_layer
         return StepCounts(
-            launches=2 * n_attn + n_gdn * ((2 if self.conv == "separate" else 1) + (1 if self.epilogues else 0)),
+            launches=attn_launches * n_attn
+            + n_gdn * ((2 if self.conv == "separate" else 1) + (1 if self.epilogues else 0)),
             attn_bytes=attn_bytes_layer * n_attn,
             gdn_bytes=gdn_bytes_layer * n_gdn,
             append_bytes=append_bytes_layer * n_attn,
             h2d_bytes=self.in_dev.numel() * esize,
             d2h_bytes=self.out_dev.numel() * esize,
-            per_kernel={f"decode_attn_int{self.kv_bits}_paged": attn_bytes_layer, "gdn_recurrent": gdn_bytes_layer,
-                        f"append_quant_int{self.kv_bits}": append_bytes_layer},
+            per_kernel=per_kernel,
         )

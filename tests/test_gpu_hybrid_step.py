@@ -28,12 +28,14 @@ def _gates(layer):
     return ogdn.decay_gates(f(layer.a), f(layer.b), f(layer.A_log), f(layer.dt_bias), rnd=kq.round_bf16)
 
 
-@pytest.mark.parametrize("gates", ["given", "fused"])
-def test_graph_step_matches_oracle(gates):
+@pytest.mark.parametrize("gates,fused_append", [("given", True), ("fused", True), ("given", False)])
+def test_graph_step_matches_oracle(gates, fused_append):
+    """The captured step against the oracle: fused or separate append, given or computed gates
+    (the fused append's attention launches start early after each GDN layer)."""
     from optiz_qwen_b200.hybrid import HybridDecodeStack, HybridShape
 
     shape = HybridShape(batch=3, context=[70, 130, 5], num_layers=8)
-    stack = HybridDecodeStack(shape, device="cuda", seed=3, gates=gates)
+    stack = HybridDecodeStack(shape, device="cuda", seed=3, gates=gates, fused_append=fused_append)
     stack.fill_inputs()
     states0 = [layer.state.cpu().numpy().copy() for layer in stack.gdn]
     graph = stack.capture()          # (the capture runs one eager step first)
