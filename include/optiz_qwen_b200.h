@@ -62,7 +62,7 @@ enum oq_gdn_flags {
   OQ_GDN_STATE_PREFETCH = 1
 };
 
-/* Flags of oq_decode_attn_paged_append and oq_decode_attn_int4_paged_xrank. */
+/* Flags of oq_decode_attn_paged_ex and oq_decode_attn_int4_paged_xrank. */
 enum oq_attn_flags {
   /* Launch with programmatic stream serialisation and read seq_lens, the block table and the
    * cached pages (all but the page that receives an appended token) before the kernel ahead
@@ -216,17 +216,19 @@ int oq_decode_attn_int8_paged_gated(
     void* workspace, size_t workspace_bytes, int num_splits,
     int32_t* device_status, void* stream);
 
-/* Append + attend in one launch (no reference counterpart as one call: it fuses the cache
- * layer's update -- QServeAttentionLayer._append_decode_token / _quantize_groupwise,
- * qserve_kv_cache.py:200-232, 313-335 -- with the decode attention that follows it,
- * qserve_int4_attention.py:520-545, 576-620).  The token new_key / new_value [batch,
- * num_kv_heads, head_dim] (query dtype, last dim contiguous, rows 16-byte aligned) is
- * quantised into the `bits`-bit cache (4 or 8) at position seq_lens[b], with the same codes
+/* Decode attention with the options of a decode step: an appended token, a gate and launch
+ * flags, over the `bits`-bit cache (4 or 8).  With new_key / new_value [batch, num_kv_heads,
+ * head_dim] (query dtype, last dim contiguous, rows 16-byte aligned) the launch is append +
+ * attend in one (no reference counterpart as one call: it fuses the cache layer's update --
+ * QServeAttentionLayer._append_decode_token / _quantize_groupwise, qserve_kv_cache.py:200-232,
+ * 313-335 -- with the decode attention that follows it, qserve_int4_attention.py:520-545,
+ * 576-620): the token is quantised into the cache at position seq_lens[b], with the same codes
  * and fp16 scale / min as oq_append_quant_int4 / _int8, and the query attends over the
  * seq_lens[b] + 1 tokens.  seq_lens is not modified (advance it with oq_advance_seq_lens, or
- * keep it to hold the context).  gate may be NULL (else as oq_decode_attn_int4_paged_gated:
- * out only); other arguments as oq_decode_attn_int4_paged; flags: OQ_ATTN_EARLY or 0. */
-int oq_decode_attn_paged_append(
+ * keep it to hold the context).  Both NULL: no token is appended.  gate may be NULL (else as
+ * oq_decode_attn_int4_paged_gated: out only); other arguments as oq_decode_attn_int4_paged;
+ * flags: OQ_ATTN_EARLY or 0. */
+int oq_decode_attn_paged_ex(
     int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
     const void* new_value, int64_t value_stride_b, int64_t value_stride_h,

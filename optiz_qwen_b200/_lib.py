@@ -62,7 +62,7 @@ SIGNATURES = {
     "oq_decode_attn_int4_paged_xrank": (i32, [p, i32, i64, i64, p, p, i64, i64, p, i64, i64, p,
                                               i64, i64, i64, i64, f32, p, i64, i64, p, p, p, sz, i32, p, i32, i32,
                                               i32, p, p]),
-    "oq_decode_attn_paged_append": (i32, [i32, p, i32, i64, i64, p, i64, i64, p, i64, i64, p, p, i64, i64,
+    "oq_decode_attn_paged_ex": (i32, [i32, p, i32, i64, i64, p, i64, i64, p, i64, i64, p, p, i64, i64,
                                           p, i64, i64, p, i64, i64, i64, i64, f32, p, i64, i64, p, i64, i64,
                                           p, p, p, sz, i32, i32, p, p]),
     "oq_gather_dequant_int4": (i32, [p, p, i64, i64, p, i64, i64, p, i64, i64, i64, i64, p, p, i32, p, p]),

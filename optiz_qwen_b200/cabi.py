@@ -158,7 +158,8 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
     (``oq_decode_attn_int4_paged_xrank``).  With ``new_key`` / ``new_value`` ``[B, Hkv, D]`` (query
     dtype) the launch first quantises that token into the cache at position ``seq_lens[b]`` and
     attends over ``seq_lens[b] + 1`` tokens; ``seq_lens`` is left as it is
-    (``oq_decode_attn_paged_append``).  ``early``: launch before the kernel ahead in the stream
+    (``oq_decode_attn_paged_ex``, which also serves ``early`` alone).  ``early``: launch before the kernel
+    ahead in the stream
     has finished and read the lengths, the block table and the cached pages meanwhile; only
     when that kernel writes none of them (``OQ_ATTN_EARLY``).
     """
@@ -188,17 +189,21 @@ def decode_attention(query: torch.Tensor, pool: PagedKvPool, block_table: torch.
             raise ValueError("gate must be [B, Hq, D] in the query dtype with unit stride along D")
         if out is None or out_f32 is not None or out_lse is not None:
             raise ValueError("a gated call writes the query-dtype output only")
-    if new_key is not None or new_value is not None:
+    if new_key is not None or new_value is not None or (early and exchange is None):
         if exchange is not None:
             raise ValueError("an appended token with the cross-GPU exchange is not supported")
         require_cuda(new_key, new_value)
         hkv = pool.num_kv_heads
-        for t in (new_key, new_value):
-            if t is None or t.dtype != query.dtype or t.dim() != 3 or tuple(t.shape) != (b, hkv, d) or t.stride(2) != 1:
-                raise ValueError("new_key / new_value must be [B, Hkv, D] in the query dtype with unit stride along D")
-        call("oq_decode_attn_paged_append", pool.bits, ptr(query), dtype_code(query.dtype), query.stride(0),
-             query.stride(1), ptr(new_key), new_key.stride(0), new_key.stride(1), ptr(new_value), new_value.stride(0),
-             new_value.stride(1), ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
+        if new_key is not None or new_value is not None:
+            for t in (new_key, new_value):
+                if (t is None or t.dtype != query.dtype or t.dim() != 3 or tuple(t.shape) != (b, hkv, d)
+                        or t.stride(2) != 1):
+                    raise ValueError("new_key / new_value must be [B, Hkv, D] in the query dtype with unit stride "
+                                     "along D")
+        ks = (new_key.stride(0), new_key.stride(1)) if new_key is not None else (0, 0)
+        vs = (new_value.stride(0), new_value.stride(1)) if new_value is not None else (0, 0)
+        call("oq_decode_attn_paged_ex", pool.bits, ptr(query), dtype_code(query.dtype), query.stride(0),
+             query.stride(1), ptr(new_key), ks[0], ks[1], ptr(new_value), vs[0], vs[1], ptr(pool.kv_codes), ptr(pool.kv_meta), pool.num_pages, pool.page_size,
              ptr(block_table), block_table.stride(0), block_table.shape[1], ptr(seq_lens),
              b, hq, hkv, d, float(scaling), ptr(gate), gate.stride(0) if gate is not None else 0,
              gate.stride(1) if gate is not None else 0,

@@ -15,12 +15,15 @@ New decode tokens are appended to the last rank's range (the tail of the
 sequence).  The reference decodes on one GPU; this module has no counterpart
 there.
 
-Two exchanges give the same bits.  The NCCL path packs the partial, all-gathers
-it through torch.distributed and merges with ``oq_lse_merge``.  The NVLink path
-(``PeerExchange``) is one kernel per layer, ``oq_xrank_lse_merge``: it stores the
-partial into every rank's receive buffer with plain stores over NVLink (CUDA IPC
-mappings, no multicast), raises a per-call flag, waits (bounded) for every rank's
-flag and merges in the same order as ``oq_lse_merge``.
+Two exchanges.  The NCCL path packs the partial, all-gathers it through
+torch.distributed and merges with ``oq_lse_merge``.  The NVLink path
+(``PeerExchange``) stores each merged row into every rank's receive buffer with
+plain 8-byte stores over NVLink (CUDA IPC mappings, no multicast), each value
+tagged with its call's epoch, polls (bounded) until every rank's row has arrived
+and merges in the same order as ``oq_lse_merge``.  By default it runs inside the
+attention launch's split merge (``oq_decode_attn_int4_paged_xrank``: one launch
+pair per layer); ``oq_xrank_lse_merge`` is the same exchange as a kernel of its
+own after the partial, bit-identical to the NCCL path.
 """
 
 from __future__ import annotations
@@ -191,6 +194,10 @@ class ContextParallelDecoder:
         # inside the attention's split merge (fused_exchange) or as its own kernel after it
         self.exchange, self.site = exchange, site
         self.fused_exchange = True
+        # early: launch the attention before the kernel ahead of it finishes, loading the cached
+        # pages meanwhile -- only when that kernel writes none of this decoder's cache (e.g. the
+        # previous layer's attention and merge)
+        self.early = False
 
     def prefill(self, keys: torch.Tensor, values: torch.Tensor, *, capacity_tokens: int | None = None,
                 page_seed: int | None = None) -> None:
@@ -248,12 +255,12 @@ class ContextParallelDecoder:
         lse = torch.empty((b, hq), dtype=torch.float32, device=self.device)
         self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
                                         self.head_dim ** -0.5, out_f32=out_f32, out_lse=lse,
-                                        workspace=self._workspace(q), want_out=False)
+                                        workspace=self._workspace(q), want_out=False, early=self.early)
         return out_f32, lse
 
     def _single(self, q: torch.Tensor) -> torch.Tensor:
         return self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
-                                               self.head_dim ** -0.5, workspace=self._workspace(q))
+                                               self.head_dim ** -0.5, workspace=self._workspace(q), early=self.early)
 
     def _merge(self, part_out: torch.Tensor, part_lse: torch.Tensor) -> torch.Tensor:
         return self.cabi.lse_merge(part_out, part_lse, dtype=self.out_dtype)
@@ -266,7 +273,7 @@ class ContextParallelDecoder:
         return self.cabi.decode_attention_int4(q, self.paged.pool, self.paged.block_table, self.paged.seq_lens,
                                                self.head_dim ** -0.5, workspace=self._workspace(q),
                                                exchange=self.exchange.table(self.site),
-                                               device_status=self.exchange.status)
+                                               device_status=self.exchange.status, early=self.early)
 
     def decode(self, q: torch.Tensor) -> torch.Tensor:
         if self.exchange is not None and self.world > 1 and q.dtype == self.out_dtype and self.fused_exchange:

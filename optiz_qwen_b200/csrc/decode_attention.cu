@@ -1202,7 +1202,7 @@ extern "C" int oq_decode_attn_int4_paged_xrank(
                               &xr, &ex);
 }
 
-extern "C" int oq_decode_attn_paged_append(
+extern "C" int oq_decode_attn_paged_ex(
     int bits, const void* query, int dtype, int64_t query_stride_b, int64_t query_stride_h,
     const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
     const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
@@ -1216,10 +1216,10 @@ extern "C" int oq_decode_attn_paged_append(
     float* out_f32, float* out_lse,
     void* workspace, size_t workspace_bytes, int num_splits, int flags,
     int32_t* device_status, void* stream) {
-  if (bits != 4 && bits != 8) return oq::fail(OQ_ERR_UNSUPPORTED, "decode_attn_paged_append: bits must be 4 or 8");
-  if (!new_key || !new_value) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_append: null key / value");
+  if (bits != 4 && bits != 8) return oq::fail(OQ_ERR_UNSUPPORTED, "decode_attn_paged_ex: bits must be 4 or 8");
+  if (!new_key != !new_value) return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_ex: key without value");
   if (gate && (out_f32 || out_lse)) {
-    return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_append: a gated call writes the query-dtype output only");
+    return oq::fail(OQ_ERR_INVALID_ARGUMENT, "decode_attn_paged_ex: a gated call writes the query-dtype output only");
   }
   const oq::AttnExtras ex{new_key, new_value, key_stride_b, key_stride_h, value_stride_b, value_stride_h, flags};
   return oq::decode_attn_impl(bits, query, dtype, query_stride_b, query_stride_h, kv_codes, kv_meta, num_pages,

@@ -1,4 +1,4 @@
-"""Append + attend in one launch (``oq_decode_attn_paged_append``) against the separate launches.
+"""Append + attend in one launch (``oq_decode_attn_paged_ex``) against the separate launches.
 
 The fused launch must leave the cache bit-identical to ``oq_append_quant_int4`` / ``_int8``
 and the oracle's quantiser, and give the same output bits as the append launch followed by
@@ -146,3 +146,29 @@ def test_fused_append_rejects_bad_arguments():
         cabi.decode_attention(q, pa, table, lens, 1 / 16, new_key=k[:, :1], new_value=v[:, :1])
     with pytest.raises(ValueError):
         cabi.decode_attention(q, pa, table, lens, 1 / 16, new_key=k.half(), new_value=v.half())
+
+
+@pytest.mark.parametrize("lengths,num_splits", [([3000, 64, 1], 0), ([20000], 0)])
+def test_early_launch_without_append_matches_plain(lengths, num_splits):
+    """OQ_ATTN_EARLY alone (no appended token), in a CUDA graph behind another kernel: the same
+    bits as the plain launch, with one range per CTA and with the split merge kernel."""
+    from optiz_qwen_b200 import cabi
+
+    (pa, _), table, lens, rng = _cache(lengths, 4, seed=21)
+    q, _, _, _ = _inputs(rng, len(lengths), torch.bfloat16)
+    ws = cabi.new_decode_workspace(len(lengths), HQ, HKV, table.shape[1], "cuda")
+    ref = cabi.decode_attention(q, pa, table, lens, D ** -0.5, workspace=ws, num_splits=num_splits)
+    out = torch.empty_like(q)
+    scratch = torch.zeros(1 << 20, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        scratch.mul_(0.5)
+        cabi.decode_attention(q, pa, table, lens, D ** -0.5, out=out, workspace=ws, num_splits=num_splits,
+                              early=True)
+    for _ in range(2):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
