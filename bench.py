@@ -63,6 +63,8 @@ def parse_args(argv=None):
                     help="hybrid/serving: width of the paged KV cache codes (8: the reference's k_bits=8 preset)")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="the new token's append-quantize: inside the attention launch, or its own launch")
+    ap.add_argument("--no-early-gdn", action="store_true",
+                    help="start a GDN step right after an attention launch only once that launch has finished")
     ap.add_argument("--no-early-attn", action="store_true",
                     help="launch attention only after the GDN layer ahead of it has finished")
     ap.add_argument("--conv", choices=["separate", "fused"], default=None,
@@ -419,6 +421,7 @@ def run_b200(args):
     hbm_peak, peak_src = peaks()
 
     stack, global_batch, desc = build_stack(args, world, rank, device)
+    stack.early_gdn_after_attn = stack.early_gdn_after_attn and not args.no_early_gdn
     stack.fill_inputs()
     counts = stack.counts()
     graph = stack.capture()
