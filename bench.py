@@ -648,7 +648,9 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "fp32 (numpy)", "data": "synthetic, seeded", "config": desc,
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": sample},
-            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            # one host process on rank 0 whatever the GPU count: the same CPU figure at every N
+            "ranks": f"rank 0 alone, one process on {cores} host threads, for all {world} GPU rank(s)"}
     print(json.dumps(line), flush=True)
 
 
