@@ -116,11 +116,13 @@ def advance_seq_lens(seq_lens: torch.Tensor, delta: int = 1) -> None:
     call("oq_advance_seq_lens", ptr(seq_lens), seq_lens.shape[0], int(delta), stream_ptr(seq_lens.device))
 
 
-def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int = 148, ctas_per_sm: int = 3) -> int:
-    """Split count used when ``num_splits <= 0``: enough KV ranges per (sequence, KV head) to
-    fill one wave of resident CTAs (the C side reads SM count and occupancy from the device)."""
+def choose_splits(batch: int, num_kv_heads: int, max_pages: int, sm_count: int = 148, ctas_per_sm: int = 1) -> int:
+    """Split count used when ``num_splits <= 0`` (a mirror of the C plan, for host-side sizing):
+    enough KV ranges per (sequence, KV head) to fill ~7/8 of one wave of resident CTAs (one per
+    SM for the 4-bit kernel; the C side reads SM count and occupancy from the device), at least
+    4 pages per range, ranges of equal length."""
     units = batch * num_kv_heads
-    splits = min(max(1, (sm_count * ctas_per_sm) // units), max(1, max_pages // 8), 512)
+    splits = min(max(1, (sm_count * ctas_per_sm * 7 // 8) // units), max(1, max_pages // 4), max_pages, 512)
     pps = -(-max_pages // splits)
     return -(-max_pages // pps)
 

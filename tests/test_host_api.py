@@ -216,6 +216,7 @@ def test_conv_hook_rejects_unsupported_arguments():
 def test_workspace_split_heuristic_matches_the_c_side():
     from optiz_qwen_b200 import cabi
 
-    assert cabi.choose_splits(64, 2, 66) == 3
-    assert cabi.choose_splits(1, 2, 2048) <= 512
+    assert cabi.choose_splits(64, 2, 66) == 1          # 128 units already fill the 148 SMs
+    assert cabi.choose_splits(1, 2, 2048) == 64        # one long sequence: 64 ranges of 32 pages
+    assert cabi.choose_splits(1, 2, 256) == 64         # ... of 4 pages (the floor)
     assert cabi.choose_splits(1024, 2, 128) == 1

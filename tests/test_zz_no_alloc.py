@@ -73,7 +73,7 @@ def test_noalloc_rejects_scratch_beyond_its_fixed_size():
 def test_noalloc_runs_the_regular_partition(lengths):
     """Both entry points pick the same split count (the regular heuristic) whenever its scratch
     fits, so their fp32 outputs are bit-identical: one range per CTA at the hybrid bench shape,
-    74 ranges and the merge kernel at 131072 tokens."""
+    64 ranges and the merge kernel at 131072 tokens."""
     from optiz_qwen_b200 import _lib, cabi
 
     rng = np.random.default_rng(79)
