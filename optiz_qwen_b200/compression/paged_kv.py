@@ -109,6 +109,20 @@ class PagedKvState:
                           device_status=device_status)
         self.host_lens = [length + n for length in self.host_lens]
 
+    def append_attend(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scaling: float, *,
+                      workspace: torch.Tensor, gate: torch.Tensor | None = None,
+                      device_status: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode token per row in one launch: ``key`` / ``value`` ``[batch, Hkv, D]`` go into the
+        cache at the end of every row and ``query`` ``[batch, Hq, D]`` attends over the rows with them
+        (``oq_decode_attn_paged_ex``); returns ``[batch, Hq, D]`` in the query dtype (gated when
+        ``gate`` is given).  The row lengths then advance by one."""
+        self.reserve([length + 1 for length in self.host_lens])
+        out = cabi.decode_attention(query, self.pool, self.block_table, self.seq_lens, scaling, workspace=workspace,
+                                    gate=gate, new_key=key, new_value=value, device_status=device_status)
+        cabi.advance_seq_lens(self.seq_lens, 1)
+        self.host_lens = [length + 1 for length in self.host_lens]
+        return out
+
     def set_lengths(self, lengths) -> None:
         """Truncate rows (crop); pages past the new end go back to the free list."""
         for b, n in enumerate(lengths):

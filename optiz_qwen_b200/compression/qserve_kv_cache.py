@@ -197,7 +197,7 @@ class QServeAttentionLayer(CacheLayerMixin):
         self.is_initialized = False
 
     # ------------------------------------------------------------------ storage engine
-    def _rebuild_from_full(self, keys: torch.Tensor, values: torch.Tensor) -> None:
+    def _rebuild_from_full(self, keys: torch.Tensor, values: torch.Tensor, extra_tokens: int = 0) -> None:
         if keys.shape[-1] != self.config.group_size:
             raise ValueError(
                 f"qserve_kv paged cache keeps one group per token: group_size ({self.config.group_size}) "
@@ -209,9 +209,10 @@ class QServeAttentionLayer(CacheLayerMixin):
         if self.paged is not None:
             self.paged.release()
         if self.paged is None or self.paged.batch != batch or self.paged.pool.num_kv_heads != heads:
-            pages = max(4, 2 * batch * cabi.pages_for(seq + 1, self.config.page_size))
+            cap = seq + 1 + int(extra_tokens)
+            pages = max(4, 2 * batch * cabi.pages_for(cap, self.config.page_size))
             pool = cabi.PagedKvPool(pages, heads, dim, self.config.page_size, keys.device, bits=self.config.k_bits)
-            self.paged = PagedKvState(pool, batch, max_pages=cabi.pages_for(seq + 1, self.config.page_size),
+            self.paged = PagedKvState(pool, batch, max_pages=cabi.pages_for(cap, self.config.page_size),
                                       allocator=PageAllocator(pages, self.config.page_seed))
         self._seq_length = 0
         self._append(keys, values)
@@ -286,6 +287,36 @@ class QServeFusedAttentionLayer(QServeAttentionLayer):
         return (torch.cat([previous_keys, key_states], dim=-2), torch.cat([previous_values, value_states], dim=-2))
 
 
+    def packed_ready(self) -> bool:
+        """Whether the next decode token can go through :meth:`append_and_attend` (packed storage
+        holds the layer's history)."""
+        return self.is_initialized and self.paged is not None and self._seq_length > 0
+
+    def prepare_decode(self) -> bool:
+        """Called before a one-token decode step: :meth:`packed_ready` (the deferred layer packs
+        here the history that the coming token's ``update`` would pack)."""
+        return self.packed_ready()
+
+    def append_and_attend(self, query: torch.Tensor, key_states: torch.Tensor, value_states: torch.Tensor, *,
+                          scaling: float, gate: torch.Tensor | None = None) -> torch.Tensor:
+        """The decode step's cache update and attention in one launch: ``key_states`` /
+        ``value_states`` ``[B, Hkv, 1, D]`` are quantised into the packed pool and ``query``
+        ``[B, Hq, 1, D]`` attends over the cache with them, gated by ``gate`` ``[B, Hq, D]`` when
+        given.  Returns ``[B, 1, Hq, D]`` in the query dtype.  Equivalent to ``update`` followed by
+        the packed attention launcher (and the gate multiply), bit for bit."""
+        if not self.packed_ready():
+            raise RuntimeError("append_and_attend needs a packed qserve cache layer")
+        if query.shape[-2] != 1 or key_states.shape[-2] != 1:
+            raise RuntimeError("append_and_attend takes one decode token")
+        q = query[:, :, 0, :]
+        out = self.paged.append_attend(q, key_states[:, :, 0, :], value_states[:, :, 0, :], scaling,
+                                       workspace=self.decode_workspace(q.shape[1]), gate=gate)
+        self._seq_length += 1
+        self.keys = None
+        self.values = None
+        return out.unsqueeze(1)
+
+
 class QServeDeferredSplitFusedAttentionLayer(QServeFusedAttentionLayer):
     """Dense until ``activation_threshold`` tokens, then packed once (:473-547)."""
 
@@ -341,6 +372,20 @@ class QServeDeferredSplitFusedAttentionLayer(QServeFusedAttentionLayer):
     def reset(self) -> None:
         super().reset()
         self._deferred_prefill = False
+
+    def packed_ready(self) -> bool:
+        return not self._deferred_prefill and super().packed_ready()
+
+    def prepare_decode(self) -> bool:
+        # ``update`` packs once the dense length with the new token reaches the threshold; packing
+        # the history before that token gives the same pages (tokens are quantised one by one)
+        if (self._deferred_prefill and self.keys is not None
+                and self._seq_length + 1 >= self.config.activation_threshold):
+            keys, values = self.keys, self.values
+            self._deferred_prefill = False
+            self._seq_length = 0
+            self._rebuild_from_full(keys, values, extra_tokens=1)  # (sized as update sizes it, token included)
+        return self.packed_ready()
 
     @property
     def _key_code(self):
