@@ -793,7 +793,7 @@ def measure_prefill(args, world, rank, device, dist, hbm_peak, peak_src, steps: 
         graphs["decode"].replay()
     barrier(dist, device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    with ClockSampler(device.index if world == 1 else local) as clocks:
+    with ClockSampler(device.index) as clocks:
         ev[0].record()
         for _ in range(steps):
             graphs["prefill"].replay()
