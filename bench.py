@@ -63,6 +63,8 @@ def parse_args(argv=None):
                     help="hybrid/serving: width of the paged KV cache codes (8: the reference's k_bits=8 preset)")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="the new token's append-quantize: inside the attention launch, or its own launch")
+    ap.add_argument("--serving-order", choices=["longest-first", "index"], default="longest-first",
+                    help="order of a serving shard's sequences in the batch (the attention launch's CTA order)")
     ap.add_argument("--no-early-gdn", action="store_true",
                     help="start a GDN step right after an attention launch only once that launch has finished")
     ap.add_argument("--no-early-attn", action="store_true",
@@ -226,7 +228,10 @@ def build_stack(args, world, rank, device):
         return stack, bsz * world, desc
     lengths = serving_lengths()
     shards = shard_by_cost(lengths, world)
-    mine = [lengths[i] for i in shards[rank]]
+    from optiz_qwen_b200.serving import longest_first
+
+    order = longest_first(lengths, shards[rank]) if args.serving_order == "longest-first" else shards[rank]
+    mine = [lengths[i] for i in order]
     shape = HybridShape(batch=len(mine), context=mine)
     stack = HybridDecodeStack(shape, device=device, seed=3 + rank, page_seed=3, conv=args.conv,
                               epilogues=args.epilogues, kv_bits=args.kv_bits, gates=args.gates,
@@ -237,6 +242,7 @@ def build_stack(args, world, rank, device):
             "workload": "batched serving: B=1024 ragged sequences, context U[256,8192] (seed 3), sharded by byte "
                         f"cost across GPUs, 24-layer hybrid hot path, INT{args.kv_bits} paged KV", "global_batch": 1024,
             "batch_this_rank": len(mine), "layers": 24, "l2": "no flush: working set far above L2",
+            "batch_order": "longest context first" if args.serving_order == "longest-first" else "by index",
             "parallelism": f"sequence-sharded x{world}"}
     return stack, 1024, desc
 

@@ -53,11 +53,11 @@ struct __align__(16) SmemTail {
 // shared memory of the rings and the registers of 384 threads at up to 168 per thread).
 // For INT8, 3 groups x 2 stages beat 2 groups x 3 stages (the same 6 pages in flight per
 // SM, 12 warps instead of 8 to cover the page loop's latencies).
-template <int kBits>
+template <int kBits, int kGroups = 3>
 struct PageFormat {
   static constexpr int kCodeBytes = 2 * kPage * kHeadDim * kBits / 8;
   static constexpr int kStagesN = kBits == 8 ? 2 : kStages;
-  static constexpr int kWG = 3;
+  static constexpr int kWG = kGroups;
   // one warp group's region, 1024-aligned: stage codes | stage metas | tail
   static constexpr size_t kWgBytes =
       (size_t(kStagesN) * (kCodeBytes + kStageMetaBytes) + sizeof(SmemTail) + 1023) / 1024 * 1024;
@@ -136,12 +136,13 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
          ((uint32_t(d) & 0xFFu) << 24);
 }
 
-template <typename T, bool kDual, int kBits>
-__global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
+template <typename T, bool kDual, int kBits, int kGroups>
+__global__ void __launch_bounds__(kGroups * kThreads, kGroups == 3 ? 1 : 3)
     decode_attn_kernel(const __grid_constant__ CUtensorMap tmap, AttnParams p) {
-  constexpr int kSt = PageFormat<kBits>::kStagesN;
-  constexpr int kCB = PageFormat<kBits>::kCodeBytes;
-  constexpr int kWG = PageFormat<kBits>::kWG;
+  using PF = PageFormat<kBits, kGroups>;
+  constexpr int kSt = PF::kStagesN;
+  constexpr int kCB = PF::kCodeBytes;
+  constexpr int kWG = PF::kWG;
   constexpr int kNT = kWG * kThreads;  // threads of the CTA
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -150,11 +151,11 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
   const int ctid = threadIdx.x;
   const int wg = ctid / kThreads;
   const int bar_wg = 1 + wg;
-  uint8_t* codes = smem + wg * PageFormat<kBits>::kWgBytes;  // kSt x kCB bytes, 1024-aligned
+  uint8_t* codes = smem + wg * PF::kWgBytes;  // kSt x kCB bytes, 1024-aligned
   uint8_t* metas = codes + kSt * kCB;                           // kSt x 512 B
   SmemTail* tail = reinterpret_cast<SmemTail*>(metas + kSt * kStageMetaBytes);
   auto tail_of = [&](int g) {
-    return reinterpret_cast<SmemTail*>(smem + g * PageFormat<kBits>::kWgBytes + kSt * (kCB + kStageMetaBytes));
+    return reinterpret_cast<SmemTail*>(smem + g * PF::kWgBytes + kSt * (kCB + kStageMetaBytes));
   };
 
   const int tid = ctid - wg * kThreads;
@@ -745,7 +746,7 @@ __global__ void __launch_bounds__(PageFormat<kBits>::kWG * kThreads, 1)
       float num = 0.0f;
 #pragma unroll
       for (int g = 0; g < kWG; ++g) {
-        const float* rg = reinterpret_cast<const float*>(smem + g * PageFormat<kBits>::kWgBytes);
+        const float* rg = reinterpret_cast<const float*>(smem + g * PF::kWgBytes);
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) num += rg[red_index(w, h, d)];
       }
@@ -857,38 +858,75 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(AttnParams p
 size_t counters_bytes(int64_t units) { return size_t((units * sizeof(int) + 255) / 256 * 256); }
 
 // SMs x resident CTAs per SM of `kernel` on the current device (cached per device and kernel).
+// (Every decode_attn_kernel instance -- 2 widths x 2 query dtypes x 2 MMA layouts x 2 group counts --
+// fits the table; an unexpected kernel is computed uncached.)
 int64_t resident_slots(const void* kernel, int threads, size_t smem) {
+  constexpr int kKernels = 32;
   static std::mutex mu;
-  static int64_t cache[64][8] = {};
-  static const void* kernels[8] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 3;
-  std::lock_guard<std::mutex> lock(mu);
-  int k = 0;
-  for (; k < 8 && kernels[k] != nullptr && kernels[k] != kernel; ++k) {
-  }
-  if (k == 8) return 148 * 3;
-  kernels[k] = kernel;
-  if (cache[dev][k] == 0) {
+  static int64_t cache[64][kKernels] = {};
+  static const void* kernels[kKernels] = {};
+  auto compute = [&](int dev) {
     int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
-    cache[dev][k] = int64_t(std::max(1, sms)) * std::max(1, per_sm);
+    return int64_t(std::max(1, sms)) * std::max(1, per_sm);
+  };
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev >= 64) return compute(dev);
+  std::lock_guard<std::mutex> lock(mu);
+  int k = 0;
+  for (; k < kKernels && kernels[k] != nullptr && kernels[k] != kernel; ++k) {
   }
+  if (k == kKernels) return compute(dev);
+  kernels[k] = kernel;
+  if (cache[dev][k] == 0) cache[dev][k] = compute(dev);
   return cache[dev][k];
 }
 
 using Kernel = void (*)(const CUtensorMap, AttnParams);
 
-Kernel pick_kernel(int bits, int dtype, int64_t group) {
-  if (bits == 8) {
-    return dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 8>
-                                         : decode_attn_kernel<__nv_bfloat16, false, 8>)
-                            : (group > 4 ? decode_attn_kernel<__half, true, 8> : decode_attn_kernel<__half, false, 8>);
-  }
-  return dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, 4>
-                                       : decode_attn_kernel<__nv_bfloat16, false, 4>)
-                          : (group > 4 ? decode_attn_kernel<__half, true, 4> : decode_attn_kernel<__half, false, 4>);
+// A launchable form of the kernel: instance, dynamic shared memory and threads per CTA.
+struct KernelChoice {
+  Kernel kernel;
+  size_t smem;
+  int threads;
+};
+
+template <int kBits, int kG>
+KernelChoice kernel_choice(int dtype, int64_t group) {
+  const Kernel k = dtype == OQ_BF16 ? (group > 4 ? decode_attn_kernel<__nv_bfloat16, true, kBits, kG>
+                                                 : decode_attn_kernel<__nv_bfloat16, false, kBits, kG>)
+                                    : (group > 4 ? decode_attn_kernel<__half, true, kBits, kG>
+                                                 : decode_attn_kernel<__half, false, kBits, kG>);
+  return {k, PageFormat<kBits, kG>::kSmem, kG * kThreads};
+}
+
+// groups = 3: one CTA of three warp groups per SM (few units: long ranges, one wave);
+// groups = 1: one warp group per CTA, three CTAs per SM, so that a CTA's prologue and
+// epilogue run under its neighbours' page loops (many units in many waves, e.g. serving).
+KernelChoice pick_kernel(int bits, int dtype, int64_t group, int groups = 3) {
+  KernelChoice c = bits == 8 ? (groups == 1 ? kernel_choice<8, 1>(dtype, group) : kernel_choice<8, 3>(dtype, group))
+                             : (groups == 1 ? kernel_choice<4, 1>(dtype, group) : kernel_choice<4, 3>(dtype, group));
+  cudaFuncSetAttribute(c.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(c.smem));
+  return c;
+}
+
+// Which form a one-range-per-unit launch takes: the one with the shorter estimate of
+//   waves x (pages per warp group + fixed cost),
+// waves = ceil(units / resident CTAs), pages = the longest sequence's.  The fixed cost (prologue
+// and epilogue, in pages of loop time) is ~5 pages for the three-group CTA, alone on its SM, and
+// ~2 for the one-group CTA, whose neighbours' loops run under it.  Measured at context 4096:
+// 160, 192 and 384 sequences faster with one group (100 / 101 / 195 us against 114 / 116 / 225),
+// 256 slower (171 against 152); ragged U[256, 8192]: 1024 sequences faster (512 against 549 us),
+// 256 and 512 slower or level.
+bool prefer_one_group(int64_t units, int64_t max_pages, const KernelChoice& three, const KernelChoice& one) {
+  const int64_t s3 = resident_slots(reinterpret_cast<const void*>(three.kernel), three.threads, three.smem);
+  const int64_t s1 = resident_slots(reinterpret_cast<const void*>(one.kernel), one.threads, one.smem);
+  const double p = double(max_pages);
+  const double t3 = double((units + s3 - 1) / s3) * (p / 3.0 + 5.0);
+  const double t1 = double((units + s1 - 1) / s1) * (p + 2.0);
+  return t1 <= t3;
 }
 
 }  // namespace
@@ -902,11 +940,8 @@ int decode_attn_plan(int bits, int dtype, int64_t group, int64_t batch, int64_t 
   const int64_t units = std::max<int64_t>(1, batch * num_kv_heads);
   int splits = num_splits;
   if (splits <= 0) {
-    const Kernel kernel = pick_kernel(bits, dtype, group);
-    const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
-    const int threads = (bits == 8 ? PageFormat<8>::kWG : PageFormat<4>::kWG) * kThreads;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
-    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kernel), threads, smem_bytes);
+    const KernelChoice kc = pick_kernel(bits, dtype, group);
+    const int64_t slots = resident_slots(reinterpret_cast<const void*>(kc.kernel), kc.threads, kc.smem);
     // ... but at least kMinPagesPerSplit pages per range: merging many short ranges costs more than it saves
     splits = int(std::min<int64_t>(std::max<int64_t>(1, slots * 7 / 8 / units),
                                    std::max<int64_t>(1, max_pages_per_seq / kMinPagesPerSplit)));
@@ -1012,14 +1047,17 @@ int decode_attn_impl(
     return fail(OQ_ERR_UNSUPPORTED, "%s: page pool too large for 32-bit TMA rows", name);
   }
 
-  const Kernel kernel = pick_kernel(bits, dtype, group);
-  const size_t smem_bytes = bits == 8 ? PageFormat<8>::kSmem : PageFormat<4>::kSmem;
-  const int threads = (bits == 8 ? PageFormat<8>::kWG : PageFormat<4>::kWG) * kThreads;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes));
-
   const int64_t units = batch * num_kv_heads;
   int pps = 0;
   int splits = decode_attn_plan(bits, dtype, group, batch, num_kv_heads, max_pages_per_seq, num_splits, &pps);
+  KernelChoice kc = pick_kernel(bits, dtype, group);
+  if (splits == 1) {
+    const KernelChoice one = pick_kernel(bits, dtype, group, 1);
+    if (prefer_one_group(units, max_pages_per_seq, kc, one)) kc = one;
+  }
+  const Kernel kernel = kc.kernel;
+  const size_t smem_bytes = kc.smem;
+  const int threads = kc.threads;
   if (xr) {
     if (gate) return fail(OQ_ERR_UNSUPPORTED, "%s: no gate with the cross-GPU exchange", name);
     if (!xr->peers || xr->world <= 0 || xr->rank < 0 || xr->rank >= xr->world || xr->world > kXrankMaxWorld) {

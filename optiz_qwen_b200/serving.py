@@ -46,3 +46,14 @@ def shard_by_cost(lengths, world: int, **cost_kw) -> list[list[int]]:
 
 def shard_loads(lengths, shards, **cost_kw) -> list[int]:
     return [sum(sequence_cost(lengths[i], **cost_kw) for i in s) for s in shards]
+
+
+def longest_first(lengths, shard) -> list[int]:
+    """A shard's sequence indices ordered for decoding: longest context first, ties by index.
+
+    The attention launch runs one CTA per (sequence, KV head) in batch order, in many waves at
+    serving batch sizes; with the longest sequences first the last wave holds short ones, so
+    the launch does not wait on a long sequence that started late (longest-processing-time
+    order).  The GDN step and the output rows do not depend on the order.
+    """
+    return sorted(shard, key=lambda i: (-int(lengths[i]), i))

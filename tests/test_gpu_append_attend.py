@@ -69,6 +69,7 @@ def _separate(pool, table, lens, q, k, v, ws, num_splits, gate=None):
     ([4096, 1000], 4),                # the new page in the last split, in-launch merge
     ([4096, 1000], 64),               # many splits, merge kernel
     ([2000, 3000], 1),                # one range: the new page beyond a group's first four pages
+    ([int(x) for x in np.random.default_rng(2).integers(0, 700, 200)], 0),  # many units: one-group form
 ])
 def test_fused_append_matches_separate_launches(bits, lengths, num_splits):
     from optiz_qwen_b200 import cabi

@@ -166,6 +166,15 @@ def test_edge_lengths(length):
     np.testing.assert_allclose(lse, ref_lse, rtol=LSE_TOL, atol=LSE_TOL)
 
 
+def test_many_units_one_group_form():
+    """256 short ragged sequences: the 8-bit launch takes the one-warp-group form; every row
+    against the oracle."""
+    lengths = [int(x) for x in np.random.default_rng(6).integers(1, 600, 256)]
+    out, out32, lse, ref, ref_lse = _run(lengths, seed=6)
+    assert_attn_close(out32, ref)
+    assert_attn_close(out, ref)
+
+
 @pytest.mark.parametrize("splits", [1, 2, 3, 0])
 def test_forced_splits_ragged_batch(splits):
     out, out32, lse, ref, ref_lse = _run([700, 64, 1, 333, 129], seed=3, splits=splits)

@@ -52,18 +52,20 @@ def test_poll_limit_hook_round_trips():
     assert lib.oq_debug_set_wait_polls(-1) == default
 
 
-@pytest.mark.parametrize("num_splits", [1, 4, 64])
-def test_attention_timeout_reports_and_leaves_workspace_consistent(num_splits):
-    """1 split (single range per CTA), 4 (last-CTA merge through the counters), 64 (merge kernel)."""
+@pytest.mark.parametrize("num_splits,many", [(1, False), (4, False), (64, False), (1, True)])
+def test_attention_timeout_reports_and_leaves_workspace_consistent(num_splits, many):
+    """1 split (single range per CTA), 4 (last-CTA merge through the counters), 64 (merge kernel);
+    and 300 short sequences, whose launch takes the one-warp-group form."""
     from optiz_qwen_b200 import _lib, cabi
 
     rng = np.random.default_rng(91)
-    lengths = [4097, 300, 1, 2500]
+    lengths = [int(x) for x in rng.integers(1, 400, 300)] if many else [4097, 300, 1, 2500]
     cache = kq.fill_paged_cache(rng, lengths, 2, 256, 64, seed_pages=3)
     pool, table, lens = upload_pool(cache)
-    q = torch.from_numpy(kq.round_bf16(rng.standard_normal((4, 8, 256), dtype=np.float32))).cuda().to(torch.bfloat16)
+    b = len(lengths)
+    q = torch.from_numpy(kq.round_bf16(rng.standard_normal((b, 8, 256), dtype=np.float32))).cuda().to(torch.bfloat16)
     scaling = 256 ** -0.5
-    ws = cabi.new_decode_workspace(4, 8, 2, table.shape[1], q.device)
+    ws = cabi.new_decode_workspace(b, 8, 2, table.shape[1], q.device)
     st = _status()
     with wait_polls(0):
         out = cabi.decode_attention_int4(q, pool, table, lens, scaling, workspace=ws, num_splits=num_splits,
@@ -72,7 +74,7 @@ def test_attention_timeout_reports_and_leaves_workspace_consistent(num_splits):
     assert int(st.item()) & _lib.OQ_DEV_TIMEOUT
     assert torch.isfinite(out.float()).all()
     # every merge counter is back at zero, so the next launch on this workspace merges correctly
-    counters = ws[: 4 * 2 * 4].view(torch.int32)
+    counters = ws[: b * 2 * 4].view(torch.int32)
     assert int(counters.abs().sum().item()) == 0
     st.zero_()
     out = cabi.decode_attention_int4(q, pool, table, lens, scaling, workspace=ws, num_splits=num_splits,
