@@ -40,11 +40,15 @@ constexpr int kThreads = 256;   // two threads per TMEM lane (warps w and w + 4)
 constexpr uint32_t kTmemCols = 512;
 
 // TMEM columns (fp32 accumulators, lane = dv row unless noted)
-constexpr uint32_t kColG = 0;     // [K;Q]K^T (lane = token), then W^T (lane = dk)
-constexpr uint32_t kColU = 64;    // U^T
-constexpr uint32_t kColWS = 128;  // (W S)^T
-constexpr uint32_t kColQS = 192;  // (Q S)^T
-constexpr uint32_t kColPV = 256;  // Vn^T P^T
+// Products of a raw operand with a split (hi | lo) one are one N = 128 MMA over the two split
+// tiles, which lie next to each other as K-major tiles; the two 64-column halves of the
+// accumulator are added when read.
+constexpr uint32_t kColG = 0;     // [K;Q]K^T (lane = token)
+constexpr uint32_t kColW = 0;     // W^T (lane = dk), 128 columns: the Ar hi | Ar lo halves (after G is read)
+constexpr uint32_t kColQS = 64;   // (Q S)^T (after W is read; the next chunk's G takes columns 0-63 only)
+constexpr uint32_t kColWS = 128;  // (W S)^T, 128 columns: S_hi W_hi + S_lo W_hi | S_hi W_lo
+constexpr uint32_t kColU = 256;   // U^T, 128 columns: the Ab hi | Ab lo halves
+constexpr uint32_t kColPV = 256;  // Vn^T P^T, 128 columns: Vn_hi P_hi + Vn_lo P_hi | Vn_hi P_lo (after U is read)
 constexpr uint32_t kColS = 384;   // S^T, 128 columns: the state (dS^T accumulates onto e^{gc_last} S^T)
 
 // Shared memory (byte offsets from a 1024-aligned base).  A "tile" is 64 rows x 128 B.
@@ -71,8 +75,9 @@ constexpr uint32_t kWaitHintNs = 20000;
 
 constexpr uint32_t kIdescN64 = idesc_bf16_f32(128, 64, false, false);
 constexpr uint32_t kIdescN64BMn = idesc_bf16_f32(128, 64, false, true);
-constexpr uint32_t kIdescN64AMn = idesc_bf16_f32(128, 64, true, false);
 constexpr uint32_t kIdescN128BMn = idesc_bf16_f32(128, 128, false, true);
+constexpr uint32_t kIdescN128AMn = idesc_bf16_f32(128, 128, true, false);
+constexpr uint32_t kIdescN128 = idesc_bf16_f32(128, 128, false, false);
 
 struct ChunkParams {
   const void *g, *beta;
@@ -555,16 +560,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a_k = smem_desc_sw128(kq_a + kk * 2048, 2 * kTile, 1024);
-          const uint64_t b_r = smem_desc_sw128(sa + kOffW + part * kTile + kk * 32, 16, 1024);
-          umma_bf16(tmem + kColG, a_k, b_r, kIdescN64AMn, part | kk);
-          const uint64_t a_v = smem_desc_sw128(sa + kOffV + kk * 2048, kTile, 1024);
-          const uint64_t b_b = smem_desc_sw128(sa + kOffW + (2 + part) * kTile + kk * 32, 16, 1024);
-          umma_bf16(tmem + kColU, a_v, b_b, kIdescN64AMn, part | kk);
-        }
+      for (int kk = 0; kk < 4; ++kk) {  // B = the hi and lo tiles together (N = 128)
+        const uint64_t a_k = smem_desc_sw128(kq_a + kk * 2048, 2 * kTile, 1024);
+        const uint64_t b_r = smem_desc_sw128(sa + kOffW + kk * 32, 16, 1024);
+        umma_bf16(tmem + kColW, a_k, b_r, kIdescN128AMn, kk > 0);
+        const uint64_t a_v = smem_desc_sw128(sa + kOffV + kk * 2048, kTile, 1024);
+        const uint64_t b_b = smem_desc_sw128(sa + kOffW + 2 * kTile + kk * 32, 16, 1024);
+        umma_bf16(tmem + kColU, a_v, b_b, kIdescN128AMn, kk > 0);
       }
       umma_commit(&bars->mma);
     }
@@ -574,8 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- W tiles: MN-major [d][t] (row d = this thread's lane)
     {
-      float w[32];
-      tmem_ld32(lane_base + kColG + 32 * half, w);
+      float w[32], wl[32];
+      tmem_ld32(lane_base + kColW + 32 * half, w);
+      tmem_ld32(lane_base + kColW + 64 + 32 * half, wl);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] += wl[j];
       store_split32(sm + kOffW, sm + kOffW + 16384, lane, 4 * half, w);
     }
     fence_proxy_async_smem();
@@ -593,11 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t a_hi = smem_desc_sw128(sh + aoff, 16, 1024);
         const uint64_t a_lo = smem_desc_sw128(sl + aoff, 16, 1024);
         const uint64_t b_whi = smem_desc_sw128(sa + kOffW + kk * 2048, 16384, 1024);
-        const uint64_t b_wlo = smem_desc_sw128(sa + kOffW + 16384 + kk * 2048, 16384, 1024);
         const uint64_t b_q = smem_desc_sw128(kq_a + kTile + (kk >> 2) * 2 * kTile + (kk & 3) * 32, 16, 1024);
-        umma_bf16(tmem + kColWS, a_hi, b_whi, kIdescN64BMn, kk > 0);
-        umma_bf16(tmem + kColWS, a_lo, b_whi, kIdescN64BMn, true);
-        umma_bf16(tmem + kColWS, a_hi, b_wlo, kIdescN64BMn, true);
+        umma_bf16(tmem + kColWS, a_hi, b_whi, kIdescN128BMn, kk > 0);  // S_hi [W_hi | W_lo] (W_lo at the LBO)
+        umma_bf16(tmem + kColWS, a_lo, b_whi, kIdescN64BMn, true);      // + S_lo W_hi
         umma_bf16(tmem + kColQS, a_hi, b_q, kIdescN64, kk > 0);
         umma_bf16(tmem + kColQS, a_lo, b_q, kIdescN64, true);
       }
@@ -629,8 +632,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* vs_hi = sm + kOffS + 32768;
       uint8_t* vs_lo = sm + kOffS + 49152;
       float ws[32], u[32];
-      tmem_ld32(lane_base + kColWS + 32 * half, ws);
+      tmem_ld32(lane_base + kColU + 64 + 32 * half, ws);  // (the lo half of U first)
       tmem_ld32(lane_base + kColU + 32 * half, u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) u[j] += ws[j];
+      tmem_ld32(lane_base + kColWS + 64 + 32 * half, ws);  // (the S_hi W_lo half)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) u[j] -= ws[j];
+      tmem_ld32(lane_base + kColWS + 32 * half, ws);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         ws[j] = u[j] - ws[j];                   // v_new
@@ -652,16 +661,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
       tc_fence_after();
       const uint32_t vnh = sa + kOffS, vnl = vnh + 16384, vsh = vnh + 32768, vsl = vnh + 49152;
-      const uint32_t ph = sa + kOffP, pl = ph + kTile;
+      const uint32_t ph = sa + kOffP;  // P_hi, with P_lo the next tile
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint64_t a_nh = smem_desc_sw128(vnh + kk * 32, 16, 1024);
         const uint64_t a_nl = smem_desc_sw128(vnl + kk * 32, 16, 1024);
         const uint64_t b_ph = smem_desc_sw128(ph + kk * 32, 16, 1024);
-        const uint64_t b_pl = smem_desc_sw128(pl + kk * 32, 16, 1024);
-        umma_bf16(tmem + kColPV, a_nh, b_ph, kIdescN64, kk > 0);
-        umma_bf16(tmem + kColPV, a_nh, b_pl, kIdescN64, true);
-        umma_bf16(tmem + kColPV, a_nl, b_ph, kIdescN64, true);
+        umma_bf16(tmem + kColPV, a_nh, b_ph, kIdescN128, kk > 0);  // Vn_hi [P_hi | P_lo]
+        umma_bf16(tmem + kColPV, a_nl, b_ph, kIdescN64, true);     // + Vn_lo P_hi
         const uint64_t a_sh = smem_desc_sw128(vsh + kk * 32, 16, 1024);
         const uint64_t a_sl = smem_desc_sw128(vsl + kk * 32, 16, 1024);
         const uint64_t b_k = smem_desc_sw128(kq_a + kk * 2048, 2 * kTile, 1024);
@@ -689,8 +696,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(sm + kOffP);
       float qs[32], pv[32];
-      tmem_ld32(lane_base + kColQS + 32 * half, qs);
+      tmem_ld32(lane_base + kColPV + 64 + 32 * half, qs);  // (the Vn_hi P_lo half first)
       tmem_ld32(lane_base + kColPV + 32 * half, pv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) pv[j] += qs[j];
+      tmem_ld32(lane_base + kColQS + 32 * half, qs);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int t = 32 * half + j;
