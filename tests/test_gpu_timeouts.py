@@ -52,10 +52,11 @@ def test_poll_limit_hook_round_trips():
     assert lib.oq_debug_set_wait_polls(-1) == default
 
 
-@pytest.mark.parametrize("num_splits,many", [(1, False), (4, False), (64, False), (1, True)])
+@pytest.mark.parametrize("num_splits,many", [(1, False), (4, False), (16, False), (64, False), (1, True)])
 def test_attention_timeout_reports_and_leaves_workspace_consistent(num_splits, many):
-    """1 split (single range per CTA), 4 (last-CTA merge through the counters), 64 (merge kernel);
-    and 300 short sequences, whose launch takes the one-warp-group form."""
+    """1 split (single range per CTA), 4 (last-CTA merge through the counters), 16 (units of
+    13 and 8 ranges, merged by the merge kernel), 64 (the merge kernel); and 300 short
+    sequences, whose launch takes the one-warp-group form."""
     from optiz_qwen_b200 import _lib, cabi
 
     rng = np.random.default_rng(91)
